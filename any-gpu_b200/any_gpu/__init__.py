@@ -1,0 +1,233 @@
+"""Python host mirror of any-gpu's `GpuDevice` API over the libagpu C ABI.
+
+Method names, argument order and error behaviour follow the reference crate
+(`src/device.rs`, `src/ops/*.rs`): every op returns a new `GpuBuffer`, size
+mismatches raise `AnyGpuError` (the reference returns `Err` from `ensure!`),
+`read` blocks until the device stream has drained.
+
+    dev = GpuDevice.gpu()
+    c = dev.matmul(dev.upload(a), dev.upload(b), m, n, k)   # (m, n, k) order
+    out = dev.read(c)
+
+All compute runs in libagpu.so's sm_100a kernels; this module only marshals
+handles and host arrays.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+
+__all__ = ["GpuDevice", "GpuBuffer", "AnyGpuError", "PRECISIONS"]
+
+PRECISIONS = {"tf32": 0, "tf32x3": 1, "ffma": 2}
+_STATUS_NAMES = {0: "OK", 1: "SHAPE", 2: "INVALID", 3: "CUDA", 4: "OOM", 5: "NO_DEVICE",
+                 6: "TIMEOUT", 7: "UNSUPPORTED"}
+
+
+class AnyGpuError(RuntimeError):
+    """A failed C-ABI call; `.status` holds the agpu_status code."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[{_STATUS_NAMES.get(status, status)}] {msg}")
+        self.status = status
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        lib = _lib.load()
+        raise AnyGpuError(status, lib.agpu_last_error_message().decode(errors="replace"))
+
+
+class GpuBuffer:
+    """Owned device buffer of f32 (reference: `GpuBuffer`, src/device.rs:22-26)."""
+
+    __slots__ = ("_h", "_dev", "len")
+
+    def __init__(self, handle: int, dev: "GpuDevice"):
+        self._h = C.c_void_p(handle)
+        self._dev = dev
+        self.len = int(_lib.load().agpu_buffer_len(self._h))
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    @property
+    def device_ptr(self) -> int:
+        return int(_lib.load().agpu_buffer_device_ptr(self._h) or 0)
+
+    def free(self) -> None:
+        if self._h and self._h.value:
+            _lib.load().agpu_buffer_free(self._h)
+            self._h = C.c_void_p(None)
+
+    def __del__(self):  # Drop
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return self.len
+
+
+def _f32(data) -> np.ndarray:
+    arr = np.ascontiguousarray(np.asarray(data, dtype=np.float32).reshape(-1))
+    return arr
+
+
+class GpuDevice:
+    """One CUDA device, its stream and memory pool (reference: `GpuDevice`)."""
+
+    def __init__(self, ordinal: int = 0):
+        lib = _lib.load()
+        h = C.c_void_p()
+        _check(lib.agpu_device_create(ordinal, C.byref(h)))
+        self._h = h
+        name = C.create_string_buffer(256)
+        _check(lib.agpu_device_name(h, name, 256))
+        self.adapter_name = name.value.decode()
+        self.backend = "CUDA sm_100a"
+        self.ordinal = ordinal
+
+    @classmethod
+    def gpu(cls, ordinal: int = 0) -> "GpuDevice":
+        """Reference: `GpuDevice::gpu()` (src/device.rs:31)."""
+        return cls(ordinal)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and self._h.value:
+            _lib.load().agpu_device_destroy(self._h)
+            self._h = C.c_void_p(None)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------ plumbing --
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    @property
+    def stream(self) -> int:
+        return int(_lib.load().agpu_device_stream(self._h) or 0)
+
+    @property
+    def sm_count(self) -> int:
+        v = C.c_int()
+        _check(_lib.load().agpu_device_sm_count(self._h, C.byref(v)))
+        return v.value
+
+    @property
+    def launch_count(self) -> int:
+        return int(_lib.load().agpu_device_launch_count(self._h))
+
+    def synchronize(self) -> None:
+        _check(_lib.load().agpu_synchronize(self._h))
+
+    def set_precision(self, mode: str) -> None:
+        _check(_lib.load().agpu_set_precision(self._h, PRECISIONS[mode]))
+
+    def get_precision(self) -> str:
+        v = C.c_int()
+        _check(_lib.load().agpu_get_precision(self._h, C.byref(v)))
+        return {v_: k for k, v_ in PRECISIONS.items()}[v.value]
+
+    def _new(self, fn, *args) -> GpuBuffer:
+        out = C.c_void_p()
+        _check(fn(self._h, *args, C.byref(out)))
+        return GpuBuffer(out.value, self)
+
+    # ------------------------------------------------------------- buffers --
+    def upload(self, data) -> GpuBuffer:
+        """Reference: `upload(&[f32])` (src/device.rs:80)."""
+        arr = _f32(data)
+        out = C.c_void_p()
+        _check(_lib.load().agpu_upload(self._h, arr.ctypes.data_as(C.c_void_p), arr.size,
+                                       C.byref(out)))
+        # the H2D copy is stream-ordered from pageable memory: it has completed
+        # (or been staged) before agpu_upload returns, so `arr` may be dropped.
+        return GpuBuffer(out.value, self)
+
+    def alloc(self, n: int) -> GpuBuffer:
+        """Reference: `alloc(n)` (src/device.rs:97)."""
+        out = C.c_void_p()
+        _check(_lib.load().agpu_alloc(self._h, int(n), C.byref(out)))
+        return GpuBuffer(out.value, self)
+
+    def read(self, buf: GpuBuffer, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Reference: `read(&GpuBuffer) -> Vec<f32>` (src/device.rs:115)."""
+        if out is None:
+            out = np.empty(buf.len, dtype=np.float32)
+        _check(_lib.load().agpu_read(self._h, buf.handle, out.ctypes.data_as(C.c_void_p),
+                                     out.size))
+        return out
+
+    def write(self, buf: GpuBuffer, data: np.ndarray) -> None:
+        arr = _f32(data)
+        _check(_lib.load().agpu_write(self._h, buf.handle, arr.ctypes.data_as(C.c_void_p),
+                                      arr.size))
+
+    # -------------------------------------------------------- contractions --
+    def matmul(self, a: GpuBuffer, b: GpuBuffer, m: int, n: int, k: int) -> GpuBuffer:
+        """C[m,n] = A[m,k] B[k,n]; reference `matmul(a,b,m,n,k)` (src/ops/conv.rs:416)."""
+        return self._new(_lib.load().agpu_matmul, a.handle, b.handle, m, n, k)
+
+    def batch_matmul(self, a, b, batch: int, m: int, n: int, k: int) -> GpuBuffer:
+        """Reference: `batch_matmul(a,b,batch,m,n,k)` (src/ops/conv.rs:426)."""
+        return self._new(_lib.load().agpu_batch_matmul, a.handle, b.handle, batch, m, n, k)
+
+    def softmax(self, x: GpuBuffer, rows: int, cols: int) -> GpuBuffer:
+        """Reference: `softmax(input, rows, cols)` (src/ops/attention.rs:91)."""
+        return self._new(_lib.load().agpu_softmax, x.handle, rows, cols)
+
+    # --------------------------------------------------------- elementwise --
+    def add(self, a, b): return self._new(_lib.load().agpu_add, a.handle, b.handle)
+    def sub(self, a, b): return self._new(_lib.load().agpu_sub, a.handle, b.handle)
+    def mul(self, a, b): return self._new(_lib.load().agpu_mul, a.handle, b.handle)
+    def relu(self, a): return self._new(_lib.load().agpu_relu, a.handle)
+    def sigmoid(self, a): return self._new(_lib.load().agpu_sigmoid, a.handle)
+    def swish(self, a): return self._new(_lib.load().agpu_swish, a.handle)
+    def tanh_act(self, a): return self._new(_lib.load().agpu_tanh_act, a.handle)
+
+    def scale(self, a, s: float):
+        return self._new(_lib.load().agpu_scale, a.handle, C.c_float(s))
+
+    def relu_backward(self, grad_out, input):
+        return self._new(_lib.load().agpu_relu_backward, grad_out.handle, input.handle)
+
+    def sigmoid_backward(self, grad_out, output):
+        return self._new(_lib.load().agpu_sigmoid_backward, grad_out.handle, output.handle)
+
+    def swish_backward(self, grad_out, input):
+        return self._new(_lib.load().agpu_swish_backward, grad_out.handle, input.handle)
+
+    def tanh_backward(self, grad_out, output):
+        return self._new(_lib.load().agpu_tanh_backward, grad_out.handle, output.handle)
+
+    # ---------------------------------------------------------- tensor ops --
+    def transpose(self, a, outer_size: int, d0: int, d1: int, inner: int):
+        """Reference: `transpose(a, outer, d0, d1, inner)` (src/ops/tensor_ops.rs:251)."""
+        return self._new(_lib.load().agpu_transpose, a.handle, outer_size, d0, d1, inner)
+
+    def add_per_col(self, a, b, rows: int, cols: int):
+        """Reference: `add_per_col(a, b, rows, cols)` (src/ops/tensor_ops.rs:336)."""
+        return self._new(_lib.load().agpu_add_per_col, a.handle, b.handle, rows, cols)
+
+    # ------------------------------------------- launch layer (raw pointers) --
+    def launch_batch_matmul(self, a_ptr: int, b_ptr: int, c_ptr: int, batch: int, m: int,
+                            n: int, k: int, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_batch_matmul(self._h, a_ptr, b_ptr, c_ptr, batch, m, n,
+                                                    k, stream or None))
+
+    def launch_softmax(self, x_ptr: int, y_ptr: int, rows: int, cols: int,
+                       stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_softmax(self._h, x_ptr, y_ptr, rows, cols,
+                                               stream or None))

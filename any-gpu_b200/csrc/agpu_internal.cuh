@@ -1,0 +1,95 @@
+// Internal runtime state shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/agpu.h"
+
+struct agpu_device {
+  int ordinal = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  cudaMemPool_t pool = nullptr;
+  agpu_precision precision = AGPU_PREC_TF32;
+  char name[256] = {0};
+  // Device-side status word written by kernels whose bounded waits expire.
+  unsigned int* d_status = nullptr;
+  std::atomic<uint64_t> launches{0};
+  std::mutex mu;  // guards descriptor caches and pool growth
+};
+
+struct agpu_buffer {
+  float* dptr = nullptr;
+  uint64_t len = 0;
+  agpu_device* dev = nullptr;
+};
+
+namespace agpu {
+
+// Per-thread last error message (agpu_last_error_message).
+void set_error(const char* fmt, ...);
+agpu_status fail(agpu_status s, const char* fmt, ...);
+
+// Check a CUDA call; on failure record the message and return AGPU_ERR_CUDA
+// (or AGPU_ERR_OOM for allocation failures).
+agpu_status cuda_status(cudaError_t e, const char* what);
+
+#define AGPU_CUDA(expr)                                             \
+  do {                                                              \
+    cudaError_t e__ = (expr);                                       \
+    if (e__ != cudaSuccess) return ::agpu::cuda_status(e__, #expr); \
+  } while (0)
+
+#define AGPU_TRY(expr)                     \
+  do {                                     \
+    agpu_status s__ = (expr);              \
+    if (s__ != AGPU_OK) return s__;        \
+  } while (0)
+
+// Stream-ordered allocation from the device pool; sets OOM on failure.
+agpu_status pool_alloc(agpu_device* dev, size_t bytes, void** out, cudaStream_t s);
+void pool_free(agpu_device* dev, void* p, cudaStream_t s);
+
+// Allocate an output buffer of n floats on the device stream.
+agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out);
+
+inline cudaStream_t pick_stream(agpu_device* dev, void* s) {
+  return s ? static_cast<cudaStream_t>(s) : dev->stream;
+}
+
+// After a launch: record it and turn launch errors into a status.
+agpu_status after_launch(agpu_device* dev, const char* kernel, int n_launches = 1);
+
+// Read back and clear the device status word (non-zero = a bounded wait expired).
+agpu_status check_device_status(agpu_device* dev);
+
+inline uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+// ----------------------------------------------------------- op launchers --
+// Implemented in the kernel translation units; all validate nothing (the
+// C-ABI layer validates) and enqueue on `s`.
+agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
+                        uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                        bool a_trans, bool b_trans, cudaStream_t s);
+agpu_status launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,
+                           uint32_t cols, cudaStream_t s);
+
+enum class Unary : int { Relu = 0, Sigmoid, Swish, Tanh, Scale };
+enum class Binary : int {
+  Add = 0, Sub, Mul, ReluBwd, SigmoidBwd, SwishBwd, TanhBwd
+};
+agpu_status launch_unary(agpu_device* dev, Unary op, const float* a, float* out, uint64_t n,
+                         float s, cudaStream_t st);
+agpu_status launch_binary(agpu_device* dev, Binary op, const float* a, const float* b,
+                          float* out, uint64_t n, cudaStream_t st);
+agpu_status launch_transpose(agpu_device* dev, const float* a, float* out, uint64_t outer,
+                             uint64_t d0, uint64_t d1, uint64_t inner, cudaStream_t st);
+agpu_status launch_add_per_col(agpu_device* dev, const float* a, const float* b, float* out,
+                               uint64_t rows, uint64_t cols, cudaStream_t st);
+
+}  // namespace agpu

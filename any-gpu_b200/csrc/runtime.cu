@@ -1,0 +1,253 @@
+// Device runtime behind the C ABI: device handle, stream, stream-ordered
+// memory pool, buffers, H2D/D2H, error reporting.
+//
+// Replaces the wgpu plumbing of the reference's src/device.rs:12-190
+// (instance/adapter/queue, create_buffer_init, map_async read-back and the
+// WGSL pipeline cache).  CUDA modules are loaded once with the library, so
+// there is no per-shader compile step to cache.
+#include <cstdarg>
+#include <cstring>
+
+#include "agpu_internal.cuh"
+
+namespace agpu {
+
+static thread_local char g_err[1024] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+agpu_status fail(agpu_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+agpu_status cuda_status(cudaError_t e, const char* what) {
+  set_error("%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+  if (e == cudaErrorMemoryAllocation) return AGPU_ERR_OOM;
+  if (e == cudaErrorNoDevice || e == cudaErrorInvalidDevice) return AGPU_ERR_NO_DEVICE;
+  return AGPU_ERR_CUDA;
+}
+
+agpu_status pool_alloc(agpu_device* dev, size_t bytes, void** out, cudaStream_t s) {
+  *out = nullptr;
+  if (bytes == 0) bytes = 256;  // keep every buffer addressable
+  cudaError_t e = cudaMallocFromPoolAsync(out, bytes, dev->pool, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AGPU_ERR_OOM, "device pool: cannot allocate %zu bytes (%s)", bytes,
+                cudaGetErrorString(e));
+  }
+  return AGPU_OK;
+}
+
+void pool_free(agpu_device* dev, void* p, cudaStream_t s) {
+  (void)dev;
+  if (p) cudaFreeAsync(p, s);
+}
+
+agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out) {
+  void* p = nullptr;
+  AGPU_TRY(pool_alloc(dev, n * sizeof(float), &p, dev->stream));
+  auto* b = new agpu_buffer;
+  b->dptr = static_cast<float*>(p);
+  b->len = n;
+  b->dev = dev;
+  *out = b;
+  return AGPU_OK;
+}
+
+agpu_status after_launch(agpu_device* dev, const char* kernel, int n_launches) {
+  dev->launches.fetch_add(n_launches, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, kernel);
+  return AGPU_OK;
+}
+
+agpu_status check_device_status(agpu_device* dev) {
+  unsigned int h = 0;
+  AGPU_CUDA(cudaMemcpyAsync(&h, dev->d_status, sizeof(h), cudaMemcpyDeviceToHost, dev->stream));
+  AGPU_CUDA(cudaStreamSynchronize(dev->stream));
+  if (h != 0) {
+    AGPU_CUDA(cudaMemsetAsync(dev->d_status, 0, sizeof(unsigned int), dev->stream));
+    return fail(AGPU_ERR_TIMEOUT, "a device-side bounded wait expired (code 0x%x)", h);
+  }
+  return AGPU_OK;
+}
+
+}  // namespace agpu
+
+using namespace agpu;
+
+extern "C" {
+
+const char* agpu_last_error_message(void) { return agpu::g_err; }
+
+const char* agpu_status_string(agpu_status s) {
+  switch (s) {
+    case AGPU_OK: return "ok";
+    case AGPU_ERR_SHAPE: return "shape mismatch";
+    case AGPU_ERR_INVALID: return "invalid argument";
+    case AGPU_ERR_CUDA: return "cuda error";
+    case AGPU_ERR_OOM: return "out of device memory";
+    case AGPU_ERR_NO_DEVICE: return "no such device";
+    case AGPU_ERR_TIMEOUT: return "device wait timed out";
+    case AGPU_ERR_UNSUPPORTED: return "unsupported";
+  }
+  return "unknown status";
+}
+
+agpu_status agpu_device_create(int ordinal, agpu_device** out) {
+  if (!out) return fail(AGPU_ERR_INVALID, "agpu_device_create: out is NULL");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(AGPU_ERR_NO_DEVICE, "no CUDA device available (%s)", cudaGetErrorString(e));
+  }
+  if (ordinal < 0 || ordinal >= count)
+    return fail(AGPU_ERR_NO_DEVICE, "device ordinal %d out of range [0,%d)", ordinal, count);
+  AGPU_CUDA(cudaSetDevice(ordinal));
+  cudaDeviceProp prop;
+  AGPU_CUDA(cudaGetDeviceProperties(&prop, ordinal));
+  if (prop.major != 10)
+    return fail(AGPU_ERR_UNSUPPORTED, "device %d (%s) is sm_%d%d; this library is built for sm_100a",
+                ordinal, prop.name, prop.major, prop.minor);
+  auto* d = new agpu_device;
+  d->ordinal = ordinal;
+  d->sm_count = prop.multiProcessorCount;
+  snprintf(d->name, sizeof(d->name), "%s", prop.name);
+  e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaStreamCreate"); }
+  e = cudaDeviceGetDefaultMemPool(&d->pool, ordinal);
+  if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaDeviceGetDefaultMemPool"); }
+  // Keep freed blocks cached in the pool instead of returning them to the
+  // driver at every synchronisation: steady-state ops never hit cudaMalloc.
+  uint64_t threshold = UINT64_MAX;
+  cudaMemPoolSetAttribute(d->pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+  e = cudaMalloc(&d->d_status, sizeof(unsigned int));
+  if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaMalloc(status)"); }
+  cudaMemset(d->d_status, 0, sizeof(unsigned int));
+  *out = d;
+  return AGPU_OK;
+}
+
+agpu_status agpu_device_destroy(agpu_device* dev) {
+  if (!dev) return AGPU_OK;
+  cudaSetDevice(dev->ordinal);
+  cudaStreamSynchronize(dev->stream);
+  cudaFree(dev->d_status);
+  cudaStreamDestroy(dev->stream);
+  delete dev;
+  return AGPU_OK;
+}
+
+agpu_status agpu_device_name(const agpu_device* dev, char* buf, size_t n) {
+  if (!dev || !buf || n == 0) return fail(AGPU_ERR_INVALID, "agpu_device_name: bad argument");
+  snprintf(buf, n, "%s", dev->name);
+  return AGPU_OK;
+}
+
+agpu_status agpu_device_sm_count(const agpu_device* dev, int* out) {
+  if (!dev || !out) return fail(AGPU_ERR_INVALID, "agpu_device_sm_count: bad argument");
+  *out = dev->sm_count;
+  return AGPU_OK;
+}
+
+agpu_status agpu_device_ordinal(const agpu_device* dev, int* out) {
+  if (!dev || !out) return fail(AGPU_ERR_INVALID, "agpu_device_ordinal: bad argument");
+  *out = dev->ordinal;
+  return AGPU_OK;
+}
+
+void* agpu_device_stream(const agpu_device* dev) { return dev ? (void*)dev->stream : nullptr; }
+
+agpu_status agpu_synchronize(agpu_device* dev) {
+  if (!dev) return fail(AGPU_ERR_INVALID, "agpu_synchronize: NULL device");
+  AGPU_CUDA(cudaStreamSynchronize(dev->stream));
+  return check_device_status(dev);
+}
+
+agpu_status agpu_set_precision(agpu_device* dev, agpu_precision p) {
+  if (!dev) return fail(AGPU_ERR_INVALID, "agpu_set_precision: NULL device");
+  if (p != AGPU_PREC_TF32 && p != AGPU_PREC_TF32X3 && p != AGPU_PREC_FFMA)
+    return fail(AGPU_ERR_INVALID, "agpu_set_precision: unknown mode %d", (int)p);
+  dev->precision = p;
+  return AGPU_OK;
+}
+
+agpu_status agpu_get_precision(const agpu_device* dev, agpu_precision* p) {
+  if (!dev || !p) return fail(AGPU_ERR_INVALID, "agpu_get_precision: bad argument");
+  *p = dev->precision;
+  return AGPU_OK;
+}
+
+uint64_t agpu_device_launch_count(const agpu_device* dev) {
+  return dev ? dev->launches.load() : 0;
+}
+
+agpu_status agpu_upload(agpu_device* dev, const float* host, uint64_t n, agpu_buffer** out) {
+  if (!dev || !out || (!host && n)) return fail(AGPU_ERR_INVALID, "agpu_upload: bad argument");
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  AGPU_TRY(new_buffer(dev, n, out));
+  if (n) {
+    cudaError_t e = cudaMemcpyAsync((*out)->dptr, host, n * sizeof(float),
+                                    cudaMemcpyHostToDevice, dev->stream);
+    if (e != cudaSuccess) {
+      agpu_buffer_free(*out);
+      *out = nullptr;
+      return cuda_status(e, "agpu_upload");
+    }
+  }
+  return AGPU_OK;
+}
+
+agpu_status agpu_alloc(agpu_device* dev, uint64_t n, agpu_buffer** out) {
+  if (!dev || !out) return fail(AGPU_ERR_INVALID, "agpu_alloc: bad argument");
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  return new_buffer(dev, n, out);
+}
+
+agpu_status agpu_write(agpu_device* dev, agpu_buffer* buf, const float* host, uint64_t n) {
+  if (!dev || !buf || (!host && n)) return fail(AGPU_ERR_INVALID, "agpu_write: bad argument");
+  if (n != buf->len)
+    return fail(AGPU_ERR_SHAPE, "agpu_write: buffer has %llu elems, host has %llu",
+                (unsigned long long)buf->len, (unsigned long long)n);
+  AGPU_CUDA(cudaMemcpyAsync(buf->dptr, host, n * sizeof(float), cudaMemcpyHostToDevice,
+                            dev->stream));
+  return AGPU_OK;
+}
+
+agpu_status agpu_read(agpu_device* dev, const agpu_buffer* buf, float* host, uint64_t n) {
+  if (!dev || !buf || (!host && n)) return fail(AGPU_ERR_INVALID, "agpu_read: bad argument");
+  if (n != buf->len)
+    return fail(AGPU_ERR_SHAPE, "agpu_read: buffer has %llu elems, host has %llu",
+                (unsigned long long)buf->len, (unsigned long long)n);
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  if (n)
+    AGPU_CUDA(cudaMemcpyAsync(host, buf->dptr, n * sizeof(float), cudaMemcpyDeviceToHost,
+                              dev->stream));
+  AGPU_CUDA(cudaStreamSynchronize(dev->stream));
+  return check_device_status(dev);
+}
+
+agpu_status agpu_buffer_free(agpu_buffer* buf) {
+  if (!buf) return AGPU_OK;
+  if (buf->dev) pool_free(buf->dev, buf->dptr, buf->dev->stream);
+  delete buf;
+  return AGPU_OK;
+}
+
+uint64_t agpu_buffer_len(const agpu_buffer* buf) { return buf ? buf->len : 0; }
+
+void* agpu_buffer_device_ptr(const agpu_buffer* buf) { return buf ? (void*)buf->dptr : nullptr; }
+
+}  // extern "C"

@@ -1,0 +1,167 @@
+/*
+ * agpu.h -- C ABI of the B200-native dense-op library that replaces the
+ * hot path of any-gpu's `GpuDevice` (reference crate `any_gpu`, Rust + WGSL).
+ *
+ * Every entry point is plain C: opaque handles, raw pointers, 64-bit sizes,
+ * an `agpu_status` return code.  No CUDA, torch or C++ types cross it, so a
+ * Rust `extern "C"` block, ctypes, JNI or cgo can bind it unchanged.
+ *
+ * Two layers:
+ *   1. Buffer layer (mirrors `GpuDevice`): ops take `agpu_buffer*` inputs and
+ *      return a freshly allocated output buffer owned by the caller, exactly
+ *      like the reference's `fn op(&self, ...) -> Result<GpuBuffer>`.
+ *      Size mismatches return AGPU_ERR_SHAPE before anything is launched,
+ *      where the reference returns `Err` from `ensure!`.
+ *   2. Launch layer (`agpu_launch_*`): the same kernels on caller-owned
+ *      device memory and a caller-chosen CUDA stream (passed as `void*`),
+ *      for frameworks that manage their own memory (torch, NCCL buffers).
+ *
+ * Ordering: every op of a device is enqueued on that device's stream in call
+ * order; `agpu_read` and `agpu_synchronize` block until the stream drains.
+ * Inputs are only read; outputs never alias inputs.
+ * All element counts are 64-bit, so no `u32` wraparound at BH*S*S >= 2^32.
+ */
+#ifndef AGPU_H
+#define AGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define AGPU_API __attribute__((visibility("default")))
+#else
+#define AGPU_API
+#endif
+
+typedef enum agpu_status {
+  AGPU_OK = 0,
+  AGPU_ERR_SHAPE = 1,       /* buffer length / dimension mismatch (reference: ensure!) */
+  AGPU_ERR_INVALID = 2,     /* null handle, zero dimension, bad enum value            */
+  AGPU_ERR_CUDA = 3,        /* CUDA runtime / launch error                             */
+  AGPU_ERR_OOM = 4,         /* device memory pool exhausted                            */
+  AGPU_ERR_NO_DEVICE = 5,   /* no CUDA device with that ordinal                        */
+  AGPU_ERR_TIMEOUT = 6,     /* a bounded device-side wait expired; results invalid     */
+  AGPU_ERR_UNSUPPORTED = 7  /* shape/option combination this build does not handle     */
+} agpu_status;
+
+/* Arithmetic used by the contractions (matmul, batch_matmul, sdpa, conv2d). */
+typedef enum agpu_precision {
+  AGPU_PREC_TF32 = 0,   /* tcgen05 kind::tf32, fp32 accumulate (default)            */
+  AGPU_PREC_TF32X3 = 1, /* error-corrected 3xTF32 on tcgen05: fp32-level accuracy   */
+  AGPU_PREC_FFMA = 2    /* SIMT fp32 FFMA (exact fp32 products, slow)               */
+} agpu_precision;
+
+typedef struct agpu_device agpu_device;
+typedef struct agpu_buffer agpu_buffer;
+
+/* ---------------------------------------------------------------- errors -- */
+/* Message of the last failing call on this thread ("" if none).
+ * Replaces the anyhow::Error text of the reference. */
+AGPU_API const char* agpu_last_error_message(void);
+AGPU_API const char* agpu_status_string(agpu_status s);
+
+/* ---------------------------------------------------------------- device -- */
+/* Replaces GpuDevice::gpu() (src/device.rs:31-78): binds CUDA device
+ * `ordinal`, creates its stream and a stream-ordered memory pool. */
+AGPU_API agpu_status agpu_device_create(int ordinal, agpu_device** out);
+AGPU_API agpu_status agpu_device_destroy(agpu_device* dev);
+/* Replaces the `adapter_name` / `backend` fields (src/device.rs:15-16). */
+AGPU_API agpu_status agpu_device_name(const agpu_device* dev, char* buf, size_t buf_len);
+AGPU_API agpu_status agpu_device_sm_count(const agpu_device* dev, int* out);
+AGPU_API agpu_status agpu_device_ordinal(const agpu_device* dev, int* out);
+/* The device's CUDA stream as an opaque cudaStream_t. */
+AGPU_API void* agpu_device_stream(const agpu_device* dev);
+AGPU_API agpu_status agpu_synchronize(agpu_device* dev);
+AGPU_API agpu_status agpu_set_precision(agpu_device* dev, agpu_precision p);
+AGPU_API agpu_status agpu_get_precision(const agpu_device* dev, agpu_precision* p);
+/* Number of this library's kernels launched on `dev` since creation. */
+AGPU_API uint64_t agpu_device_launch_count(const agpu_device* dev);
+
+/* --------------------------------------------------------------- buffers -- */
+/* Replaces GpuDevice::upload (src/device.rs:80-94): H2D copy of n f32. */
+AGPU_API agpu_status agpu_upload(agpu_device* dev, const float* host, uint64_t n,
+                                 agpu_buffer** out);
+/* Replaces GpuDevice::alloc (src/device.rs:97-112). Contents undefined. */
+AGPU_API agpu_status agpu_alloc(agpu_device* dev, uint64_t n, agpu_buffer** out);
+/* Replaces GpuDevice::read (src/device.rs:115-145): blocking D2H of the
+ * whole buffer; `n` must equal the buffer length. */
+AGPU_API agpu_status agpu_read(agpu_device* dev, const agpu_buffer* buf, float* host,
+                               uint64_t n);
+/* Stream-ordered H2D into an existing buffer (no new allocation). */
+AGPU_API agpu_status agpu_write(agpu_device* dev, agpu_buffer* buf, const float* host,
+                                uint64_t n);
+/* Replaces Drop for GpuBuffer: returns memory to the device pool. */
+AGPU_API agpu_status agpu_buffer_free(agpu_buffer* buf);
+/* GpuBuffer::len (src/device.rs:25). */
+AGPU_API uint64_t agpu_buffer_len(const agpu_buffer* buf);
+/* Device address of the buffer's first element (for interop). */
+AGPU_API void* agpu_buffer_device_ptr(const agpu_buffer* buf);
+
+/* ------------------------------------------------------ contractions ------ */
+/* GpuDevice::matmul(a, b, m, n, k) (src/ops/conv.rs:416-423).
+ * C[m,n] = A[m,k] * B[k,n], row-major.  Argument order is the code's (m,n,k). */
+AGPU_API agpu_status agpu_matmul(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                                 uint32_t m, uint32_t n, uint32_t k, agpu_buffer** out);
+/* GpuDevice::batch_matmul (src/ops/conv.rs:426-433). C[b] = A[b] * B[b]. */
+AGPU_API agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a,
+                                       const agpu_buffer* b, uint32_t batch, uint32_t m,
+                                       uint32_t n, uint32_t k, agpu_buffer** out);
+
+/* ----------------------------------------------------------- attention ---- */
+/* GpuDevice::softmax (src/ops/attention.rs:91-145): row softmax of [rows, cols]. */
+AGPU_API agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows,
+                                  uint32_t cols, agpu_buffer** out);
+
+/* --------------------------------------------------------- elementwise ---- */
+/* src/ops/elementwise.rs:188-250.  Binary ops require equal lengths. */
+AGPU_API agpu_status agpu_add(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                              agpu_buffer** out);
+AGPU_API agpu_status agpu_sub(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                              agpu_buffer** out);
+AGPU_API agpu_status agpu_mul(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                              agpu_buffer** out);
+AGPU_API agpu_status agpu_relu(agpu_device* dev, const agpu_buffer* a, agpu_buffer** out);
+AGPU_API agpu_status agpu_sigmoid(agpu_device* dev, const agpu_buffer* a, agpu_buffer** out);
+AGPU_API agpu_status agpu_swish(agpu_device* dev, const agpu_buffer* a, agpu_buffer** out);
+AGPU_API agpu_status agpu_tanh_act(agpu_device* dev, const agpu_buffer* a, agpu_buffer** out);
+AGPU_API agpu_status agpu_scale(agpu_device* dev, const agpu_buffer* a, float s,
+                                agpu_buffer** out);
+/* Activation backward (src/ops/elementwise.rs:229-250). */
+AGPU_API agpu_status agpu_relu_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                        const agpu_buffer* input, agpu_buffer** out);
+AGPU_API agpu_status agpu_sigmoid_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                           const agpu_buffer* output, agpu_buffer** out);
+AGPU_API agpu_status agpu_swish_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                         const agpu_buffer* input, agpu_buffer** out);
+AGPU_API agpu_status agpu_tanh_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                        const agpu_buffer* output, agpu_buffer** out);
+
+/* ----------------------------------------------------------- tensor ops --- */
+/* GpuDevice::transpose (src/ops/tensor_ops.rs:251-269): [outer,d0,d1,inner] ->
+ * [outer,d1,d0,inner]. */
+AGPU_API agpu_status agpu_transpose(agpu_device* dev, const agpu_buffer* a, uint32_t outer,
+                                    uint32_t d0, uint32_t d1, uint32_t inner,
+                                    agpu_buffer** out);
+/* GpuDevice::add_per_col (src/ops/tensor_ops.rs:336-352): out[r,c] = a[r,c] + b[c]. */
+AGPU_API agpu_status agpu_add_per_col(agpu_device* dev, const agpu_buffer* a,
+                                      const agpu_buffer* b, uint32_t rows, uint32_t cols,
+                                      agpu_buffer** out);
+
+/* ------------------------------------------------ launch layer (raw ptrs) -- */
+/* Same kernels on caller-owned device memory; `stream` is a cudaStream_t
+ * (NULL = the device's own stream).  No allocation happens in these calls
+ * unless stated.  Shapes are validated; pointers are trusted. */
+AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, const float* b,
+                                              float* c, uint32_t batch, uint32_t m, uint32_t n,
+                                              uint32_t k, void* stream);
+AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
+                                         uint64_t rows, uint32_t cols, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AGPU_H */

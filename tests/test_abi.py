@@ -1,0 +1,79 @@
+"""CPU tests of the C-ABI boundary: the library builds/loads, exports every
+function include/agpu.h declares, the ctypes table covers the header, and the
+calls that need no GPU behave (status strings, NULL handling, no device)."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT, cuda_available
+
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions() -> list[str]:
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"AGPU_API\s+[\w\s\*]+?\b(agpu_\w+)\s*\(", text)
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert len(names) >= 30
+    assert len(set(names)) == len(names)
+
+
+def test_library_exports_every_declared_symbol():
+    from any_gpu import _lib
+    lib = _lib.load()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (agpu_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+def test_ctypes_table_matches_header():
+    from any_gpu import _lib
+    assert set(_lib.SIGNATURES) == set(declared_functions())
+
+
+def test_status_strings_and_null_handling():
+    from any_gpu import _lib
+    lib = _lib.load()
+    assert lib.agpu_status_string(0) == b"ok"
+    assert lib.agpu_status_string(1) == b"shape mismatch"
+    assert lib.agpu_status_string(6) == b"device wait timed out"
+    # NULL handles are rejected without touching a GPU
+    assert lib.agpu_buffer_len(None) == 0
+    assert lib.agpu_buffer_free(None) == 0
+    assert lib.agpu_synchronize(None) == 2
+    assert lib.agpu_set_precision(None, 0) == 2
+    out = C.c_void_p()
+    assert lib.agpu_matmul(None, None, None, 1, 1, 1, C.byref(out)) == 2
+    assert b"NULL" in lib.agpu_last_error_message()
+    assert lib.agpu_device_create(0, None) == 2
+
+
+@pytest.mark.skipif(cuda_available(), reason="checks the no-GPU path")
+def test_device_create_without_gpu_reports_no_device():
+    from any_gpu import AnyGpuError, GpuDevice
+    with pytest.raises(AnyGpuError) as e:
+        GpuDevice.gpu(0)
+    assert e.value.status == 5
+
+
+def test_product_does_not_reference_oracle():
+    # the shipped package and CUDA sources never import or link the oracle
+    for p in list((ROOT / "any-gpu_b200").rglob("*.py")) + list(
+            (ROOT / "any-gpu_b200" / "csrc").glob("*.cu*")):
+        text = p.read_text()
+        assert "oracle" not in text.lower().replace("oracle-free", ""), p

@@ -1,0 +1,144 @@
+"""CPU tests: the oracle against the reference's own known answers (pinning
+it), against float64 numpy on seeded inputs, and the reference's numeric
+gradient check for conv2d_grad_weight (src/ops/conv.rs:871-904)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import KATS
+from kat_runner import check, run_oracle
+
+LITERAL = [c for c in KATS if isinstance(c["expect"], list) or c.get("expect_slices")]
+VS_CPU = [c for c in KATS if c["expect"] == "oracle"]
+
+
+@pytest.mark.parametrize("case", LITERAL, ids=[c["name"] for c in LITERAL])
+def test_oracle_matches_reference_literal(orc, case):
+    got = run_oracle(orc, case)
+    check(case, got)
+
+
+def _f64_reference(case):
+    op, x, a = case["op"], case["inputs"], case["args"]
+    f = lambda v: np.asarray(v, np.float64)
+    if op == "matmul":
+        return (f(x["a"]).reshape(a["m"], a["k"]) @ f(x["b"]).reshape(a["k"], a["n"])).ravel()
+    if op == "batch_matmul":
+        A = f(x["a"]).reshape(a["batch"], a["m"], a["k"])
+        B = f(x["b"]).reshape(a["batch"], a["k"], a["n"])
+        return (A @ B).ravel()
+    if op == "softmax":
+        X = f(x["x"]).reshape(a["rows"], a["cols"])
+        E = np.exp(X - X.max(1, keepdims=True))
+        return (E / E.sum(1, keepdims=True)).ravel()
+    if op == "sdpa":
+        s, d = a["seq"], a["dk"]
+        Q, K, V = (f(x[n]).reshape(-1, s, d) for n in "qkv")
+        S = Q @ K.transpose(0, 2, 1) / np.sqrt(d)
+        P = np.exp(S - S.max(-1, keepdims=True))
+        P /= P.sum(-1, keepdims=True)
+        return (P @ V).ravel()
+    return None
+
+
+@pytest.mark.parametrize("case", VS_CPU, ids=[c["name"] for c in VS_CPU])
+def test_oracle_vs_float64(orc, case):
+    want = _f64_reference(case)
+    if want is None:
+        pytest.skip("no float64 restatement for this op")
+    got = run_oracle(orc, case)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+
+
+def test_oracle_conv_grad_weight_numeric(orc):
+    # src/ops/conv.rs:871-904: loss = sum(conv2d(x, w)), eps 1e-3, tol 1e-2
+    x = [v * 0.1 for v in range(1, 17)]
+    w = np.array([0.5, -0.5, 0.3, -0.3], np.float32)
+    gw = orc.conv2d_grad_weight(x, np.ones(9, np.float32), 1, 1, 4, 4, 1, 3, 3, 2, 2, 1, 1, 0, 0,
+                                1, 1, 1)
+    eps = np.float32(1e-3)
+    for i in range(4):
+        wp, wm = w.copy(), w.copy()
+        wp[i] += eps
+        wm[i] -= eps
+        sp = orc.conv2d(x, wp, None, 1, 1, 4, 4, 1, 2, 2).sum(dtype=np.float32)
+        sm = orc.conv2d(x, wm, None, 1, 1, 4, 4, 1, 2, 2).sum(dtype=np.float32)
+        assert abs(gw[i] - (sp - sm) / (2 * eps)) < 1e-2
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 48, 96), (17, 13, 11), (128, 256, 64)])
+def test_oracle_matmul_random(orc, m, n, k):
+    r = np.random.default_rng(7)
+    a = r.uniform(-1, 1, m * k).astype(np.float32)
+    b = r.uniform(-1, 1, k * n).astype(np.float32)
+    got = orc.matmul(a, b, m, n, k)
+    want = a.astype(np.float64).reshape(m, k) @ b.astype(np.float64).reshape(k, n)
+    assert orc.rel_fro(got, want) < 1e-6
+    np.testing.assert_array_equal(got, orc.matmul(a, b, m, n, k, threads=True))
+
+
+def test_oracle_conv2d_random(orc):
+    r = np.random.default_rng(3)
+    N, C, H, W, O = 2, 4, 9, 7, 6
+    x = r.standard_normal(N * C * H * W).astype(np.float32)
+    w = r.standard_normal(O * C * 9).astype(np.float32)
+    bias = r.standard_normal(O).astype(np.float32)
+    got = orc.conv2d(x, w, bias, N, C, H, W, O, 3, 3, (1, 1), (1, 1), (1, 1), 1)
+    xp = np.pad(x.reshape(N, C, H, W).astype(np.float64), ((0, 0), (0, 0), (1, 1), (1, 1)))
+    wf = w.reshape(O, C, 3, 3).astype(np.float64)
+    want = np.zeros((N, O, H, W))
+    for i in range(3):
+        for j in range(3):
+            want += np.einsum("nchw,oc->nohw", xp[:, :, i:i + H, j:j + W], wf[:, :, i, j])
+    want += bias[None, :, None, None]
+    assert orc.rel_fro(got, want) < 1e-6
+    np.testing.assert_array_equal(got, orc.conv2d(x, w, bias, N, C, H, W, O, 3, 3, (1, 1),
+                                                  (1, 1), (1, 1), 1, threads=True))
+
+
+def test_oracle_group_norm_random(orc):
+    r = np.random.default_rng(5)
+    N, C, S, G = 3, 8, 50, 4
+    x = r.standard_normal(N * C * S).astype(np.float32)
+    g = r.standard_normal(C).astype(np.float32)
+    b = r.standard_normal(C).astype(np.float32)
+    got = orc.group_norm(x, g, b, N, C, S, G, 1e-5)
+    X = x.reshape(N, G, -1).astype(np.float64)
+    Y = (X - X.mean(-1, keepdims=True)) / np.sqrt(X.var(-1, keepdims=True) + 1e-5)
+    want = Y.reshape(N, C, S) * g[None, :, None] + b[None, :, None]
+    assert orc.rel_fro(got, want) < 1e-5
+
+
+def test_oracle_attention_random(orc):
+    r = np.random.default_rng(9)
+    bh, s, d = 3, 33, 16
+    q, k, v = (r.standard_normal(bh * s * d).astype(np.float32) for _ in range(3))
+    got = orc.attention(q, k, v, bh, s, d)
+    case = {"op": "sdpa", "inputs": {"q": q, "k": k, "v": v}, "args": {"seq": s, "dk": d}}
+    assert orc.rel_fro(got, _f64_reference(case)) < 1e-5
+    np.testing.assert_array_equal(got, orc.attention(q, k, v, bh, s, d, threads=True))
+
+
+def test_oracle_causal_first_row_is_v0(orc):
+    r = np.random.default_rng(1)
+    q, k, v = (r.standard_normal(2 * 5 * 4).astype(np.float32) for _ in range(3))
+    out = orc.attention(q, k, v, 2, 5, 4, causal=True).reshape(2, 5, 4)
+    np.testing.assert_allclose(out[:, 0], v.reshape(2, 5, 4)[:, 0], rtol=1e-6)
+
+
+def test_oracle_rmsnorm_rope(orc):
+    r = np.random.default_rng(2)
+    x = r.standard_normal(4 * 64).astype(np.float32)
+    w = r.standard_normal(64).astype(np.float32)
+    got = orc.rmsnorm(x, w, 4, 64, 1e-5)
+    X = x.reshape(4, 64).astype(np.float64)
+    want = X / np.sqrt((X * X).mean(1, keepdims=True) + 1e-5) * w
+    assert orc.rel_fro(got, want) < 1e-6
+    # RoPE at position 0 is the identity; rotation preserves pair norms
+    xr = r.standard_normal(1 * 3 * 2 * 8).astype(np.float32)
+    y = orc.rope(xr, 1, 3, 2, 8).reshape(3, 2, 8)
+    np.testing.assert_allclose(y[0], xr.reshape(3, 2, 8)[0], rtol=1e-6)
+    X = xr.reshape(3, 2, 8)
+    np.testing.assert_allclose(y[..., :4] ** 2 + y[..., 4:] ** 2,
+                               X[..., :4] ** 2 + X[..., 4:] ** 2, rtol=1e-5)

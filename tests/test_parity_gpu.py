@@ -1,0 +1,161 @@
+"""GPU parity: seeded inputs through the C ABI against the oracle.
+
+Tolerances (max relative Frobenius error vs the fp32 oracle):
+  TF32 contractions          <= 1e-3
+  3xTF32 / FFMA contractions <= 1e-5
+  softmax / elementwise      <= 1e-5 (exact for add/sub/mul/relu/scale/transpose)
+At full workload sizes the checks are sampled rows against float64 plus
+size-independent properties (softmax rows sum to 1)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"tf32": 1e-3, "tf32x3": 1e-5, "ffma": 1e-5}
+
+
+def _uniform(seed, n):
+    return np.random.default_rng(seed).uniform(-1, 1, n).astype(np.float32)
+
+
+@pytest.mark.parametrize("prec", ["tf32", "tf32x3", "ffma"])
+@pytest.mark.parametrize("size", [64, 128, 256, 512, 1024])
+def test_matmul_square_sweep(dev, orc, size, prec):
+    """Config: square matmul, A,B ~ U[-1,1), the bench sweep 64..1024."""
+    m = n = k = size
+    a, b = _uniform(1234, m * k), _uniform(1235, k * n)
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.matmul(dev.upload(a), dev.upload(b), m, n, k))
+    finally:
+        dev.set_precision("tf32")
+    want = orc.matmul(a, b, m, n, k, threads=True)
+    err = orc.rel_fro(got, want)
+    assert err <= TOL[prec], f"{prec} {size}: rel_fro {err:.3e}"
+
+
+@pytest.mark.parametrize("prec", ["tf32", "tf32x3"])
+@pytest.mark.parametrize("m,n,k", [(300, 260, 100), (256, 96, 64), (128, 8, 36), (4, 512, 40),
+                                   (520, 1000, 8), (129, 132, 516)])
+def test_matmul_ragged_tensor_core(dev, orc, m, n, k, prec):
+    """Tile tails in M, N and K on the tensor-core path (pitches % 16 B == 0)."""
+    a, b = _uniform(m, m * k), _uniform(n + 7, k * n)
+    dev.set_precision(prec)
+    try:
+        before = dev.launch_count
+        got = dev.read(dev.matmul(dev.upload(a), dev.upload(b), m, n, k))
+        assert dev.launch_count == before + 1
+    finally:
+        dev.set_precision("tf32")
+    want = orc.matmul(a, b, m, n, k, threads=True)
+    assert orc.rel_fro(got, want) <= TOL[prec]
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 13, 11), (33, 65, 127), (1, 1, 1000), (200, 3, 7)])
+def test_matmul_unaligned_simt(dev, orc, m, n, k):
+    """Pitches that TMA cannot address run on the exact-fp32 SIMT kernel."""
+    a, b = _uniform(5, m * k), _uniform(6, k * n)
+    got = dev.read(dev.matmul(dev.upload(a), dev.upload(b), m, n, k))
+    assert orc.rel_fro(got, orc.matmul(a, b, m, n, k)) <= 1e-5
+
+
+@pytest.mark.parametrize("prec", ["tf32", "tf32x3"])
+def test_batch_matmul_parity(dev, orc, prec):
+    batch, m, n, k = 5, 256, 384, 512
+    r = np.random.default_rng(2)
+    a = (r.standard_normal(batch * m * k) * 0.05).astype(np.float32)
+    b = (r.standard_normal(batch * k * n) * 0.05).astype(np.float32)
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.batch_matmul(dev.upload(a), dev.upload(b), batch, m, n, k))
+    finally:
+        dev.set_precision("tf32")
+    want = orc.batch_matmul(a, b, batch, m, n, k, threads=True)
+    assert orc.rel_fro(got, want) <= TOL[prec]
+
+
+@pytest.mark.parametrize("rows,cols", [(1000, 2048), (513, 1000), (64, 4), (77, 37),
+                                       (9, 5000), (3, 1), (4096, 128), (2, 100000)])
+def test_softmax_parity(dev, orc, rows, cols):
+    x = (np.random.default_rng(rows * cols).standard_normal(rows * cols) * 3).astype(np.float32)
+    got = dev.read(dev.softmax(dev.upload(x), rows, cols))
+    want = orc.softmax(x, rows, cols, threads=True)
+    assert orc.rel_fro(got, want) <= 1e-5
+    sums = got.reshape(rows, cols).astype(np.float64).sum(1)
+    assert np.all(np.abs(sums - 1) < 1e-4)
+
+
+EXACT = ["add", "sub", "mul", "relu", "scale", "relu_backward"]
+APPROX = ["sigmoid", "swish", "tanh", "sigmoid_backward", "swish_backward", "tanh_backward"]
+
+
+@pytest.mark.parametrize("n", [1, 3, 1000003, 4 << 20])
+@pytest.mark.parametrize("op", EXACT + APPROX)
+def test_elementwise_parity(dev, orc, op, n):
+    r = np.random.default_rng(n)
+    a = (r.standard_normal(n) * 4).astype(np.float32)
+    b = (r.standard_normal(n) * 4).astype(np.float32)
+    if op in ("sigmoid_backward",):
+        b = (1 / (1 + np.exp(-b))).astype(np.float32)
+    if op in ("tanh_backward",):
+        b = np.tanh(b).astype(np.float32)
+    A, B = dev.upload(a), dev.upload(b)
+    if op == "scale":
+        got, want = dev.read(dev.scale(A, -0.37)), orc.elementwise("scale", a, None, -0.37)
+    elif op in ("relu", "sigmoid", "swish"):
+        got, want = dev.read(getattr(dev, op)(A)), orc.elementwise(op, a)
+    elif op == "tanh":
+        got, want = dev.read(dev.tanh_act(A)), orc.elementwise("tanh", a)
+    else:
+        got, want = dev.read(getattr(dev, op)(A, B)), orc.elementwise(op, a, b)
+    if op in EXACT:
+        np.testing.assert_array_equal(got, want)
+    else:
+        assert orc.rel_fro(got, want) <= 1e-5
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("outer,d0,d1,inner", [(1, 1000, 700, 1), (256, 2048, 128, 1),
+                                               (3, 5, 7, 9), (2, 64, 33, 128), (1, 1, 1, 1)])
+def test_transpose_parity(dev, orc, outer, d0, d1, inner):
+    a = np.arange(outer * d0 * d1 * inner, dtype=np.float32)
+    got = dev.read(dev.transpose(dev.upload(a), outer, d0, d1, inner))
+    np.testing.assert_array_equal(got, orc.transpose(a, outer, d0, d1, inner))
+    back = dev.read(dev.transpose(dev.upload(got), outer, d1, d0, inner))
+    np.testing.assert_array_equal(back, a)
+
+
+def test_add_per_col_parity(dev, orc):
+    r = np.random.default_rng(11)
+    for rows, cols in [(1000, 4096), (7, 13)]:
+        a = r.standard_normal(rows * cols).astype(np.float32)
+        b = r.standard_normal(cols).astype(np.float32)
+        got = dev.read(dev.add_per_col(dev.upload(a), dev.upload(b), rows, cols))
+        np.testing.assert_array_equal(got, orc.add_per_col(a, b, rows, cols))
+
+
+def test_batch_matmul_softmax_full_config(dev, orc):
+    """The headline workload at full size: batch 64, M=K=N=2048, inputs
+    N(0,1)*0.05, then row softmax.  Checked on sampled rows against float64
+    and by the row-sum property on every row."""
+    batch = m = None
+    batch, m, n, k = 64, 2048, 2048, 2048
+    r = np.random.default_rng(1235)
+    a = (r.standard_normal(batch * m * k, dtype=np.float32) * np.float32(0.05))
+    b = (r.standard_normal(batch * k * n, dtype=np.float32) * np.float32(0.05))
+    A, B = dev.upload(a), dev.upload(b)
+    C = dev.batch_matmul(A, B, batch, m, n, k)
+    S = dev.softmax(C, batch * m, n)
+    c = dev.read(C).reshape(batch, m, n)
+    s = dev.read(S).reshape(batch, m, n)
+    sums = s.astype(np.float64).sum(-1)
+    assert np.abs(sums - 1).max() < 1e-4
+    av, bv = a.reshape(batch, m, k), b.reshape(batch, k, n)
+    for bi in (0, 31, 63):
+        rows = np.array([0, 1, 777, 2047])
+        want = av[bi, rows].astype(np.float64) @ bv[bi].astype(np.float64)
+        assert orc.rel_fro(c[bi, rows], want) <= 1e-3
+        e = np.exp(want - want.max(-1, keepdims=True))
+        assert orc.rel_fro(s[bi, rows], e / e.sum(-1, keepdims=True)) <= 1e-3
