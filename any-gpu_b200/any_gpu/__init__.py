@@ -184,6 +184,12 @@ class GpuDevice:
         """Reference: `batch_matmul(a,b,batch,m,n,k)` (src/ops/conv.rs:426)."""
         return self._new(_lib.load().agpu_batch_matmul, a.handle, b.handle, batch, m, n, k)
 
+    def gemm(self, a, b, batch: int, m: int, n: int, k: int, trans_a: bool = False,
+             trans_b: bool = False) -> GpuBuffer:
+        """C[b] = op(A[b]) op(B[b]); op = transpose when trans_* (autograd backward GEMMs)."""
+        return self._new(_lib.load().agpu_gemm, a.handle, b.handle, batch, m, n, k,
+                         int(trans_a), int(trans_b))
+
     def softmax(self, x: GpuBuffer, rows: int, cols: int) -> GpuBuffer:
         """Reference: `softmax(input, rows, cols)` (src/ops/attention.rs:91)."""
         return self._new(_lib.load().agpu_softmax, x.handle, rows, cols)

@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_buffer_device_ptr": (C.c_void_p, [c_buf]),
     "agpu_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, P_buf]),
     "agpu_batch_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, P_buf]),
+    "agpu_gemm": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, i32, i32, P_buf]),
     "agpu_softmax": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
     "agpu_add": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_sub": (c_status, [c_dev, c_buf, c_buf, P_buf]),
@@ -58,6 +59,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_add_per_col": (c_status, [c_dev, c_buf, c_buf, u32, u32, P_buf]),
     "agpu_launch_batch_matmul": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
                                             u32, u32, u32, u32, C.c_void_p]),
+    "agpu_launch_gemm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p, u32, u32, u32,
+                                    u32, i32, i32, C.c_void_p]),
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
 }
 

@@ -111,6 +111,21 @@ agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a, const agpu
   });
 }
 
+agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                      uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a, int trans_b,
+                      agpu_buffer** out) {
+  CHECK_DEV(dev, "gemm");
+  CHECK_BUF(a, "gemm", "A");
+  CHECK_BUF(b, "gemm", "B");
+  CHECK_OUT(out, "gemm");
+  CHECK_LEN(a, (uint64_t)batch * m * k, "gemm", "A");
+  CHECK_LEN(b, (uint64_t)batch * k * n, "gemm", "B");
+  return with_output(dev, (uint64_t)batch * m * n, out, [&](float* c) {
+    return launch_gemm(dev, a->dptr, b->dptr, c, batch, m, n, k, trans_a != 0, trans_b != 0,
+                       dev->stream);
+  });
+}
+
 // --------------------------------------------------------------- softmax --
 agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows, uint32_t cols,
                          agpu_buffer** out) {
@@ -202,6 +217,16 @@ agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, const flo
   if ((!a || !b || !c) && (uint64_t)batch * m * n)
     return fail(AGPU_ERR_INVALID, "launch_batch_matmul: NULL pointer");
   return launch_gemm(dev, a, b, c, batch, m, n, k, false, false, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
+                             uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a,
+                             int trans_b, void* stream) {
+  CHECK_DEV(dev, "launch_gemm");
+  if ((!a || !b || !c) && (uint64_t)batch * m * n)
+    return fail(AGPU_ERR_INVALID, "launch_gemm: NULL pointer");
+  return launch_gemm(dev, a, b, c, batch, m, n, k, trans_a != 0, trans_b != 0,
+                     pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,

@@ -20,6 +20,11 @@ struct agpu_device {
   // Device-side status word written by kernels whose bounded waits expire.
   unsigned int* d_status = nullptr;
   std::atomic<uint64_t> launches{0};
+  // One reference held by the handle returned from agpu_device_create, one
+  // per live buffer: buffers may outlive agpu_device_destroy (their memory
+  // goes back to the pool when they are freed), and the stream and status
+  // word are released with the last reference.
+  std::atomic<int64_t> refs{1};
   std::mutex mu;  // guards descriptor caches and pool growth
 };
 
@@ -54,6 +59,9 @@ agpu_status cuda_status(cudaError_t e, const char* what);
 // Stream-ordered allocation from the device pool; sets OOM on failure.
 agpu_status pool_alloc(agpu_device* dev, size_t bytes, void** out, cudaStream_t s);
 void pool_free(agpu_device* dev, void* p, cudaStream_t s);
+
+// Drop one reference to `dev`; the last one releases the stream.
+void device_release(agpu_device* dev);
 
 // Allocate an output buffer of n floats on the device stream.
 agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out);

@@ -79,6 +79,19 @@ __device__ __forceinline__ void tile_coords(const GemmShape& s, long long t, int
   n0 = nb * BN_;
 }
 
+// Shared-memory descriptor of one MMA's K-slice of an operand tile.
+//  K-major  (rows of 32 fp32 = 128 B along K): 128-byte swizzle (layout 2),
+//           8-row groups 1024 B apart; the K-slice advances 32 B in the row.
+//  MN-major (32-element MN chunks of BK rows, 4 KB per chunk): 128-byte
+//           swizzle with 32-byte atoms (layout 1, the only layout the tensor
+//           core accepts for MN-major 32-bit operands); chunks 4 KB apart
+//           (leading offset), 4-row K groups 512 B apart (stride offset); the
+//           K-slice of 8 rows advances 1024 B.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t saddr) {
+  return MN ? ptx::make_sdesc(saddr, BK * 128, 512, 1) : ptx::make_sdesc(saddr, 16, 1024, 2);
+}
+
 // Split every fp32 word of a staged tile into hi (kept in place, exactly a
 // tf32 value) and lo = x - hi (written to the twin buffer).  Works on the
 // raw smem image, so it is independent of the swizzle.
@@ -228,15 +241,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, X3>::THREADS, 1)
             // MN-major: advance 8 rows of 128 B.
             const uint32_t a_off = A_MN ? kk * 1024 : kk * 32;
             const uint32_t b_off = B_MN ? kk * 1024 : kk * 32;
-            const uint32_t a_lbo = A_MN ? BK * 128 : 16;
-            const uint32_t b_lbo = B_MN ? BK * 128 : 16;
-            const uint64_t ad = ptx::make_sdesc_sw128(a_addr + a_off, a_lbo, 1024);
-            const uint64_t bd = ptx::make_sdesc_sw128(b_addr + b_off, b_lbo, 1024);
+            const uint64_t ad = operand_desc<A_MN>(a_addr + a_off);
+            const uint64_t bd = operand_desc<B_MN>(b_addr + b_off);
             const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
             ptx::mma_tf32_ss(d_tmem, ad, bd, idesc, accum);
             if (X3) {
-              const uint64_t bl = ptx::make_sdesc_sw128(lb_addr + b_off, b_lbo, 1024);
-              const uint64_t al = ptx::make_sdesc_sw128(la_addr + a_off, a_lbo, 1024);
+              const uint64_t bl = operand_desc<B_MN>(lb_addr + b_off);
+              const uint64_t al = operand_desc<A_MN>(la_addr + a_off);
               ptx::mma_tf32_ss(d_tmem, ad, bl, idesc, 1u);
               ptx::mma_tf32_ss(d_tmem, al, bd, idesc, 1u);
             }
@@ -397,10 +408,12 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
-// 3-D fp32 tensor map {inner, outer, batch} with 128-byte swizzle.
+// 3-D fp32 tensor map {inner, outer, batch}.  `mn_major` selects the
+// 128-byte swizzle with 32-byte atoms that MN-major tf32 operands need;
+// otherwise the plain 128-byte swizzle.
 agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
                              uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
-                             uint32_t box_outer) {
+                             uint32_t box_outer, bool mn_major) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {inner, outer, batch};
@@ -408,7 +421,8 @@ agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) inner=%llu outer=%llu", (int)r,
@@ -423,14 +437,14 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   CUtensorMap ta, tb;
   // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
   if (!A_MN)
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM));
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false));
   else
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK));
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true));
   // B: MN-major stored [K,N] -> dims {N, K}; K-major stored [N,K] -> dims {K, N}.
   if (B_MN)
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK));
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true));
   else
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, BN));
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, BN, false));
   GemmShape sh;
   sh.M = m; sh.N = n; sh.K = k; sh.batch = batch;
   sh.tiles_m = (int)ceil_div(m, BM);

@@ -248,6 +248,20 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lb
   return d;
 }
 
+// Same descriptor with an explicit layout type: 2 = 128-byte swizzle
+// (K-major operands), 1 = 128-byte swizzle with 32-byte atoms (the only
+// layout the tensor core accepts for MN-major 32-bit operands).
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::tf32 with fp32 accumulate:
 //   [4,6) D format (1 = f32), [7,10) A format (2 = tf32), [10,13) B format,
 //   [15] A major (1 = MN-major), [16] B major, [17,23) N>>3, [24,29) M>>4.

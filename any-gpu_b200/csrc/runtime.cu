@@ -60,8 +60,18 @@ agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out) {
   b->dptr = static_cast<float*>(p);
   b->len = n;
   b->dev = dev;
+  dev->refs.fetch_add(1, std::memory_order_relaxed);
   *out = b;
   return AGPU_OK;
+}
+
+void device_release(agpu_device* dev) {
+  if (dev->refs.fetch_sub(1, std::memory_order_acq_rel) != 1) return;
+  cudaSetDevice(dev->ordinal);
+  cudaStreamSynchronize(dev->stream);
+  cudaFree(dev->d_status);
+  cudaStreamDestroy(dev->stream);
+  delete dev;
 }
 
 agpu_status after_launch(agpu_device* dev, const char* kernel, int n_launches) {
@@ -144,9 +154,7 @@ agpu_status agpu_device_destroy(agpu_device* dev) {
   if (!dev) return AGPU_OK;
   cudaSetDevice(dev->ordinal);
   cudaStreamSynchronize(dev->stream);
-  cudaFree(dev->d_status);
-  cudaStreamDestroy(dev->stream);
-  delete dev;
+  device_release(dev);
   return AGPU_OK;
 }
 
@@ -241,8 +249,13 @@ agpu_status agpu_read(agpu_device* dev, const agpu_buffer* buf, float* host, uin
 
 agpu_status agpu_buffer_free(agpu_buffer* buf) {
   if (!buf) return AGPU_OK;
-  if (buf->dev) pool_free(buf->dev, buf->dptr, buf->dev->stream);
+  agpu_device* dev = buf->dev;
+  if (dev) {
+    cudaSetDevice(dev->ordinal);
+    pool_free(dev, buf->dptr, dev->stream);
+  }
   delete buf;
+  if (dev) device_release(dev);
   return AGPU_OK;
 }
 

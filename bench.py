@@ -68,12 +68,12 @@ REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
 
 
 class ClockSampler(threading.Thread):
-    """Samples SM clock and clock-event reasons every 200 ms via NVML."""
+    """Samples SM clock and clock-event reasons every 20 ms via NVML."""
 
     def __init__(self, cuda_index: int):
         super().__init__(daemon=True)
         self.samples, self.reasons, self.max_mhz = [], set(), None
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self._h = None
         try:
             import pynvml
@@ -98,7 +98,7 @@ class ClockSampler(threading.Thread):
         nv = self._nv
         get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
             getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-        while not self._stop.is_set():
+        while not self._halt.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
                 r = get_reasons(self._h)
@@ -107,10 +107,10 @@ class ClockSampler(threading.Thread):
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._halt.wait(0.02)
 
     def stop(self) -> dict:
-        self._stop.set()
+        self._halt.set()
         self.join(timeout=2)
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
@@ -141,18 +141,17 @@ def cpu_sample(orc, threads: bool, target_s: float):
     r = np.random.default_rng(SEED)
     a = (r.standard_normal(M * K, dtype=np.float32) * np.float32(0.05))
     b = (r.standard_normal(K * N, dtype=np.float32) * np.float32(0.05))
-    rows, spent, flops, t_total = 8, 0.0, 0.0, 0.0
-    while True:
+    chunk = max(16, 2 * orc.num_threads())
+    done, t_total, start = 0, 0.0, 0
+    while t_total < target_s:
+        rows = min(chunk, M - start)
         t0 = time.perf_counter()
-        c = orc.matmul(a[: rows * K], b, rows, N, K, threads=threads)
+        c = orc.matmul(a[start * K:(start + rows) * K], b, rows, N, K, threads=threads)
         orc.softmax(c, rows, N, threads=threads)
-        dt = time.perf_counter() - t0
-        flops += 2.0 * rows * N * K
-        t_total += dt
-        if t_total >= target_s or rows >= M:
-            break
-        rows = int(min(M, max(rows * 2, rows * (target_s - t_total) / max(dt, 1e-3))))
-    return flops / t_total / 1e12, int(flops / (2.0 * N * K)), t_total
+        t_total += time.perf_counter() - t0
+        done += rows
+        start = (start + rows) % M
+    return 2.0 * done * N * K / t_total / 1e12, done, t_total
 
 
 # -------------------------------------------------------------- arms -----
@@ -179,8 +178,9 @@ def run_reference(args, world, rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args, world),
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": "port",
-                         "sample": f"batch item 0, first {rows_done} of {M} rows per step "
-                                   "(batch_matmul rows + their softmax), extrapolated by FLOPs"},
+                         "sample": f"{rows_done} rows of batch item 0 per step (each: a "
+                                   f"1x{K} by {K}x{N} matmul row + its softmax), "
+                                   "extrapolated by FLOPs"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -220,8 +220,13 @@ def run_agpu(args, world, rank, local):
     S = torch.empty_like(C)
     gathered = (torch.empty(world * BATCH * M * N, dtype=torch.float32,
                             device=f"cuda:{local}") if (args.gather and world > 1) else None)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the library launches on it and the CUDA events are
+    # recorded on it (handle 0, torch's legacy default stream, would mean
+    # "the library's own stream" at the C ABI).
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
+    assert sptr != 0
 
     def step(ev=None):
         if ev is not None:
@@ -323,8 +328,8 @@ def run_agpu(args, world, rank, local):
             v, rows, secs = cpu_sample(orc, threads=True, target_s=args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": v, "unit": "TFLOPS", "cores": orc.num_threads(), "kind": "port",
-                "sample": f"batch item 0, first {rows} of {M} rows (batch_matmul rows + their "
-                          f"softmax), {secs:.1f} s, extrapolated by FLOPs"}
+                "sample": f"{rows} rows of batch item 0 (each: a 1x{K} by {K}x{N} matmul row + "
+                          f"its softmax), {secs:.1f} s, extrapolated by FLOPs"}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -335,7 +340,7 @@ def run_agpu(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["agpu", "reference"], default="agpu")
     ap.add_argument("--gather", action="store_true",

@@ -68,6 +68,8 @@ AGPU_API const char* agpu_status_string(agpu_status s);
 /* Replaces GpuDevice::gpu() (src/device.rs:31-78): binds CUDA device
  * `ordinal`, creates its stream and a stream-ordered memory pool. */
 AGPU_API agpu_status agpu_device_create(int ordinal, agpu_device** out);
+/* Releases the handle.  Buffers still alive keep the device's stream and
+ * memory valid until they are freed (like GpuBuffer holding its device). */
 AGPU_API agpu_status agpu_device_destroy(agpu_device* dev);
 /* Replaces the `adapter_name` / `backend` fields (src/device.rs:15-16). */
 AGPU_API agpu_status agpu_device_name(const agpu_device* dev, char* buf, size_t buf_len);
@@ -110,6 +112,16 @@ AGPU_API agpu_status agpu_matmul(agpu_device* dev, const agpu_buffer* a, const a
 AGPU_API agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a,
                                        const agpu_buffer* b, uint32_t batch, uint32_t m,
                                        uint32_t n, uint32_t k, agpu_buffer** out);
+
+/* General (batched) GEMM with optional transposed operands, the kernels the
+ * reference's autograd backward reaches through transpose + matmul
+ * (src/autograd.rs:357-366): dA = dC * B^T (trans_b), dB = A^T * dC (trans_a).
+ * trans_a = 0: A stored [batch, m, k]; 1: A stored [batch, k, m].
+ * trans_b = 0: B stored [batch, k, n]; 1: B stored [batch, n, k].
+ * C is always [batch, m, n] row-major. */
+AGPU_API agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                               uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a,
+                               int trans_b, agpu_buffer** out);
 
 /* ----------------------------------------------------------- attention ---- */
 /* GpuDevice::softmax (src/ops/attention.rs:91-145): row softmax of [rows, cols]. */
@@ -158,6 +170,9 @@ AGPU_API agpu_status agpu_add_per_col(agpu_device* dev, const agpu_buffer* a,
 AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, const float* b,
                                               float* c, uint32_t batch, uint32_t m, uint32_t n,
                                               uint32_t k, void* stream);
+AGPU_API agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
+                                      uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                      int trans_a, int trans_b, void* stream);
 AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
                                          uint64_t rows, uint32_t cols, void* stream);
 
