@@ -194,6 +194,20 @@ class GpuDevice:
         """Reference: `softmax(input, rows, cols)` (src/ops/attention.rs:91)."""
         return self._new(_lib.load().agpu_softmax, x.handle, rows, cols)
 
+    # ---------------------------------------------------------- group norm --
+    def group_norm(self, x, gamma, beta, batch: int, channels: int, spatial: int, groups: int,
+                   eps: float) -> GpuBuffer:
+        """Reference: `group_norm(input, gamma, beta, batch, channels, spatial, groups, eps)`
+        (src/ops/norm.rs:210)."""
+        return self._new(_lib.load().agpu_group_norm, x.handle, gamma.handle, beta.handle, batch,
+                         channels, spatial, groups, C.c_float(eps))
+
+    def group_norm_swish(self, x, gamma, beta, batch: int, channels: int, spatial: int,
+                         groups: int, eps: float) -> GpuBuffer:
+        """group_norm then swish in one pass."""
+        return self._new(_lib.load().agpu_group_norm_swish, x.handle, gamma.handle, beta.handle,
+                         batch, channels, spatial, groups, C.c_float(eps))
+
     # --------------------------------------------------------- elementwise --
     def add(self, a, b): return self._new(_lib.load().agpu_add, a.handle, b.handle)
     def sub(self, a, b): return self._new(_lib.load().agpu_sub, a.handle, b.handle)
@@ -232,6 +246,12 @@ class GpuDevice:
                             n: int, k: int, stream: int = 0) -> None:
         _check(_lib.load().agpu_launch_batch_matmul(self._h, a_ptr, b_ptr, c_ptr, batch, m, n,
                                                     k, stream or None))
+
+    def launch_group_norm(self, x_ptr, g_ptr, b_ptr, y_ptr, batch, channels, spatial, groups,
+                          eps, swish=False, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_group_norm(self._h, x_ptr, g_ptr, b_ptr, y_ptr, batch,
+                                                  channels, spatial, groups, C.c_float(eps),
+                                                  int(swish), stream or None))
 
     def launch_softmax(self, x_ptr: int, y_ptr: int, rows: int, cols: int,
                        stream: int = 0) -> None:

@@ -43,6 +43,10 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_batch_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, P_buf]),
     "agpu_gemm": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, i32, i32, P_buf]),
     "agpu_softmax": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
+    "agpu_group_norm": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, u32, f32,
+                                   P_buf]),
+    "agpu_group_norm_swish": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, u32, f32,
+                                         P_buf]),
     "agpu_add": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_sub": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_mul": (c_status, [c_dev, c_buf, c_buf, P_buf]),
@@ -61,6 +65,9 @@ SIGNATURES: dict[str, tuple] = {
                                             u32, u32, u32, u32, C.c_void_p]),
     "agpu_launch_gemm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p, u32, u32, u32,
                                     u32, i32, i32, C.c_void_p]),
+    "agpu_launch_group_norm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, u32, u32, u32, u32, f32, i32,
+                                          C.c_void_p]),
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
 }
 

@@ -139,6 +139,48 @@ agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows, 
   });
 }
 
+// ------------------------------------------------------------ group norm --
+static agpu_status group_norm_impl(agpu_device* dev, const agpu_buffer* x,
+                                   const agpu_buffer* gamma, const agpu_buffer* beta,
+                                   uint32_t batch, uint32_t channels, uint32_t spatial,
+                                   uint32_t groups, float eps, bool swish, agpu_buffer** out,
+                                   const char* fn) {
+  if (!dev) return fail(AGPU_ERR_INVALID, "%s: NULL device", fn);
+  if (!x || !gamma || !beta) return fail(AGPU_ERR_INVALID, "%s: input is NULL", fn);
+  if (!out) return fail(AGPU_ERR_INVALID, "%s: out is NULL", fn);
+  *out = nullptr;
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  // src/ops/norm.rs:218-221
+  const uint64_t total = (uint64_t)batch * channels * spatial;
+  if (x->len != total)
+    return fail(AGPU_ERR_SHAPE, "%s: input has %llu elems, expected %llu", fn,
+                (unsigned long long)x->len, (unsigned long long)total);
+  if (gamma->len != channels || beta->len != channels)
+    return fail(AGPU_ERR_SHAPE, "%s: gamma/beta must have %u elems", fn, channels);
+  if (groups == 0 || channels % groups != 0)
+    return fail(AGPU_ERR_SHAPE, "%s: channels must be divisible by groups", fn);
+  return with_output(dev, total, out, [&](float* y) {
+    return launch_group_norm(dev, x->dptr, gamma->dptr, beta->dptr, y, batch, channels, spatial,
+                             groups, eps, swish, dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_group_norm(agpu_device* dev, const agpu_buffer* x,
+                                       const agpu_buffer* gamma, const agpu_buffer* beta,
+                                       uint32_t batch, uint32_t channels, uint32_t spatial,
+                                       uint32_t groups, float eps, agpu_buffer** out) {
+  return group_norm_impl(dev, x, gamma, beta, batch, channels, spatial, groups, eps, false, out,
+                         "group_norm");
+}
+
+extern "C" agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer* x,
+                                             const agpu_buffer* gamma, const agpu_buffer* beta,
+                                             uint32_t batch, uint32_t channels, uint32_t spatial,
+                                             uint32_t groups, float eps, agpu_buffer** out) {
+  return group_norm_impl(dev, x, gamma, beta, batch, channels, spatial, groups, eps, true, out,
+                         "group_norm_swish");
+}
+
 // ----------------------------------------------------------- elementwise --
 agpu_status agpu_add(agpu_device* d, const agpu_buffer* a, const agpu_buffer* b, agpu_buffer** o) {
   return binary(d, a, b, o, Binary::Add, "add");
@@ -227,6 +269,17 @@ agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, f
     return fail(AGPU_ERR_INVALID, "launch_gemm: NULL pointer");
   return launch_gemm(dev, a, b, c, batch, m, n, k, trans_a != 0, trans_b != 0,
                      pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,
+                                   const float* beta, float* y, uint32_t batch, uint32_t channels,
+                                   uint32_t spatial, uint32_t groups, float eps, int apply_swish,
+                                   void* stream) {
+  CHECK_DEV(dev, "launch_group_norm");
+  if (groups == 0 || channels % groups != 0)
+    return fail(AGPU_ERR_SHAPE, "launch_group_norm: channels must be divisible by groups");
+  return launch_group_norm(dev, x, gamma, beta, y, batch, channels, spatial, groups, eps,
+                           apply_swish != 0, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,

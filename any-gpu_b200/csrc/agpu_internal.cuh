@@ -87,6 +87,11 @@ agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float*
 agpu_status launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,
                            uint32_t cols, cudaStream_t s);
 
+agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gamma,
+                              const float* beta, float* y, uint32_t batch, uint32_t channels,
+                              uint32_t spatial, uint32_t groups, float eps, bool swish,
+                              cudaStream_t s);
+
 enum class Unary : int { Relu = 0, Sigmoid, Swish, Tanh, Scale };
 enum class Binary : int {
   Add = 0, Sub, Mul, ReluBwd, SigmoidBwd, SwishBwd, TanhBwd

@@ -128,6 +128,21 @@ AGPU_API agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agp
 AGPU_API agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows,
                                   uint32_t cols, agpu_buffer** out);
 
+/* ------------------------------------------------------------ group norm -- */
+/* GpuDevice::group_norm (src/ops/norm.rs:210-278): x [batch, channels, spatial]
+ * in `groups` groups of channels/groups channels; y = (x-mean)/sqrt(var+eps) *
+ * gamma[c] + beta[c].  channels % groups != 0 -> AGPU_ERR_SHAPE. */
+AGPU_API agpu_status agpu_group_norm(agpu_device* dev, const agpu_buffer* x,
+                                     const agpu_buffer* gamma, const agpu_buffer* beta,
+                                     uint32_t batch, uint32_t channels, uint32_t spatial,
+                                     uint32_t groups, float eps, agpu_buffer** out);
+/* group_norm followed by swish in one pass (the UNet block's GN -> swish,
+ * src/ops/norm.rs:210 then src/ops/elementwise.rs:211). */
+AGPU_API agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer* x,
+                                           const agpu_buffer* gamma, const agpu_buffer* beta,
+                                           uint32_t batch, uint32_t channels, uint32_t spatial,
+                                           uint32_t groups, float eps, agpu_buffer** out);
+
 /* --------------------------------------------------------- elementwise ---- */
 /* src/ops/elementwise.rs:188-250.  Binary ops require equal lengths. */
 AGPU_API agpu_status agpu_add(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
@@ -173,6 +188,10 @@ AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, 
 AGPU_API agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
                                       uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                       int trans_a, int trans_b, void* stream);
+AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,
+                                            const float* beta, float* y, uint32_t batch,
+                                            uint32_t channels, uint32_t spatial, uint32_t groups,
+                                            float eps, int apply_swish, void* stream);
 AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
                                          uint64_t rows, uint32_t cols, void* stream);
 

@@ -6,7 +6,7 @@ import numpy as np
 # ops of the reference whose C-ABI entry points exist in this build
 GPU_OPS = {"matmul", "batch_matmul", "softmax", "add", "sub", "mul", "relu", "sigmoid", "swish",
            "tanh", "scale", "relu_backward", "sigmoid_backward", "swish_backward",
-           "tanh_backward", "transpose"}
+           "tanh_backward", "transpose", "group_norm"}
 
 
 def run_oracle(orc, case) -> np.ndarray:
@@ -55,6 +55,9 @@ def run_gpu(dev, case) -> np.ndarray:
                                          a["k"]))
     if op == "softmax":
         return dev.read(dev.softmax(up(x["x"]), a["rows"], a["cols"]))
+    if op == "group_norm":
+        return dev.read(dev.group_norm(up(x["x"]), up(x["gamma"]), up(x["beta"]), a["batch"],
+                                       a["channels"], a["spatial"], a["groups"], a["eps"]))
     if op == "transpose":
         return dev.read(dev.transpose(up(x["a"]), a["outer"], a["d0"], a["d1"], a["inner"]))
     if op == "scale":

@@ -186,3 +186,47 @@ def test_batch_matmul_softmax_full_config(dev, orc):
         assert orc.rel_fro(c[bi, rows], want) <= 1e-3
         e = np.exp(want - want.max(-1, keepdims=True))
         assert orc.rel_fro(s[bi, rows], e / e.sum(-1, keepdims=True)) <= 1e-3
+
+
+def _gn64(x, gamma, beta, n, c, s, g, eps):
+    X = np.asarray(x, np.float64).reshape(n, g, -1)
+    Y = (X - X.mean(-1, keepdims=True)) / np.sqrt(X.var(-1, keepdims=True) + eps)
+    return (Y.reshape(n, c, s) * np.asarray(gamma, np.float64)[None, :, None]
+            + np.asarray(beta, np.float64)[None, :, None]).ravel()
+
+
+@pytest.mark.parametrize("swish", [False, True])
+@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block (cluster of 4 CTAs)
+                                     (2, 64, 1024, 32),      # 2 channels x 1024 per group
+                                     (3, 12, 37, 4),         # spatial % 4 != 0: chunked path
+                                     (1, 4, 300000, 2),      # 600k-element groups: chunked
+                                     (2, 6, 8, 6)])          # per-channel groups
+def test_group_norm_parity(dev, orc, n, c, s, g, swish):
+    """Config 4's group_norm (eps 1e-5, gamma 1, beta 0 there) and ragged shapes
+    against the oracle; tolerance as for softmax (the reference's E[x^2]-mean^2
+    in sequential fp32 drifts on large groups)."""
+    r = np.random.default_rng(n * c + s)
+    x = r.standard_normal(n * c * s).astype(np.float32)
+    gamma = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(c)).astype(np.float32)
+    X, G, B = dev.upload(x), dev.upload(gamma), dev.upload(beta)
+    fn = dev.group_norm_swish if swish else dev.group_norm
+    got = dev.read(fn(X, G, B, n, c, s, g, 1e-5))
+    want = orc.group_norm(x, gamma, beta, n, c, s, g, 1e-5, threads=True)
+    ref64 = _gn64(x, gamma, beta, n, c, s, g, 1e-5)
+    if swish:
+        want = orc.elementwise("swish", want)
+        ref64 = ref64 / (1 + np.exp(-ref64))
+    err_orc = orc.rel_fro(want, ref64)
+    assert orc.rel_fro(got, ref64) <= max(1e-5, err_orc)
+    assert orc.rel_fro(got, want) <= 1e-5 + err_orc
+
+
+def test_group_norm_errors(dev):
+    from any_gpu import AnyGpuError
+    x = dev.upload(np.ones(10, np.float32))
+    g = dev.upload(np.ones(5, np.float32))
+    for args in [(1, 5, 2, 2), (1, 5, 2, 3), (2, 5, 1, 5)]:
+        with pytest.raises(AnyGpuError) as e:
+            dev.group_norm(x, g, g, *args, 1e-5)
+        assert e.value.status == 1
