@@ -194,6 +194,38 @@ class GpuDevice:
         """Reference: `softmax(input, rows, cols)` (src/ops/attention.rs:91)."""
         return self._new(_lib.load().agpu_softmax, x.handle, rows, cols)
 
+    # -------------------------------------------------------------- conv2d --
+    def conv2d(self, input, weight, bias, batch, in_c, in_h, in_w, out_c, kh, kw,
+               stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1) -> GpuBuffer:
+        """Reference: `conv2d(input, weight, bias, batch, in_c, in_h, in_w, out_c, kh, kw,
+        stride, padding, dilation, groups)` (src/ops/conv.rs:437)."""
+        return self._new(_lib.load().agpu_conv2d, input.handle, weight.handle,
+                         bias.handle if bias is not None else None, batch, in_c, in_h, in_w,
+                         out_c, kh, kw, stride[0], stride[1], padding[0], padding[1],
+                         dilation[0], dilation[1], groups)
+
+    def conv_transpose2d(self, input, weight, bias, batch, in_c, in_h, in_w, out_c, kh, kw,
+                         stride=(1, 1), padding=(0, 0), output_padding=(0, 0),
+                         dilation=(1, 1), groups=1) -> GpuBuffer:
+        """Reference: `conv_transpose2d(...)` (src/ops/conv.rs:484)."""
+        return self._new(_lib.load().agpu_conv_transpose2d, input.handle, weight.handle,
+                         bias.handle if bias is not None else None, batch, in_c, in_h, in_w,
+                         out_c, kh, kw, stride[0], stride[1], padding[0], padding[1],
+                         output_padding[0], output_padding[1], dilation[0], dilation[1], groups)
+
+    def conv2d_grad_weight(self, input, grad_out, batch, in_c, in_h, in_w, out_c, out_h, out_w,
+                           kh, kw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w,
+                           groups) -> GpuBuffer:
+        """Reference: `conv2d_grad_weight(...)` (src/ops/conv.rs:531)."""
+        return self._new(_lib.load().agpu_conv2d_grad_weight, input.handle, grad_out.handle,
+                         batch, in_c, in_h, in_w, out_c, out_h, out_w, kh, kw, stride_h,
+                         stride_w, pad_h, pad_w, dil_h, dil_w, groups)
+
+    def conv2d_grad_bias(self, grad_out, batch, out_c, out_h, out_w) -> GpuBuffer:
+        """Reference: `conv2d_grad_bias(...)` (src/ops/conv.rs:551)."""
+        return self._new(_lib.load().agpu_conv2d_grad_bias, grad_out.handle, batch, out_c,
+                         out_h, out_w)
+
     # ---------------------------------------------------------- group norm --
     def group_norm(self, x, gamma, beta, batch: int, channels: int, spatial: int, groups: int,
                    eps: float) -> GpuBuffer:

@@ -139,6 +139,111 @@ agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows, 
   });
 }
 
+// --------------------------------------------------------------- conv2d --
+static agpu_status conv_geometry(uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+                                 uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t sh,
+                                 uint32_t sw, uint32_t ph, uint32_t pw, uint32_t dh, uint32_t dw,
+                                 uint32_t groups, ConvParams* p, const char* fn) {
+  if (groups == 0 || in_c % groups || out_c % groups)
+    return fail(AGPU_ERR_SHAPE, "%s: channels (%u in, %u out) not divisible by groups %u", fn,
+                in_c, out_c, groups);
+  if (sh == 0 || sw == 0 || dh == 0 || dw == 0 || kh == 0 || kw == 0)
+    return fail(AGPU_ERR_INVALID, "%s: zero stride, dilation or kernel size", fn);
+  const long long eh = (long long)in_h + 2LL * ph - (long long)dh * (kh - 1) - 1;
+  const long long ew = (long long)in_w + 2LL * pw - (long long)dw * (kw - 1) - 1;
+  if (eh < 0 || ew < 0)
+    return fail(AGPU_ERR_SHAPE, "%s: kernel larger than the padded input", fn);
+  *p = ConvParams{(int)batch, (int)in_c, (int)in_h, (int)in_w, (int)out_c, (int)kh, (int)kw,
+                  (int)sh, (int)sw, (int)ph, (int)pw, (int)dh, (int)dw, (int)groups,
+                  (int)(eh / sh + 1), (int)(ew / sw + 1)};
+  return AGPU_OK;
+}
+
+extern "C" agpu_status agpu_conv2d(agpu_device* dev, const agpu_buffer* input,
+                                   const agpu_buffer* weight, const agpu_buffer* bias,
+                                   uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+                                   uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t sh,
+                                   uint32_t sw, uint32_t ph, uint32_t pw, uint32_t dh, uint32_t dw,
+                                   uint32_t groups, agpu_buffer** out) {
+  CHECK_DEV(dev, "conv2d");
+  CHECK_BUF(input, "conv2d", "input");
+  CHECK_BUF(weight, "conv2d", "weight");
+  CHECK_OUT(out, "conv2d");
+  ConvParams p;
+  AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
+                         &p, "conv2d"));
+  // src/ops/conv.rs:450-458
+  CHECK_LEN(input, (uint64_t)batch * in_c * in_h * in_w, "conv2d", "input");
+  CHECK_LEN(weight, (uint64_t)out_c * (in_c / groups) * kh * kw, "conv2d", "weight");
+  if (bias) CHECK_LEN(bias, out_c, "conv2d", "bias");
+  return with_output(dev, (uint64_t)batch * out_c * p.ho * p.wo, out, [&](float* y) {
+    return launch_conv2d(dev, p, input->dptr, weight->dptr, bias ? bias->dptr : nullptr, y,
+                         dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_conv_transpose2d(
+    agpu_device* dev, const agpu_buffer* input, const agpu_buffer* weight,
+    const agpu_buffer* bias, uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+    uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw,
+    uint32_t oph, uint32_t opw, uint32_t dh, uint32_t dw, uint32_t groups, agpu_buffer** out) {
+  CHECK_DEV(dev, "conv_transpose2d");
+  CHECK_BUF(input, "conv_transpose2d", "input");
+  CHECK_BUF(weight, "conv_transpose2d", "weight");
+  CHECK_OUT(out, "conv_transpose2d");
+  if (groups == 0 || in_c % groups || out_c % groups || sh == 0 || sw == 0)
+    return fail(AGPU_ERR_SHAPE, "conv_transpose2d: bad groups or stride");
+  // output size: src/ops/conv.rs:498-499
+  const long long oh = ((long long)in_h - 1) * sh - 2LL * ph + (long long)dh * (kh - 1) + oph + 1;
+  const long long ow = ((long long)in_w - 1) * sw - 2LL * pw + (long long)dw * (kw - 1) + opw + 1;
+  if (oh <= 0 || ow <= 0) return fail(AGPU_ERR_SHAPE, "conv_transpose2d: empty output");
+  // src/ops/conv.rs:502-510
+  CHECK_LEN(input, (uint64_t)batch * in_c * in_h * in_w, "conv_transpose2d", "input");
+  CHECK_LEN(weight, (uint64_t)in_c * (out_c / groups) * kh * kw, "conv_transpose2d", "weight");
+  if (bias) CHECK_LEN(bias, out_c, "conv_transpose2d", "bias");
+  ConvParams p{(int)batch, (int)in_c, (int)in_h, (int)in_w, (int)out_c, (int)kh, (int)kw,
+               (int)sh, (int)sw, (int)ph, (int)pw, (int)dh, (int)dw, (int)groups, (int)oh,
+               (int)ow};
+  return with_output(dev, (uint64_t)batch * out_c * oh * ow, out, [&](float* y) {
+    return launch_conv_transpose2d(dev, p, input->dptr, weight->dptr, bias ? bias->dptr : nullptr,
+                                   y, dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_conv2d_grad_weight(
+    agpu_device* dev, const agpu_buffer* input, const agpu_buffer* grad_out, uint32_t batch,
+    uint32_t in_c, uint32_t in_h, uint32_t in_w, uint32_t out_c, uint32_t out_h, uint32_t out_w,
+    uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw, uint32_t dh,
+    uint32_t dw, uint32_t groups, agpu_buffer** out) {
+  CHECK_DEV(dev, "conv2d_grad_weight");
+  CHECK_BUF(input, "conv2d_grad_weight", "input");
+  CHECK_BUF(grad_out, "conv2d_grad_weight", "grad_out");
+  CHECK_OUT(out, "conv2d_grad_weight");
+  if (groups == 0 || in_c % groups || out_c % groups)
+    return fail(AGPU_ERR_SHAPE, "conv2d_grad_weight: channels not divisible by groups");
+  CHECK_LEN(input, (uint64_t)batch * in_c * in_h * in_w, "conv2d_grad_weight", "input");
+  CHECK_LEN(grad_out, (uint64_t)batch * out_c * out_h * out_w, "conv2d_grad_weight", "grad_out");
+  ConvParams p{(int)batch, (int)in_c, (int)in_h, (int)in_w, (int)out_c, (int)kh, (int)kw,
+               (int)sh, (int)sw, (int)ph, (int)pw, (int)dh, (int)dw, (int)groups, (int)out_h,
+               (int)out_w};
+  return with_output(dev, (uint64_t)out_c * (in_c / groups) * kh * kw, out, [&](float* gw) {
+    return launch_conv2d_grad_weight(dev, p, input->dptr, grad_out->dptr, gw, dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_conv2d_grad_bias(agpu_device* dev, const agpu_buffer* grad_out,
+                                             uint32_t batch, uint32_t out_c, uint32_t out_h,
+                                             uint32_t out_w, agpu_buffer** out) {
+  CHECK_DEV(dev, "conv2d_grad_bias");
+  CHECK_BUF(grad_out, "conv2d_grad_bias", "grad_out");
+  CHECK_OUT(out, "conv2d_grad_bias");
+  CHECK_LEN(grad_out, (uint64_t)batch * out_c * out_h * out_w, "conv2d_grad_bias", "grad_out");
+  return with_output(dev, out_c, out, [&](float* gb) {
+    return launch_conv2d_grad_bias(dev, grad_out->dptr, gb, (int)batch, (int)out_c,
+                                   (long long)out_h * out_w, dev->stream);
+  });
+}
+
 // ------------------------------------------------------------ group norm --
 static agpu_status group_norm_impl(agpu_device* dev, const agpu_buffer* x,
                                    const agpu_buffer* gamma, const agpu_buffer* beta,
@@ -269,6 +374,18 @@ agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, f
     return fail(AGPU_ERR_INVALID, "launch_gemm: NULL pointer");
   return launch_gemm(dev, a, b, c, batch, m, n, k, trans_a != 0, trans_b != 0,
                      pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_conv2d(agpu_device* dev, const float* input, const float* weight,
+                               const float* bias, float* out, uint32_t batch, uint32_t in_c,
+                               uint32_t in_h, uint32_t in_w, uint32_t out_c, uint32_t kh,
+                               uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw,
+                               uint32_t dh, uint32_t dw, uint32_t groups, void* stream) {
+  CHECK_DEV(dev, "launch_conv2d");
+  ConvParams p;
+  AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
+                         &p, "launch_conv2d"));
+  return launch_conv2d(dev, p, input, weight, bias, out, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,

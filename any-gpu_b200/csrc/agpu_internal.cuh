@@ -92,6 +92,19 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
                               uint32_t spatial, uint32_t groups, float eps, bool swish,
                               cudaStream_t s);
 
+// conv2d geometry (NCHW); ho/wo already computed.
+struct ConvParams {
+  int n, cin, h, w, cout, kh, kw, sh, sw, ph, pw, dh, dw, groups, ho, wo;
+};
+agpu_status launch_conv2d(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
+                          const float* bias, float* y, cudaStream_t s);
+agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const float* x,
+                                    const float* w, const float* bias, float* y, cudaStream_t s);
+agpu_status launch_conv2d_grad_weight(agpu_device* dev, const ConvParams& p, const float* x,
+                                      const float* gy, float* gw, cudaStream_t s);
+agpu_status launch_conv2d_grad_bias(agpu_device* dev, const float* gy, float* gb, int n, int cout,
+                                    long long hw, cudaStream_t s);
+
 enum class Unary : int { Relu = 0, Sigmoid, Swish, Tanh, Scale };
 enum class Binary : int {
   Add = 0, Sub, Mul, ReluBwd, SigmoidBwd, SwishBwd, TanhBwd

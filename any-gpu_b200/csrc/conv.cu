@@ -1,0 +1,410 @@
+// conv2d on sm_100a: implicit GEMM on tcgen05 tensor cores, plus the SIMT
+// kernels for the shapes that path does not take and for the backward ops.
+//
+// Replaces the reference's one-thread-per-output direct convolution
+// SHADER_CONV2D (src/ops/conv.rs:173-220; API :437-480): NCHW input,
+// weight [Cout, Cin/groups, kh, kw], bias (None -> zeros), stride, padding,
+// dilation, groups; out = (H + 2p - d(k-1) - 1)/s + 1.
+//
+// Tensor-core path (groups == 1, stride 1):
+//   1. stage the input NCHW -> NHWC with channels padded to Cs = ceil4(Cin)
+//      (one read + one write; makes every (pixel, 32-channel) run a
+//      128-byte row a TMA box can fetch);
+//   2. re-lay the weight to [Cout, kh, kw, Cw] with Cw = ceil32(Cin), zeros in
+//      the padding, so each (tap, 32-channel block) is one K-block;
+//   3. GEMM D[pixel, oc] = sum_k A[pixel, k] W2[oc, k], k = (kh, kw, c):
+//      M tile = 128 output pixels = BH rows x BW columns of one image,
+//      A K-block = a 4-D TMA box {32 channels, BW, BH, 1} of the NHWC input at
+//      (c0, ow0 + kw*d - p, oh0 + kh*d - p, n): out-of-range (padding)
+//      coordinates read as zeros, so no bounds checks run in the mainloop;
+//      N tile = BN output channels; the epilogue adds the bias and writes
+//      NCHW rows (lanes = consecutive output pixels -> coalesced stores).
+#include <algorithm>
+
+#include "agpu_internal.cuh"
+#include "ptx.cuh"
+#include "umma_kernel.cuh"
+
+namespace agpu {
+
+agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                             uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
+                             uint32_t box_outer, bool mn_major);
+
+using umma::BK;
+using umma::BM;
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+template <int BN_>
+struct ConvPolicy {
+  static constexpr int BN = BN_;
+  static constexpr bool A_MN = false, B_MN = false;
+  int n_img, cout, KW, ph, pw, dh, dw, Ho, Wo, BW, BH;
+  int tiles_w, tiles_h, tiles_n, cblocks, taps, cw;
+  long long tiles;
+  const float* bias;  // may be null
+  float* out;
+
+  struct Tile { int n, oh0, ow0, oc0; };
+
+  __device__ long long num_tiles() const { return tiles; }
+  __device__ int num_k() const { return taps * cblocks; }
+
+  // oc tiles innermost: consecutive CTAs reuse the same input tile from L2.
+  __device__ Tile tile(long long t) const {
+    Tile r;
+    r.oc0 = (int)(t % tiles_n) * BN;
+    long long q = t / tiles_n;
+    r.ow0 = (int)(q % tiles_w) * BW;
+    q /= tiles_w;
+    r.oh0 = (int)(q % tiles_h) * BH;
+    r.n = (int)(q / tiles_h);
+    return r;
+  }
+
+  __device__ void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
+                       uint64_t* bar, const Tile& t, int kb) const {
+    const int tap = kb / cblocks, cb = kb % cblocks;
+    const int kh = tap / KW, kw = tap % KW;
+    ptx::tma_load_4d(sa, ta, bar, cb * BK, t.ow0 + kw * dw - pw, t.oh0 + kh * dh - ph, t.n);
+    ptx::tma_load_2d(sb, tb, bar, tap * cw + cb * BK, t.oc0);
+  }
+
+  __device__ bool col_live(const Tile& t, int col0) const { return t.oc0 + col0 < cout; }
+
+  __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float*,
+                        int) const {
+    const int oh = t.oh0 + row / BW, ow = t.ow0 + row % BW;
+    if (oh >= Ho || ow >= Wo) return;
+    const long long plane = (long long)Ho * Wo;
+    float* o = out + ((long long)t.n * cout) * plane + (long long)oh * Wo + ow;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int oc = t.oc0 + col0 + j;
+      if (oc < cout) {
+        const float bb = bias ? __ldg(bias + oc) : 0.0f;
+        __stcs(o + (long long)oc * plane, __uint_as_float(v[j]) + bb);
+      }
+    }
+  }
+};
+
+// NCHW [N, C, HW] -> NHWC [N, HW, Cs] (channels >= C zero-filled).
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int C,
+                                    int HW, int Cs) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xn = x + (long long)n * C * HW;
+  float* yn = y + (long long)n * HW * Cs;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, p = p0 + threadIdx.x;
+    tile[i][threadIdx.x] = (c < C && p < HW) ? xn[(long long)c * HW + p] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int p = p0 + i, c = c0 + threadIdx.x;
+    if (p < HW && c < Cs) yn[(long long)p * Cs + c] = tile[threadIdx.x][i];
+  }
+}
+
+// W [Cout, Cin, KH, KW] -> W2 [Cout, KH, KW, Cw] (channels >= Cin zero).
+__global__ void weight_khwc_kernel(const float* __restrict__ w, float* __restrict__ w2, int Cout,
+                                   int Cin, int KH, int KW, int Cw) {
+  const long long total = (long long)Cout * KH * KW * Cw;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % Cw);
+    long long r = i / Cw;
+    const int kw = (int)(r % KW);
+    r /= KW;
+    const int kh = (int)(r % KH);
+    const int oc = (int)(r / KH);
+    w2[i] = c < Cin ? w[(((long long)oc * Cin + c) * KH + kh) * KW + kw] : 0.0f;
+  }
+}
+
+// Direct convolution, one thread per output (exact fp32; any stride,
+// dilation, groups) -- same arithmetic order as the reference shader.
+__global__ void conv2d_direct_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ bias, float* __restrict__ y,
+                                     int N, int Cin, int H, int W, int Cout, int KH, int KW,
+                                     int sh, int sw, int ph, int pw, int dh, int dw, int groups,
+                                     int Ho, int Wo) {
+  const long long total = (long long)N * Cout * Ho * Wo;
+  const int gin = Cin / groups, gout = Cout / groups;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int ow = (int)(idx % Wo);
+    const int oh = (int)((idx / Wo) % Ho);
+    const int oc = (int)((idx / ((long long)Wo * Ho)) % Cout);
+    const int n = (int)(idx / ((long long)Wo * Ho * Cout));
+    const int g = oc / gout;
+    float sum = bias ? bias[oc] : 0.0f;
+    for (int ic = 0; ic < gin; ++ic)
+      for (int kh = 0; kh < KH; ++kh) {
+        const int ih = oh * sh + kh * dh - ph;
+        if (ih < 0 || ih >= H) continue;
+        for (int kw = 0; kw < KW; ++kw) {
+          const int iw = ow * sw + kw * dw - pw;
+          if (iw < 0 || iw >= W) continue;
+          sum = fmaf(x[(((long long)n * Cin + g * gin + ic) * H + ih) * W + iw],
+                     w[(((long long)oc * gin + ic) * KH + kh) * KW + kw], sum);
+        }
+      }
+    y[idx] = sum;
+  }
+}
+
+// Transposed convolution (SHADER_CONV_TRANSPOSE2D, src/ops/conv.rs:245-296):
+// weight [Cin, Cout/groups, kh, kw].
+__global__ void conv_transpose2d_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                        const float* __restrict__ bias, float* __restrict__ y,
+                                        int N, int Cin, int H, int W, int Cout, int KH, int KW,
+                                        int sh, int sw, int ph, int pw, int dh, int dw,
+                                        int groups, int Ho, int Wo) {
+  const long long total = (long long)N * Cout * Ho * Wo;
+  const int gin = Cin / groups, gout = Cout / groups;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int ow = (int)(idx % Wo);
+    const int oh = (int)((idx / Wo) % Ho);
+    const int oc = (int)((idx / ((long long)Wo * Ho)) % Cout);
+    const int n = (int)(idx / ((long long)Wo * Ho * Cout));
+    const int g = oc / gout, ocl = oc % gout;
+    float sum = bias ? bias[oc] : 0.0f;
+    for (int ic = 0; ic < gin; ++ic)
+      for (int kh = 0; kh < KH; ++kh) {
+        const int ohf = oh + ph - kh * dh;
+        if (ohf < 0 || ohf % sh) continue;
+        const int ih = ohf / sh;
+        if (ih >= H) continue;
+        for (int kw = 0; kw < KW; ++kw) {
+          const int owf = ow + pw - kw * dw;
+          if (owf < 0 || owf % sw) continue;
+          const int iw = owf / sw;
+          if (iw >= W) continue;
+          sum = fmaf(x[(((long long)n * Cin + g * gin + ic) * H + ih) * W + iw],
+                     w[(((long long)(g * gin + ic) * gout + ocl) * KH + kh) * KW + kw], sum);
+        }
+      }
+    y[idx] = sum;
+  }
+}
+
+// grad_weight (SHADER_CONV2D_GRAD_WEIGHT, src/ops/conv.rs:337-385): one CTA
+// per weight element, the N*Ho*Wo reduction split over 256 threads.
+__global__ void __launch_bounds__(256) conv2d_grad_weight_kernel(
+    const float* __restrict__ x, const float* __restrict__ gy, float* __restrict__ gw, int N,
+    int Cin, int H, int W, int Cout, int Ho, int Wo, int KH, int KW, int sh, int sw, int ph,
+    int pw, int dh, int dw, int groups) {
+  __shared__ float red[8];
+  const int gin = Cin / groups, gout = Cout / groups;
+  const long long idx = blockIdx.x;
+  const int kw = (int)(idx % KW);
+  const int kh = (int)((idx / KW) % KH);
+  const int ic = (int)((idx / ((long long)KW * KH)) % gin);
+  const int oc = (int)(idx / ((long long)KW * KH * gin));
+  const int g = oc / gout;
+  const long long P = (long long)N * Ho * Wo;
+  float sum = 0.f;
+  for (long long p = threadIdx.x; p < P; p += blockDim.x) {
+    const int ow = (int)(p % Wo);
+    const int oh = (int)((p / Wo) % Ho);
+    const int n = (int)(p / ((long long)Wo * Ho));
+    const int ih = oh * sh + kh * dh - ph, iw = ow * sw + kw * dw - pw;
+    if (ih < 0 || iw < 0 || ih >= H || iw >= W) continue;
+    sum = fmaf(gy[(((long long)n * Cout + oc) * Ho + oh) * Wo + ow],
+               x[(((long long)n * Cin + g * gin + ic) * H + ih) * W + iw], sum);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += red[i];
+    gw[idx] = s;
+  }
+}
+
+// grad_bias (SHADER_CONV2D_GRAD_BIAS, src/ops/conv.rs:390-410): one CTA per channel.
+__global__ void __launch_bounds__(256) conv2d_grad_bias_kernel(const float* __restrict__ gy,
+                                                               float* __restrict__ gb, int N,
+                                                               int Cout, long long HW) {
+  __shared__ float red[8];
+  const int oc = blockIdx.x;
+  float sum = 0.f;
+  for (int n = 0; n < N; ++n) {
+    const float* p = gy + ((long long)n * Cout + oc) * HW;
+    for (long long i = threadIdx.x; i < HW; i += blockDim.x) sum += p[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += red[i];
+    gb[oc] = s;
+  }
+}
+
+unsigned grid_for(const agpu_device* dev, long long work) {
+  const long long want = (work + 255) / 256;
+  return (unsigned)std::max<long long>(1, std::min<long long>(want, (long long)dev->sm_count * 16));
+}
+
+template <int BN, bool X3>
+agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
+                        const float* bias, float* y, cudaStream_t s) {
+  using P = ConvPolicy<BN>;
+  using Cfg = umma::Cfg<BN, X3>;
+  const int Cs = (p.cin + 3) / 4 * 4;
+  const int Cw = (p.cin + BK - 1) / BK * BK;
+  const uint64_t xs_elems = (uint64_t)p.n * p.h * p.w * Cs;
+  const uint64_t w2_elems = (uint64_t)p.cout * p.kh * p.kw * Cw;
+  void* scratch = nullptr;
+  AGPU_TRY(pool_alloc(dev, (xs_elems + w2_elems) * sizeof(float) + 256, &scratch, s));
+  float* xs = static_cast<float*>(scratch);
+  float* w2 = xs + (xs_elems + 63) / 64 * 64;
+  {
+    dim3 grid((unsigned)ceil_div((uint64_t)p.h * p.w, 32), (unsigned)ceil_div(Cs, 32), p.n);
+    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xs, p.cin, p.h * p.w, Cs);
+    weight_khwc_kernel<<<grid_for(dev, (long long)w2_elems), 256, 0, s>>>(w, w2, p.cout, p.cin,
+                                                                          p.kh, p.kw, Cw);
+  }
+  agpu_status st = after_launch(dev, "conv staging kernels", 2);
+  if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
+
+  P pol;
+  pol.n_img = p.n; pol.cout = p.cout; pol.KW = p.kw;
+  pol.ph = p.ph; pol.pw = p.pw; pol.dh = p.dh; pol.dw = p.dw;
+  pol.Ho = p.ho; pol.Wo = p.wo;
+  int bw = 1;
+  while (bw < p.wo && bw < 128) bw *= 2;
+  pol.BW = bw;
+  pol.BH = 128 / bw;
+  pol.tiles_w = (int)ceil_div(p.wo, pol.BW);
+  pol.tiles_h = (int)ceil_div(p.ho, pol.BH);
+  pol.tiles_n = (int)ceil_div(p.cout, BN);
+  pol.cblocks = Cw / BK;
+  pol.taps = p.kh * p.kw;
+  pol.cw = Cw;
+  pol.tiles = (long long)p.n * pol.tiles_h * pol.tiles_w * pol.tiles_n;
+  pol.bias = bias;
+  pol.out = y;
+
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) { pool_free(dev, scratch, s); return fail(AGPU_ERR_CUDA, "no cuTensorMapEncodeTiled"); }
+  CUtensorMap ta, tb;
+  {
+    cuuint64_t dims[4] = {(cuuint64_t)Cs, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
+    cuuint64_t strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)p.w * Cs * 4,
+                             (cuuint64_t)p.h * p.w * Cs * 4};
+    cuuint32_t box[4] = {BK, (cuuint32_t)pol.BW, (cuuint32_t)pol.BH, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      pool_free(dev, scratch, s);
+      return fail(AGPU_ERR_CUDA, "conv2d: input tensor map encode failed (%d)", (int)r);
+    }
+  }
+  st = make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
+                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, BN, false);
+  if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
+  auto kern = umma::umma_tf32_kernel<P, X3>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg::SMEM);
+  if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
+  const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
+  kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
+  st = after_launch(dev, "conv2d_tf32 (umma_tf32_kernel)");
+  pool_free(dev, scratch, s);
+  return st;
+}
+
+// BN: output-channel tile minimising padding (N of the MMA, multiple of 32).
+template <bool X3>
+agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float* x,
+                             const float* w, const float* bias, float* y, cudaStream_t s) {
+  if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3>(dev, p, x, w, bias, y, s);
+  if (p.cout >= 256) return run_conv_tc<256, X3>(dev, p, x, w, bias, y, s);
+  if (p.cout > 96) return run_conv_tc<128, X3>(dev, p, x, w, bias, y, s);
+  return run_conv_tc<64, X3>(dev, p, x, w, bias, y, s);
+}
+
+}  // namespace
+
+bool conv_tc_eligible(const ConvParams& p) {
+  return p.groups == 1 && p.sh == 1 && p.sw == 1 && p.cout >= 16 &&
+         (long long)p.n * p.cout * p.ho * p.wo * p.cin * p.kh * p.kw >= (1LL << 22) &&
+         p.n <= 65535;
+}
+
+agpu_status launch_conv2d(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
+                          const float* bias, float* y, cudaStream_t s) {
+  const long long total = (long long)p.n * p.cout * p.ho * p.wo;
+  if (total == 0) return AGPU_OK;
+  if (dev->precision != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
+    if (dev->precision == AGPU_PREC_TF32X3) return dispatch_conv_tc<true>(dev, p, x, w, bias, y, s);
+    return dispatch_conv_tc<false>(dev, p, x, w, bias, y, s);
+  }
+  conv2d_direct_kernel<<<grid_for(dev, total), 256, 0, s>>>(
+      x, w, bias, y, p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, p.sh, p.sw, p.ph, p.pw, p.dh, p.dw,
+      p.groups, p.ho, p.wo);
+  return after_launch(dev, "conv2d_direct_kernel");
+}
+
+agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const float* x,
+                                    const float* w, const float* bias, float* y,
+                                    cudaStream_t s) {
+  const long long total = (long long)p.n * p.cout * p.ho * p.wo;
+  if (total == 0) return AGPU_OK;
+  conv_transpose2d_kernel<<<grid_for(dev, total), 256, 0, s>>>(
+      x, w, bias, y, p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, p.sh, p.sw, p.ph, p.pw, p.dh, p.dw,
+      p.groups, p.ho, p.wo);
+  return after_launch(dev, "conv_transpose2d_kernel");
+}
+
+agpu_status launch_conv2d_grad_weight(agpu_device* dev, const ConvParams& p, const float* x,
+                                      const float* gy, float* gw, cudaStream_t s) {
+  const long long nw = (long long)p.cout * (p.cin / p.groups) * p.kh * p.kw;
+  if (nw == 0) return AGPU_OK;
+  if (nw > 0x7fffffffLL) return fail(AGPU_ERR_UNSUPPORTED, "conv2d_grad_weight: too many weights");
+  conv2d_grad_weight_kernel<<<(unsigned)nw, 256, 0, s>>>(x, gy, gw, p.n, p.cin, p.h, p.w, p.cout,
+                                                         p.ho, p.wo, p.kh, p.kw, p.sh, p.sw, p.ph,
+                                                         p.pw, p.dh, p.dw, p.groups);
+  return after_launch(dev, "conv2d_grad_weight_kernel");
+}
+
+agpu_status launch_conv2d_grad_bias(agpu_device* dev, const float* gy, float* gb, int n, int cout,
+                                    long long hw, cudaStream_t s) {
+  if (cout == 0) return AGPU_OK;
+  conv2d_grad_bias_kernel<<<(unsigned)cout, 256, 0, s>>>(gy, gb, n, cout, hw);
+  return after_launch(dev, "conv2d_grad_bias_kernel");
+}
+
+}  // namespace agpu

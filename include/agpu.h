@@ -128,6 +128,43 @@ AGPU_API agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agp
 AGPU_API agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows,
                                   uint32_t cols, agpu_buffer** out);
 
+/* ------------------------------------------------------------- conv2d ----- */
+/* GpuDevice::conv2d (src/ops/conv.rs:437-480): input [batch, in_c, in_h, in_w],
+ * weight [out_c, in_c/groups, kh, kw], bias [out_c] or NULL (zeros), NCHW.
+ * out [batch, out_c, out_h, out_w], out = (in + 2*pad - dil*(k-1) - 1)/stride + 1.
+ * The reference's (stride, padding, dilation) tuples are passed as (h, w) pairs. */
+AGPU_API agpu_status agpu_conv2d(agpu_device* dev, const agpu_buffer* input,
+                                 const agpu_buffer* weight, const agpu_buffer* bias,
+                                 uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+                                 uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t stride_h,
+                                 uint32_t stride_w, uint32_t pad_h, uint32_t pad_w,
+                                 uint32_t dil_h, uint32_t dil_w, uint32_t groups,
+                                 agpu_buffer** out);
+/* GpuDevice::conv_transpose2d (src/ops/conv.rs:484-530): weight
+ * [in_c, out_c/groups, kh, kw]; out = (in-1)*stride - 2*pad + dil*(k-1) + out_pad + 1. */
+AGPU_API agpu_status agpu_conv_transpose2d(agpu_device* dev, const agpu_buffer* input,
+                                           const agpu_buffer* weight, const agpu_buffer* bias,
+                                           uint32_t batch, uint32_t in_c, uint32_t in_h,
+                                           uint32_t in_w, uint32_t out_c, uint32_t kh, uint32_t kw,
+                                           uint32_t stride_h, uint32_t stride_w, uint32_t pad_h,
+                                           uint32_t pad_w, uint32_t out_pad_h, uint32_t out_pad_w,
+                                           uint32_t dil_h, uint32_t dil_w, uint32_t groups,
+                                           agpu_buffer** out);
+/* GpuDevice::conv2d_grad_weight (src/ops/conv.rs:531-549, used by the autograd
+ * conv backward src/autograd.rs:376-427): dW [out_c, in_c/groups, kh, kw]. */
+AGPU_API agpu_status agpu_conv2d_grad_weight(agpu_device* dev, const agpu_buffer* input,
+                                             const agpu_buffer* grad_out, uint32_t batch,
+                                             uint32_t in_c, uint32_t in_h, uint32_t in_w,
+                                             uint32_t out_c, uint32_t out_h, uint32_t out_w,
+                                             uint32_t kh, uint32_t kw, uint32_t stride_h,
+                                             uint32_t stride_w, uint32_t pad_h, uint32_t pad_w,
+                                             uint32_t dil_h, uint32_t dil_w, uint32_t groups,
+                                             agpu_buffer** out);
+/* GpuDevice::conv2d_grad_bias (src/ops/conv.rs:551-563): db [out_c]. */
+AGPU_API agpu_status agpu_conv2d_grad_bias(agpu_device* dev, const agpu_buffer* grad_out,
+                                           uint32_t batch, uint32_t out_c, uint32_t out_h,
+                                           uint32_t out_w, agpu_buffer** out);
+
 /* ------------------------------------------------------------ group norm -- */
 /* GpuDevice::group_norm (src/ops/norm.rs:210-278): x [batch, channels, spatial]
  * in `groups` groups of channels/groups channels; y = (x-mean)/sqrt(var+eps) *
@@ -188,6 +225,13 @@ AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, 
 AGPU_API agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
                                       uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                       int trans_a, int trans_b, void* stream);
+AGPU_API agpu_status agpu_launch_conv2d(agpu_device* dev, const float* input, const float* weight,
+                                        const float* bias, float* out, uint32_t batch,
+                                        uint32_t in_c, uint32_t in_h, uint32_t in_w,
+                                        uint32_t out_c, uint32_t kh, uint32_t kw,
+                                        uint32_t stride_h, uint32_t stride_w, uint32_t pad_h,
+                                        uint32_t pad_w, uint32_t dil_h, uint32_t dil_w,
+                                        uint32_t groups, void* stream);
 AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,
                                             const float* beta, float* y, uint32_t batch,
                                             uint32_t channels, uint32_t spatial, uint32_t groups,

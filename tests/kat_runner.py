@@ -6,7 +6,8 @@ import numpy as np
 # ops of the reference whose C-ABI entry points exist in this build
 GPU_OPS = {"matmul", "batch_matmul", "softmax", "add", "sub", "mul", "relu", "sigmoid", "swish",
            "tanh", "scale", "relu_backward", "sigmoid_backward", "swish_backward",
-           "tanh_backward", "transpose", "group_norm"}
+           "tanh_backward", "transpose", "group_norm", "conv2d", "conv_transpose2d",
+           "conv2d_grad_bias"}
 
 
 def run_oracle(orc, case) -> np.ndarray:
@@ -55,6 +56,22 @@ def run_gpu(dev, case) -> np.ndarray:
                                          a["k"]))
     if op == "softmax":
         return dev.read(dev.softmax(up(x["x"]), a["rows"], a["cols"]))
+    if op == "conv2d":
+        bias = up(x["bias"]) if x["bias"] is not None else None
+        return dev.read(dev.conv2d(up(x["input"]), up(x["weight"]), bias, a["batch"], a["in_c"],
+                                   a["in_h"], a["in_w"], a["out_c"], a["kh"], a["kw"],
+                                   tuple(a["stride"]), tuple(a["padding"]), tuple(a["dilation"]),
+                                   a["groups"]))
+    if op == "conv_transpose2d":
+        bias = up(x["bias"]) if x["bias"] is not None else None
+        return dev.read(dev.conv_transpose2d(up(x["input"]), up(x["weight"]), bias, a["batch"],
+                                             a["in_c"], a["in_h"], a["in_w"], a["out_c"],
+                                             a["kh"], a["kw"], tuple(a["stride"]),
+                                             tuple(a["padding"]), tuple(a["output_padding"]),
+                                             tuple(a["dilation"]), a["groups"]))
+    if op == "conv2d_grad_bias":
+        return dev.read(dev.conv2d_grad_bias(up(x["grad_out"]), a["batch"], a["out_c"],
+                                             a["out_h"], a["out_w"]))
     if op == "group_norm":
         return dev.read(dev.group_norm(up(x["x"]), up(x["gamma"]), up(x["beta"]), a["batch"],
                                        a["channels"], a["spatial"], a["groups"], a["eps"]))

@@ -230,3 +230,83 @@ def test_group_norm_errors(dev):
         with pytest.raises(AnyGpuError) as e:
             dev.group_norm(x, g, g, *args, 1e-5)
         assert e.value.status == 1
+
+
+CONV_CASES = [
+    # n, cin, h, w, cout, k, stride, pad, dil, groups
+    (2, 320, 32, 32, 320, 3, 1, 1, 1, 1),   # UNet block channels (tensor-core path, BN=160)
+    (1, 3, 17, 19, 64, 3, 1, 1, 1, 1),      # Cin=3 staged to 4 channels, ragged 19-wide rows
+    (2, 64, 56, 56, 128, 1, 1, 0, 1, 1),    # 1x1
+    (1, 32, 24, 24, 48, 5, 1, 2, 1, 1),     # 5x5, Cout=48 (BN=64 tail)
+    (1, 40, 20, 30, 256, 3, 1, 2, 2, 1),    # dilation 2
+    (1, 16, 33, 33, 32, 3, 2, 1, 1, 1),     # stride 2 -> direct kernel
+    (2, 8, 12, 12, 8, 3, 1, 1, 1, 2),       # groups 2 -> direct kernel
+]
+
+
+@pytest.mark.parametrize("prec", ["tf32", "tf32x3"])
+@pytest.mark.parametrize("case", CONV_CASES, ids=[str(c) for c in CONV_CASES])
+def test_conv2d_parity(dev, orc, case, prec):
+    n, cin, h, w, cout, k, s, p, d, g = case
+    r = np.random.default_rng(cin * cout + h)
+    x = r.standard_normal(n * cin * h * w).astype(np.float32)
+    bound = np.sqrt(6.0 / (cin // g * k * k))  # Kaiming-uniform, gain sqrt(2)
+    wt = r.uniform(-bound, bound, cout * (cin // g) * k * k).astype(np.float32)
+    bias = r.standard_normal(cout).astype(np.float32)
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.conv2d(dev.upload(x), dev.upload(wt), dev.upload(bias), n, cin, h, w,
+                                  cout, k, k, (s, s), (p, p), (d, d), g))
+    finally:
+        dev.set_precision("tf32")
+    want = orc.conv2d(x, wt, bias, n, cin, h, w, cout, k, k, (s, s), (p, p), (d, d), g,
+                      threads=True)
+    assert orc.rel_fro(got, want) <= TOL[prec]
+
+
+def test_conv2d_unet_full_size_sampled(dev, orc):
+    """Config 4's conv at full size (N16, 320->320, 64x64, 3x3 pad 1), Kaiming-
+    uniform weights, bias 0: sampled output planes against float64."""
+    n, c, h, w = 16, 320, 64, 64
+    r = np.random.default_rng(1237)
+    x = r.standard_normal(n * c * h * w, dtype=np.float32)
+    bound = np.float32(np.sqrt(6.0 / (c * 9)))
+    wt = r.uniform(-bound, bound, c * c * 9).astype(np.float32)
+    y = dev.read(dev.conv2d(dev.upload(x), dev.upload(wt), None, n, c, h, w, c, 3, 3, (1, 1),
+                            (1, 1), (1, 1), 1)).reshape(n, c, h, w)
+    X = np.pad(x.reshape(n, c, h, w).astype(np.float64), ((0, 0), (0, 0), (1, 1), (1, 1)))
+    W = wt.reshape(c, c, 3, 3).astype(np.float64)
+    for ni, oc in [(0, 0), (7, 159), (15, 319), (3, 160)]:
+        ref = np.zeros((h, w))
+        for i in range(3):
+            for j in range(3):
+                ref += np.einsum("chw,c->hw", X[ni, :, i:i + h, j:j + w], W[oc, :, i, j])
+        assert orc.rel_fro(y[ni, oc], ref) <= 1e-3
+
+
+def test_conv_backward_ops_parity(dev, orc):
+    r = np.random.default_rng(77)
+    n, cin, h, w, cout, k = 2, 6, 9, 8, 4, 3
+    x = r.standard_normal(n * cin * h * w).astype(np.float32)
+    oh = ow_ = None
+    for s, p, d in [(1, 1, 1), (2, 0, 1), (1, 2, 2)]:
+        oh = (h + 2 * p - d * (k - 1) - 1) // s + 1
+        ow_ = (w + 2 * p - d * (k - 1) - 1) // s + 1
+        gy = r.standard_normal(n * cout * oh * ow_).astype(np.float32)
+        gw = dev.read(dev.conv2d_grad_weight(dev.upload(x), dev.upload(gy), n, cin, h, w, cout,
+                                             oh, ow_, k, k, s, s, p, p, d, d, 1))
+        want = orc.conv2d_grad_weight(x, gy, n, cin, h, w, cout, oh, ow_, k, k, s, s, p, p, d, d,
+                                      1)
+        assert orc.rel_fro(gw, want) <= 1e-5
+        gb = dev.read(dev.conv2d_grad_bias(dev.upload(gy), n, cout, oh, ow_))
+        assert orc.rel_fro(gb, orc.conv2d_grad_bias(gy, n, cout, oh, ow_)) <= 1e-5
+    # transposed conv with stride, padding, output padding, groups
+    for s, p, op_, d, g in [(2, 1, 1, 1, 1), (1, 0, 0, 2, 2), (3, 2, 0, 1, 1)]:
+        wt = r.standard_normal(cin * (cout // g) * k * k).astype(np.float32)
+        bias = r.standard_normal(cout).astype(np.float32)
+        got = dev.read(dev.conv_transpose2d(dev.upload(x), dev.upload(wt), dev.upload(bias), n,
+                                            cin, h, w, cout, k, k, (s, s), (p, p), (op_, op_),
+                                            (d, d), g))
+        want = orc.conv_transpose2d(x, wt, bias, n, cin, h, w, cout, k, k, (s, s), (p, p),
+                                    (op_, op_), (d, d), g)
+        assert orc.rel_fro(got, want) <= 1e-5
