@@ -87,13 +87,14 @@ struct ConvPolicy {
     const int tap = kb / cblocks, cb = kb % cblocks;
     const int kh = tap / KW, kw = tap % KW;
     ptx::tma_load_4d(sa, ta, bar, cb * BK, t.ow0 + kw * dw - pw, t.oh0 + kh * dh - ph, t.n);
-    ptx::tma_load_2d(sb, tb, bar, tap * cw + cb * BK, t.oc0);
+    // the weight map is 3-D {K, Cout, 1} (make_tmap_f32_3d): load with a 3-D box
+    ptx::tma_load_3d(sb, tb, bar, tap * cw + cb * BK, t.oc0, 0);
   }
 
   __device__ bool col_live(const Tile& t, int col0) const { return t.oc0 + col0 < cout; }
 
   __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float*,
-                        int) const {
+                        int, bool accumulate) const {
     const int oh = t.oh0 + row / BW, ow = t.ow0 + row % BW;
     if (oh >= Ho || ow >= Wo) return;
     const long long plane = (long long)Ho * Wo;
@@ -102,8 +103,13 @@ struct ConvPolicy {
     for (int j = 0; j < 32; ++j) {
       const int oc = t.oc0 + col0 + j;
       if (oc < cout) {
-        const float bb = bias ? __ldg(bias + oc) : 0.0f;
-        __stcs(o + (long long)oc * plane, __uint_as_float(v[j]) + bb);
+        float* dst = o + (long long)oc * plane;
+        if (accumulate) {
+          *dst += __uint_as_float(v[j]);
+        } else {
+          const float bb = bias ? __ldg(bias + oc) : 0.0f;
+          __stcs(dst, __uint_as_float(v[j]) + bb);
+        }
       }
     }
   }

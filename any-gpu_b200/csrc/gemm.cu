@@ -95,7 +95,7 @@ struct GemmPolicy {
   // warp transposes its 32x32 block through shared memory so that each
   // store instruction writes four full 128-byte row segments.
   __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float* stg,
-                        int lane) const {
+                        int lane, bool accumulate) const {
     float4* srow = reinterpret_cast<float4*>(stg + lane * kEpiStride);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -109,8 +109,15 @@ struct GemmPolicy {
     for (int i = 0; i < 8; ++i) {
       const int r = i * 4 + (lane >> 3);
       const int grow = row_base + r;
-      const float4 val = *reinterpret_cast<const float4*>(stg + r * kEpiStride + (lane & 7) * 4);
-      if (grow < M && col < N) *reinterpret_cast<float4*>(Cb + (long long)grow * N + col) = val;
+      float4 val = *reinterpret_cast<const float4*>(stg + r * kEpiStride + (lane & 7) * 4);
+      if (grow < M && col < N) {
+        float4* dst = reinterpret_cast<float4*>(Cb + (long long)grow * N + col);
+        if (accumulate) {
+          const float4 o = *dst;
+          val.x += o.x; val.y += o.y; val.z += o.z; val.w += o.w;
+        }
+        *dst = val;
+      }
     }
     __syncwarp();
   }

@@ -1,3 +1,10 @@
+// K segments: in 3xTF32 mode a tile's K loop is split into segments of
+// kSegX3 K-blocks, each accumulated in its own TMEM buffer and summed by the
+// epilogue in fp32, which bounds the number of MMAs accumulated into one
+// tensor-memory accumulator (its rounding error grows with that count).
+// All segments of a tile run on the same CTA, in order, so the epilogue's
+// read-modify-write of the output needs no synchronisation.
+//
 // Warp-specialised tcgen05 (kind::tf32) mainloop shared by the contraction
 // kernels (GEMM, implicit-GEMM conv2d).  A Policy supplies what differs:
 // the tile scheduler, the TMA loads of one K-block, and the epilogue store.
@@ -28,6 +35,7 @@ constexpr int BM = 128;
 constexpr int BK = 32;          // fp32 elements per 128-byte swizzle row
 constexpr int kEpiWarps = 4;
 constexpr int kEpiStride = 36;  // floats per epilogue staging row (conflict-free float4)
+constexpr int kSegX3 = 16;      // K-blocks per accumulator segment in 3xTF32 mode
 
 template <int BN_, bool X3>
 struct Cfg {
@@ -77,8 +85,11 @@ __device__ __forceinline__ void split_tf32(uint32_t* hi, uint32_t* lo, int words
 //   void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
 //             uint64_t* bar, const Tile&, int kb) const;       // issues STAGE_BYTES of TMA
 //   void store(const Tile&, int row, int col0, const uint32_t (&v)[32], float* stg,
-//              int lane) const;   // row = accumulator lane 0..127, cols col0..col0+31;
-//                                 // called by all 32 lanes of a warp together
+//              int lane, bool accumulate) const;
+//                                 // row = accumulator lane 0..127, cols col0..col0+31;
+//                                 // called by all 32 lanes of a warp together;
+//                                 // accumulate: add to the value stored for the
+//                                 // previous K segment of this tile
 //   bool col_live(const Tile&, int col0) const;  // warp-uniform: chunk has any valid column
 template <class P, bool X3>
 __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
@@ -138,6 +149,7 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_k = pol.num_k();
   const long long num_tiles = pol.num_tiles();
+  const int kseg = X3 ? kSegX3 : (num_k > 0 ? num_k : 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -147,7 +159,7 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
       long long issued = 0;
       for (long long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const auto tile = pol.tile(t);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = 0; kb < num_k; ++kb) {  // segments are consecutive K ranges
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1, status, 0x101, abort_flag)) {
             ok = false;
             break;
@@ -172,37 +184,43 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (long long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, status, 0x102, abort_flag)) break;
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
-          uint64_t* ready = X3 ? &conv[stage] : &full[stage];
-          if (!ptx::mbar_wait(ready, phase, status, 0x103, abort_flag)) { ok = false; break; }
-          ptx::tc_fence_after();
-          const uint32_t a_addr = ptx::smem_u32(stage_a(stage));
-          const uint32_t b_addr = ptx::smem_u32(stage_b(stage));
-          const uint32_t la_addr = ptx::smem_u32(lo_a(stage));
-          const uint32_t lb_addr = ptx::smem_u32(lo_b(stage));
-#pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint32_t a_off = P::A_MN ? kk * 1024 : kk * 32;
-            const uint32_t b_off = P::B_MN ? kk * 1024 : kk * 32;
-            const uint64_t ad = operand_desc<P::A_MN>(a_addr + a_off);
-            const uint64_t bd = operand_desc<P::B_MN>(b_addr + b_off);
-            ptx::mma_tf32_ss(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-            if (X3) {
-              ptx::mma_tf32_ss(d_tmem, ad, operand_desc<P::B_MN>(lb_addr + b_off), idesc, 1u);
-              ptx::mma_tf32_ss(d_tmem, operand_desc<P::A_MN>(la_addr + a_off), bd, idesc, 1u);
-            }
+      for (long long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        for (int k0 = 0; k0 < num_k && ok; k0 += kseg, ++local) {
+          const int k1 = min(num_k, k0 + kseg);
+          const int acc = local & 1;
+          const uint32_t acc_phase = (local >> 1) & 1;
+          if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, status, 0x102, abort_flag)) {
+            ok = false;
+            break;
           }
-          ptx::mma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          ptx::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (int kb = k0; kb < k1; ++kb) {
+            uint64_t* ready = X3 ? &conv[stage] : &full[stage];
+            if (!ptx::mbar_wait(ready, phase, status, 0x103, abort_flag)) { ok = false; break; }
+            ptx::tc_fence_after();
+            const uint32_t a_addr = ptx::smem_u32(stage_a(stage));
+            const uint32_t b_addr = ptx::smem_u32(stage_b(stage));
+            const uint32_t la_addr = ptx::smem_u32(lo_a(stage));
+            const uint32_t lb_addr = ptx::smem_u32(lo_b(stage));
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint32_t a_off = P::A_MN ? kk * 1024 : kk * 32;
+              const uint32_t b_off = P::B_MN ? kk * 1024 : kk * 32;
+              const uint64_t ad = operand_desc<P::A_MN>(a_addr + a_off);
+              const uint64_t bd = operand_desc<P::B_MN>(b_addr + b_off);
+              ptx::mma_tf32_ss(d_tmem, ad, bd, idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+              if (X3) {
+                ptx::mma_tf32_ss(d_tmem, ad, operand_desc<P::B_MN>(lb_addr + b_off), idesc, 1u);
+                ptx::mma_tf32_ss(d_tmem, operand_desc<P::A_MN>(la_addr + a_off), bd, idesc, 1u);
+              }
+            }
+            ptx::mma_commit(&empty[stage]);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          ptx::mma_commit(&tfull[acc]);
         }
-        if (!ok) break;
-        ptx::mma_commit(&tfull[acc]);
       }
       ptx::mma_commit(drain);
       ptx::mbar_wait(drain, 0, status, 0x104, nullptr);
@@ -211,22 +229,28 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
     const int q = warp & 3;  // TMEM sub-partition this warp may access
     float* stg = epi + (warp - 2) * 32 * kEpiStride;
     int local = 0;
-    for (long long t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    bool ok = true;
+    for (long long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       const auto tile = pol.tile(t);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x105, abort_flag)) break;
-      ptx::tc_fence_after();
+      for (int k0 = 0; k0 < num_k; k0 += kseg, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x105, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        if (!pol.col_live(tile, c * 32)) break;  // warp-uniform
-        uint32_t v[32];
-        ptx::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
-        ptx::tmem_wait_ld();
-        pol.store(tile, q * 32 + lane, c * 32, v, stg, lane);
+        for (int c = 0; c < BN / 32; ++c) {
+          if (!pol.col_live(tile, c * 32)) break;  // warp-uniform
+          uint32_t v[32];
+          ptx::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
+          ptx::tmem_wait_ld();
+          pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, k0 > 0);
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&tempty[acc]);
       }
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&tempty[acc]);
     }
   } else if (X3) {
     const int ctid = threadIdx.x - (2 + kEpiWarps) * 32;

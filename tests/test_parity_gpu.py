@@ -226,7 +226,7 @@ def test_group_norm_errors(dev):
     from any_gpu import AnyGpuError
     x = dev.upload(np.ones(10, np.float32))
     g = dev.upload(np.ones(5, np.float32))
-    for args in [(1, 5, 2, 2), (1, 5, 2, 3), (2, 5, 1, 5)]:
+    for args in [(1, 5, 2, 2), (1, 5, 2, 3), (2, 5, 2, 5)]:
         with pytest.raises(AnyGpuError) as e:
             dev.group_norm(x, g, g, *args, 1e-5)
         assert e.value.status == 1
