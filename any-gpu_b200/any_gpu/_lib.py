@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple] = {
                                           C.c_void_p, u32, u32, u32, u32, f32, i32,
                                           C.c_void_p]),
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
+    "agpu_group_norm_noalloc": (c_status, [C.c_void_p] * 4 + [u32, u32, u32, u32, f32, i32,
+                                                              C.c_void_p]),
 }
 
 _LIB = None

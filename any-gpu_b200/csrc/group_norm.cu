@@ -254,4 +254,103 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
   return st;
 }
 
+// ---------------------------------------------------------------------------
+// agpu_group_norm_noalloc: group norm that never allocates device memory.
+//
+// Some callers may not allocate device memory themselves: a serving process
+// that owns every byte of device memory through its own arena and a hard cap,
+// a foreign host (Rust, Go, JNI) that hands over only device pointers and a
+// stream, or a latency-critical loop that cannot pay for an allocation's
+// implicit synchronisation.  For them this entry point runs the chunked
+// two-kernel group norm with its per-chunk (mean, M2) partials in the
+// fixed-size array below instead of the device pool.
+//
+// * The array is part of this library's device image: every GPU that loads
+//   the library holds its 512 KiB until the process exits.
+// * Limit: batch * groups * ceil(channels/groups * spatial / 8192) partials
+//   <= kNoAllocPartials (65536), and batch * groups <= 65535; larger shapes
+//   return AGPU_ERR_UNSUPPORTED without launching anything.
+// * All calls share the array and it keeps the last call's contents.  Nothing
+//   in it has to start at zero: the first kernel writes every slot the second
+//   one reads.  Calls that overlap on the GPU (other streams, other host
+//   threads) race on it; order them on one stream or with events.
+// * The first call on a device does the set-up for that device (looks up the
+//   array's device address with cudaGetSymbolAddress, which also makes the
+//   CUDA runtime load this library's module there).  Make that first call
+//   before any stream capture.
+namespace {
+
+constexpr uint64_t kNoAllocPartials = 65536;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float2 g_gn_noalloc_partials[kNoAllocPartials];
+
+std::mutex g_noalloc_mu;
+float2* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the partials array on the current device (set up once).
+agpu_status noalloc_partials(float2** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "group_norm_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(AGPU_ERR_UNSUPPORTED, "group_norm_noalloc: device ordinal %d >= %d", dev,
+                kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gn_noalloc_partials);
+    if (e != cudaSuccess)
+      return cuda_status(e, "group_norm_noalloc: cudaGetSymbolAddress(partials)");
+    g_noalloc_ptr[dev] = static_cast<float2*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return AGPU_OK;
+}
+
+}  // namespace
+
 }  // namespace agpu
+
+extern "C" agpu_status agpu_group_norm_noalloc(const float* x, const float* gamma,
+                                               const float* beta, float* y, uint32_t batch,
+                                               uint32_t channels, uint32_t spatial,
+                                               uint32_t groups, float eps, int apply_swish,
+                                               void* stream) {
+  using namespace agpu;
+  if (groups == 0 || channels % groups != 0)
+    return fail(AGPU_ERR_SHAPE, "group_norm_noalloc: channels (%u) not divisible by groups (%u)",
+                channels, groups);
+  const uint64_t total = (uint64_t)batch * channels * spatial;
+  if (total == 0) return AGPU_OK;
+  if (!x || !gamma || !beta || !y)
+    return fail(AGPU_ERR_INVALID, "group_norm_noalloc: NULL pointer");
+  const uint64_t gsize = (uint64_t)(channels / groups) * spatial;
+  const uint64_t groups_total = (uint64_t)batch * groups;
+  const uint64_t nchunks = group_norm_chunk_count(gsize);
+  if (groups_total > 65535 || groups_total * nchunks > kNoAllocPartials)
+    return fail(AGPU_ERR_UNSUPPORTED,
+                "group_norm_noalloc: %llu groups x %llu chunks of 8192 elements need %llu "
+                "partials; the fixed scratch holds %llu (and at most 65535 groups)",
+                (unsigned long long)groups_total, (unsigned long long)nchunks,
+                (unsigned long long)(groups_total * nchunks),
+                (unsigned long long)kNoAllocPartials);
+  float2* partials = nullptr;
+  AGPU_TRY(noalloc_partials(&partials));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int chunk = 8192;
+  dim3 grid((unsigned)nchunks, (unsigned)groups_total);
+  const uint32_t cpg = channels / groups;
+  gn_partial_kernel<<<grid, kThreads, 0, s>>>(x, partials, (long long)gsize, chunk);
+  if (apply_swish)
+    gn_apply_kernel<true><<<grid, kThreads, 0, s>>>(x, partials, gamma, beta, y,
+                                                    (long long)gsize, chunk, (int)nchunks,
+                                                    (int)spatial, (int)cpg, (int)groups, eps);
+  else
+    gn_apply_kernel<false><<<grid, kThreads, 0, s>>>(x, partials, gamma, beta, y,
+                                                     (long long)gsize, chunk, (int)nchunks,
+                                                     (int)spatial, (int)cpg, (int)groups, eps);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "group_norm_noalloc: launch");
+  return AGPU_OK;
+}

@@ -239,6 +239,28 @@ AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, co
 AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
                                          uint64_t rows, uint32_t cols, void* stream);
 
+/* ------------------------------------------- allocation-free group norm -- */
+/* No counterpart in the reference.  Group norm (same math as agpu_group_norm,
+ * swish fused when apply_swish != 0) for callers that may not allocate
+ * device memory themselves -- a process that owns all device memory through
+ * its own arena and cap, a foreign host that passes only device pointers and
+ * a stream, a latency-critical loop that cannot pay for an allocation's
+ * implicit synchronisation.  It allocates nothing: its scratch (per-chunk
+ * partial statistics) lives in a fixed 512 KiB array inside the library,
+ * held by every GPU that loads the library until exit.
+ * Inputs and output are caller-owned device pointers on the current CUDA
+ * device; `stream` is a cudaStream_t (NULL = the default stream).
+ * Limit: batch*groups*ceil((channels/groups)*spatial/8192) <= 65536 and
+ * batch*groups <= 65535, else AGPU_ERR_UNSUPPORTED (nothing launched).
+ * The first call on a device sets that device up (looks up the array's
+ * address); make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race, so order them on one stream. */
+AGPU_API agpu_status agpu_group_norm_noalloc(const float* x, const float* gamma,
+                                             const float* beta, float* y, uint32_t batch,
+                                             uint32_t channels, uint32_t spatial,
+                                             uint32_t groups, float eps, int apply_swish,
+                                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif
