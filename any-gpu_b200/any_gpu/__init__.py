@@ -240,6 +240,23 @@ class GpuDevice:
         return self._new(_lib.load().agpu_group_norm_swish, x.handle, gamma.handle, beta.handle,
                          batch, channels, spatial, groups, C.c_float(eps))
 
+    # ---------------------------------------------------------------- sdpa --
+    def scaled_dot_product_attention(self, q, k, v, batch_heads: int, seq_len: int,
+                                     d_k: int) -> GpuBuffer:
+        """Reference: `scaled_dot_product_attention(q, k, v, batch_heads, seq_len, d_k)`
+        (src/ops/attention.rs:149)."""
+        return self._new(_lib.load().agpu_scaled_dot_product_attention, q.handle, k.handle,
+                         v.handle, batch_heads, seq_len, d_k)
+
+    def sdpa_causal(self, q, k, v, batch_heads: int, seq_len: int, d_k: int) -> GpuBuffer:
+        return self._new(_lib.load().agpu_sdpa_causal, q.handle, k.handle, v.handle,
+                         batch_heads, seq_len, d_k)
+
+    def launch_sdpa(self, q_ptr, k_ptr, v_ptr, o_ptr, bh, s, d, causal=False,
+                    stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_sdpa(self._h, q_ptr, k_ptr, v_ptr, o_ptr, bh, s, d,
+                                            int(causal), stream or None))
+
     # --------------------------------------------------------- elementwise --
     def add(self, a, b): return self._new(_lib.load().agpu_add, a.handle, b.handle)
     def sub(self, a, b): return self._new(_lib.load().agpu_sub, a.handle, b.handle)

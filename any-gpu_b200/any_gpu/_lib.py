@@ -51,6 +51,9 @@ SIGNATURES: dict[str, tuple] = {
                                    P_buf]),
     "agpu_group_norm_swish": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, u32, f32,
                                          P_buf]),
+    "agpu_scaled_dot_product_attention": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32,
+                                                     P_buf]),
+    "agpu_sdpa_causal": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, P_buf]),
     "agpu_add": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_sub": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_mul": (c_status, [c_dev, c_buf, c_buf, P_buf]),
@@ -73,6 +76,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_group_norm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
                                           C.c_void_p, u32, u32, u32, u32, f32, i32,
                                           C.c_void_p]),
+    "agpu_launch_sdpa": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32, u32, u32, i32,
+                                                                 C.c_void_p]),
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
     "agpu_group_norm_noalloc": (c_status, [C.c_void_p] * 4 + [u32, u32, u32, u32, f32, i32,
                                                               C.c_void_p]),

@@ -286,6 +286,41 @@ extern "C" agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer
                          "group_norm_swish");
 }
 
+// ------------------------------------------------------------------ sdpa --
+static agpu_status sdpa_impl(agpu_device* dev, const agpu_buffer* q, const agpu_buffer* k,
+                             const agpu_buffer* v, uint32_t bh, uint32_t s, uint32_t d,
+                             bool causal, agpu_buffer** out, const char* fn) {
+  if (!dev) return fail(AGPU_ERR_INVALID, "%s: NULL device", fn);
+  if (!q || !k || !v) return fail(AGPU_ERR_INVALID, "%s: input is NULL", fn);
+  if (!out) return fail(AGPU_ERR_INVALID, "%s: out is NULL", fn);
+  *out = nullptr;
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  // the reference's transpose/batch_matmul checks (src/ops/tensor_ops.rs:257,
+  // src/ops/conv.rs:427-428) require each of Q, K, V to hold bh*s*d elements
+  const uint64_t n = (uint64_t)bh * s * d;
+  if (q->len != n || k->len != n || v->len != n)
+    return fail(AGPU_ERR_SHAPE, "%s: Q/K/V have %llu/%llu/%llu elems, expected %llu", fn,
+                (unsigned long long)q->len, (unsigned long long)k->len,
+                (unsigned long long)v->len, (unsigned long long)n);
+  return with_output(dev, n, out, [&](float* o) {
+    return launch_attention(dev, q->dptr, k->dptr, v->dptr, o, bh, s, d, causal, dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_scaled_dot_product_attention(agpu_device* dev, const agpu_buffer* q,
+                                                         const agpu_buffer* k,
+                                                         const agpu_buffer* v, uint32_t bh,
+                                                         uint32_t s, uint32_t d,
+                                                         agpu_buffer** out) {
+  return sdpa_impl(dev, q, k, v, bh, s, d, false, out, "scaled_dot_product_attention");
+}
+
+extern "C" agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
+                                        const agpu_buffer* k, const agpu_buffer* v, uint32_t bh,
+                                        uint32_t s, uint32_t d, agpu_buffer** out) {
+  return sdpa_impl(dev, q, k, v, bh, s, d, true, out, "sdpa_causal");
+}
+
 // ----------------------------------------------------------- elementwise --
 agpu_status agpu_add(agpu_device* d, const agpu_buffer* a, const agpu_buffer* b, agpu_buffer** o) {
   return binary(d, a, b, o, Binary::Add, "add");
@@ -397,6 +432,13 @@ agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float
     return fail(AGPU_ERR_SHAPE, "launch_group_norm: channels must be divisible by groups");
   return launch_group_norm(dev, x, gamma, beta, y, batch, channels, spatial, groups, eps,
                            apply_swish != 0, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k, const float* v,
+                             float* out, uint32_t bh, uint32_t s, uint32_t d, int causal,
+                             void* stream) {
+  CHECK_DEV(dev, "launch_sdpa");
+  return launch_attention(dev, q, k, v, out, bh, s, d, causal != 0, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,

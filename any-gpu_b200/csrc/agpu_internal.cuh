@@ -92,6 +92,10 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
                               uint32_t spatial, uint32_t groups, float eps, bool swish,
                               cudaStream_t s);
 
+agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
+                             float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
+                             cudaStream_t st);
+
 // conv2d geometry (NCHW); ho/wo already computed.
 struct ConvParams {
   int n, cin, h, w, cout, kh, kw, sh, sw, ph, pw, dh, dw, groups, ho, wo;

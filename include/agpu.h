@@ -180,6 +180,22 @@ AGPU_API agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer* 
                                            uint32_t batch, uint32_t channels, uint32_t spatial,
                                            uint32_t groups, float eps, agpu_buffer** out);
 
+/* ------------------------------------------------------------- sdpa ------- */
+/* GpuDevice::scaled_dot_product_attention (src/ops/attention.rs:149-169):
+ * softmax(Q K^T / sqrt(d_k)) V per head, non-causal; Q, K, V, out are
+ * [batch_heads, seq_len, d_k].  One fused kernel: no [bh, S, S] scores in HBM. */
+AGPU_API agpu_status agpu_scaled_dot_product_attention(agpu_device* dev, const agpu_buffer* q,
+                                                       const agpu_buffer* k,
+                                                       const agpu_buffer* v, uint32_t batch_heads,
+                                                       uint32_t seq_len, uint32_t d_k,
+                                                       agpu_buffer** out);
+/* Causal variant (query i attends keys j <= i).  No counterpart in the
+ * reference; the LLaMA-style layer of the benchmark configs uses it. */
+AGPU_API agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
+                                      const agpu_buffer* k, const agpu_buffer* v,
+                                      uint32_t batch_heads, uint32_t seq_len, uint32_t d_k,
+                                      agpu_buffer** out);
+
 /* --------------------------------------------------------- elementwise ---- */
 /* src/ops/elementwise.rs:188-250.  Binary ops require equal lengths. */
 AGPU_API agpu_status agpu_add(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
@@ -236,6 +252,9 @@ AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, co
                                             const float* beta, float* y, uint32_t batch,
                                             uint32_t channels, uint32_t spatial, uint32_t groups,
                                             float eps, int apply_swish, void* stream);
+AGPU_API agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k,
+                                      const float* v, float* out, uint32_t batch_heads,
+                                      uint32_t seq_len, uint32_t d_k, int causal, void* stream);
 AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
                                          uint64_t rows, uint32_t cols, void* stream);
 

@@ -7,7 +7,7 @@ import numpy as np
 GPU_OPS = {"matmul", "batch_matmul", "softmax", "add", "sub", "mul", "relu", "sigmoid", "swish",
            "tanh", "scale", "relu_backward", "sigmoid_backward", "swish_backward",
            "tanh_backward", "transpose", "group_norm", "conv2d", "conv_transpose2d",
-           "conv2d_grad_bias"}
+           "conv2d_grad_bias", "sdpa"}
 
 
 def run_oracle(orc, case) -> np.ndarray:
@@ -56,6 +56,9 @@ def run_gpu(dev, case) -> np.ndarray:
                                          a["k"]))
     if op == "softmax":
         return dev.read(dev.softmax(up(x["x"]), a["rows"], a["cols"]))
+    if op == "sdpa":
+        return dev.read(dev.scaled_dot_product_attention(up(x["q"]), up(x["k"]), up(x["v"]),
+                                                         a["bh"], a["seq"], a["dk"]))
     if op == "conv2d":
         bias = up(x["bias"]) if x["bias"] is not None else None
         return dev.read(dev.conv2d(up(x["input"]), up(x["weight"]), bias, a["batch"], a["in_c"],

@@ -310,3 +310,72 @@ def test_conv_backward_ops_parity(dev, orc):
         want = orc.conv_transpose2d(x, wt, bias, n, cin, h, w, cout, k, k, (s, s), (p, p),
                                     (op_, op_), (d, d), g)
         assert orc.rel_fro(got, want) <= 1e-5
+
+
+def _attn64(q, k, v, bh, s, d, causal=False, rows=None):
+    Q = q.reshape(bh, s, d).astype(np.float64)
+    K = k.reshape(bh, s, d).astype(np.float64)
+    V = v.reshape(bh, s, d).astype(np.float64)
+    if rows is not None:
+        Q = Q[:, rows]
+    S = Q @ K.transpose(0, 2, 1) / np.sqrt(d)
+    if causal:
+        r = np.arange(s) if rows is None else np.asarray(rows)
+        S = np.where(np.arange(s)[None, None, :] > r[None, :, None], -np.inf, S)
+    P = np.exp(S - S.max(-1, keepdims=True))
+    P /= P.sum(-1, keepdims=True)
+    return P @ V
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("bh,s,d", [(4, 256, 128), (2, 200, 64), (3, 64, 128), (2, 333, 128),
+                                    (1, 1000, 64), (5, 7, 16), (2, 65, 32)])
+def test_sdpa_parity(dev, orc, bh, s, d, causal):
+    """Tensor-core flash kernel (d 64/128) and the SIMT kernel (other d) against
+    the oracle; Q,K,V ~ N(0,1) as in the SDPA config; TF32 tolerance."""
+    r = np.random.default_rng(bh * s + d)
+    q, k, v = (r.standard_normal(bh * s * d).astype(np.float32) for _ in range(3))
+    Q, K, V = dev.upload(q), dev.upload(k), dev.upload(v)
+    fn = dev.sdpa_causal if causal else dev.scaled_dot_product_attention
+    got = dev.read(fn(Q, K, V, bh, s, d))
+    want = orc.attention(q, k, v, bh, s, d, threads=not causal, causal=causal)
+    assert orc.rel_fro(got, want) <= 1e-3
+    assert orc.rel_fro(got, _attn64(q, k, v, bh, s, d, causal).ravel()) <= 1e-3
+
+
+@pytest.mark.parametrize("prec", ["tf32x3", "ffma"])
+def test_sdpa_fp32_modes_are_exact(dev, orc, prec):
+    bh, s, d = 2, 192, 128
+    r = np.random.default_rng(5)
+    q, k, v = (r.standard_normal(bh * s * d).astype(np.float32) for _ in range(3))
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.scaled_dot_product_attention(dev.upload(q), dev.upload(k),
+                                                        dev.upload(v), bh, s, d))
+    finally:
+        dev.set_precision("tf32")
+    assert orc.rel_fro(got, orc.attention(q, k, v, bh, s, d, threads=True)) <= 1e-5
+
+
+def test_sdpa_full_config_sampled(dev, orc):
+    """SDPA config: B8 H32 S2048 D128, non-causal, Q/K/V ~ N(0,1): sampled
+    rows of several heads against float64."""
+    bh, s, d = 256, 2048, 128
+    r = np.random.default_rng(1236)
+    q, k, v = (r.standard_normal(bh * s * d, dtype=np.float32) for _ in range(3))
+    out = dev.read(dev.scaled_dot_product_attention(dev.upload(q), dev.upload(k), dev.upload(v),
+                                                    bh, s, d)).reshape(bh, s, d)
+    rows = [0, 1, 127, 128, 1000, 2047]
+    for h in (0, 77, 255):
+        sl = slice(h * s * d, (h + 1) * s * d)
+        ref = _attn64(q[sl], k[sl], v[sl], 1, s, d, rows=rows)[0]
+        assert orc.rel_fro(out[h, rows], ref) <= 1e-3
+
+
+def test_sdpa_errors(dev):
+    from any_gpu import AnyGpuError
+    a = dev.upload(np.ones(12, np.float32))
+    b = dev.upload(np.ones(10, np.float32))
+    with pytest.raises(AnyGpuError) as e:
+        dev.scaled_dot_product_attention(a, a, b, 1, 3, 4)
+    assert e.value.status == 1
