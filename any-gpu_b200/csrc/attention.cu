@@ -33,7 +33,7 @@ namespace agpu {
 
 agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
                              uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
-                             uint32_t box_outer, bool mn_major);
+                             uint32_t box_outer, bool mn_major, bool round_tf32);
 
 namespace {
 
@@ -46,6 +46,14 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Round a finite non-negative float to tf32, nearest with ties to even (the
+// tensor core would otherwise truncate P).
+__device__ __forceinline__ uint32_t round_tf32(float x) {
+  uint32_t u = __float_as_uint(x);
+  u += 0xFFFu + ((u >> 13) & 1u);
+  return u & 0xFFFFE000u;
 }
 
 template <int D>
@@ -251,8 +259,8 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = 0; i < 32; ++i) {
         const float p0 = ex2(t[i] - m_used), p1 = ex2(t[32 + i] - m_used);
         ls += p0 + p1;
-        s0[i] = __float_as_uint(p0);
-        s1[i] = __float_as_uint(p1);
+        s0[i] = round_tf32(p0);
+        s1[i] = round_tf32(p1);
       }
       l += ls;
       ptx::tmem_st32(sbase, s0);
@@ -349,9 +357,10 @@ agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, c
                              float* o, int bh, int s, cudaStream_t st) {
   using C = AttnCfg<D>;
   CUtensorMap tq, tk, tv;
-  AGPU_TRY(make_tmap_f32_3d(&tq, q, D, s, bh, (uint64_t)s * D, 32, QT, false));
-  AGPU_TRY(make_tmap_f32_3d(&tk, k, D, s, bh, (uint64_t)s * D, 32, KT, false));
-  AGPU_TRY(make_tmap_f32_3d(&tv, v, D, s, bh, (uint64_t)s * D, 32, KT, true));
+  // operands rounded to tf32 (nearest-even) by the TMA unit on load
+  AGPU_TRY(make_tmap_f32_3d(&tq, q, D, s, bh, (uint64_t)s * D, 32, QT, false, true));
+  AGPU_TRY(make_tmap_f32_3d(&tk, k, D, s, bh, (uint64_t)s * D, 32, KT, false, true));
+  AGPU_TRY(make_tmap_f32_3d(&tv, v, D, s, bh, (uint64_t)s * D, 32, KT, true, true));
   auto kern = attention_tf32_kernel<D, CAUSAL>;
   AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
   dim3 grid((unsigned)ceil_div(s, QT), (unsigned)bh);

@@ -29,7 +29,7 @@ namespace agpu {
 
 agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
                              uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
-                             uint32_t box_outer, bool mn_major);
+                             uint32_t box_outer, bool mn_major, bool round_tf32);
 
 using umma::BK;
 using umma::BM;
@@ -330,7 +330,9 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
                              (cuuint64_t)p.h * p.w * Cs * 4};
     cuuint32_t box[4] = {BK, (cuuint32_t)pol.BW, (cuuint32_t)pol.BH, 1};
     cuuint32_t es[4] = {1, 1, 1, 1};
-    CUresult r = enc(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, dims, strides, box, es,
+    // TF32 mode: the TMA unit rounds to tf32 (nearest-even); 3xTF32 needs raw fp32
+    CUresult r = enc(&ta, X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32,
+                     4, xs, dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -339,7 +341,7 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     }
   }
   st = make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
-                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, BN, false);
+                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, BN, false, !X3);
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
   auto kern = umma::umma_tf32_kernel<P, X3>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

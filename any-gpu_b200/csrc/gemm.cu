@@ -203,17 +203,22 @@ EncodeTiledFn encode_fn() {
 
 // 3-D fp32 tensor map {inner, outer, batch}.  `mn_major` selects the
 // 128-byte swizzle with 32-byte atoms that MN-major tf32 operands need;
-// otherwise the plain 128-byte swizzle.
+// otherwise the plain 128-byte swizzle.  `round_tf32` makes the TMA unit
+// round every element to tf32 (nearest, ties to even) on its way into shared
+// memory; the tensor core itself truncates fp32 operands to tf32, so rounding
+// first halves the conversion error and removes its bias.
 agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
                              uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
-                             uint32_t box_outer, bool mn_major) {
+                             uint32_t box_outer, bool mn_major, bool round_tf32) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {inner, outer, batch};
   cuuint64_t strides[2] = {inner * 4, batch_stride_elems * 4};
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+  const CUtensorMapDataType dt =
+      round_tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = fn(map, dt, 3, const_cast<float*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -231,14 +236,14 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   CUtensorMap ta, tb;
   // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
   if (!A_MN)
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false));
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, !X3));
   else
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true));
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, !X3));
   // B: MN-major stored [K,N] -> dims {N, K}; K-major stored [N,K] -> dims {K, N}.
   if (B_MN)
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true));
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, !X3));
   else
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, BN, false));
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, BN, false, !X3));
   P pol;
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, BM);
