@@ -296,6 +296,14 @@ class GpuDevice:
         _check(_lib.load().agpu_launch_batch_matmul(self._h, a_ptr, b_ptr, c_ptr, batch, m, n,
                                                     k, stream or None))
 
+    def launch_conv2d(self, x_ptr, w_ptr, bias_ptr, y_ptr, batch, in_c, in_h, in_w, out_c, kh,
+                      kw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, groups,
+                      stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_conv2d(self._h, x_ptr, w_ptr, bias_ptr or None, y_ptr,
+                                              batch, in_c, in_h, in_w, out_c, kh, kw, stride_h,
+                                              stride_w, pad_h, pad_w, dil_h, dil_w, groups,
+                                              stream or None))
+
     def launch_group_norm(self, x_ptr, g_ptr, b_ptr, y_ptr, batch, channels, spatial, groups,
                           eps, swish=False, stream: int = 0) -> None:
         _check(_lib.load().agpu_launch_group_norm(self._h, x_ptr, g_ptr, b_ptr, y_ptr, batch,

@@ -1,27 +1,34 @@
 #!/usr/bin/env python
-"""Headline benchmark: fp32 batch_matmul -> row softmax on B200.
+"""Benchmark of the B200 dense-op path (one JSON line on rank 0).
 
-Workload (one "step"): C = batch_matmul(A, B) with batch 64, M = K = N = 2048,
-A, B ~ N(0,1) * 0.05 (seeded), then S = softmax(C) over the last dim
-(131072 rows x 2048).  The GEMM runs on tcgen05 tensor cores in TF32 with fp32
-accumulate; softmax is the one-read-one-write warp-per-row kernel.
+Default workload (the headline): fp32 batch_matmul -> row softmax.
+  One step = C = batch_matmul(A, B), batch 64, M = K = N = 2048, A, B ~ N(0,1)*0.05
+  (seeded), then S = softmax(C) over the last dim (131072 rows x 2048).  The GEMM
+  runs on tcgen05 tensor cores in TF32 (operands rounded to nearest by TMA) with
+  fp32 accumulation; softmax is the one-read-one-write warp-per-row kernel.
+
+Other workloads (`--workload`), each one of the benchmark configurations:
+  matmul   square fp32 matmul, A, B ~ U[-1,1)  (--size, default 512; sweep 64..8192)
+  sdpa     scaled_dot_product_attention, B8 H32 S2048 D128, non-causal, N(0,1)
+  unet     conv2d 3x3 s1 p1 (N16, 320->320, 64x64, Kaiming-uniform W, bias 0)
+           -> group_norm (32 groups, eps 1e-5, gamma 1, beta 0) -> swish
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl agpu|reference]
+                    [--workload bmm_softmax|matmul|sdpa|unet]
 
-One process per GPU (torchrun for N > 1).  Every rank runs the full workload
-on its own GPU ("scaling": "weak"; batches are independent, no data-path
-collective); `--gather` adds an NCCL all-gather of the softmax outputs.
-Rank 0 prints one JSON line.
+One process per GPU (torchrun for N > 1).  Every rank runs the full workload on
+its own GPU ("scaling": "weak": batches/heads/images are independent, no
+data-path collective); `--gather` adds an NCCL all-gather of the outputs.
 
-  value  : whole-job TFLOPS = N * 2*B*M*N*K / (max over ranks of the device
-           time per step), inputs resident in HBM, CUDA events on the
-           launching stream.  Inputs (2 GiB) + output (1 GiB) exceed the
-           126 MB L2, so no flush is needed between steps.
-  e2e    : the same FLOPs over the wall time of the public API call sequence
-           upload(A), upload(B) from pinned host memory -> batch_matmul ->
-           softmax -> read(S) into pinned host memory, max over ranks.
-  roofline: the GEMM kernel's achieved TFLOP/s (CUDA events around each GEMM
-           launch) against the TF32 dense peak = half the measured bf16 peak.
+  value    whole-job TFLOPS = N * FLOPs per step / (max over ranks of the device
+           time per step); inputs resident in HBM; CUDA events on the launching
+           stream.  Working sets exceed the 126 MB L2 (stated in `config.l2`);
+           the small matmul sizes say so and re-read their inputs from L2.
+  e2e      the same FLOPs over the wall time of the public API call sequence
+           with host buffers (upload from pinned memory -> op(s) -> read into
+           pinned memory), max over ranks.
+  roofline the dominant kernel's FLOP/s (CUDA events around each launch) against
+           the TF32 dense peak = half the measured bf16 peak.
 """
 from __future__ import annotations
 
@@ -42,22 +49,17 @@ sys.path.insert(0, str(ROOT / "any-gpu_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "TFLOPS (matmul, SDPA) and GB/s (softmax/norm) at 1/2/4/8 B200, % of roofline"
-BATCH, M, N, K = 64, 2048, 2048, 2048
-GEMM_FLOPS = 2.0 * BATCH * M * N * K
-SOFTMAX_BYTES = 2.0 * BATCH * M * N * 4  # one read + one write of C
-SEED = 1235  # 1234 + config index
 
-# dram bytes per GEMM launch from an ncu capture (profiles/gemm_tf32_*.md);
-# None until captured for the current kernel.
-GEMM_TRAFFIC_BYTES = None
+# DRAM bytes per launch of the dominant kernel from an ncu capture (see
+# profiles/), or None when not captured for the current kernel and workload.
+TRAFFIC_BYTES = {"bmm_softmax": 3.5e9}
 
 
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
-                "source": "measured"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
@@ -79,7 +81,6 @@ class ClockSampler(threading.Thread):
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
-            h = None
             try:
                 import torch
                 p = torch.cuda.get_device_properties(cuda_index)
@@ -117,83 +118,380 @@ class ClockSampler(threading.Thread):
                 "samples": len(self.samples)}
 
 
-# ------------------------------------------------------------ helpers ----
 def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
-def make_inputs(rank: int):
-    r = np.random.default_rng(SEED + 1000 * rank)
-    a = r.standard_normal(BATCH * M * K, dtype=np.float32)
-    a *= np.float32(0.05)
-    b = r.standard_normal(BATCH * K * N, dtype=np.float32)
-    b *= np.float32(0.05)
-    return a, b
+def _normal(r, n, scale=1.0):
+    x = r.standard_normal(n, dtype=np.float32)
+    if scale != 1.0:
+        x *= np.float32(scale)
+    return x
 
 
-def cpu_sample(orc, threads: bool, target_s: float):
-    """Time the oracle (reference CPU path) on a bounded sample of the step:
-    rows of batch item 0 (batch_matmul rows then their softmax).  Grows the
-    row count until about `target_s` seconds of work; returns TFLOPS."""
-    r = np.random.default_rng(SEED)
-    a = (r.standard_normal(M * K, dtype=np.float32) * np.float32(0.05))
-    b = (r.standard_normal(K * N, dtype=np.float32) * np.float32(0.05))
-    chunk = max(16, 2 * orc.num_threads())
-    done, t_total, start = 0, 0.0, 0
-    while t_total < target_s:
-        rows = min(chunk, M - start)
-        t0 = time.perf_counter()
-        c = orc.matmul(a[start * K:(start + rows) * K], b, rows, N, K, threads=threads)
-        orc.softmax(c, rows, N, threads=threads)
-        t_total += time.perf_counter() - t0
-        done += rows
-        start = (start + rows) % M
-    return 2.0 * done * N * K / t_total / 1e12, done, t_total
+# ----------------------------------------------------------- workloads ---
+class Workload:
+    """One benchmark configuration.  Subclasses define the data, the device
+    step (launch layer on a given stream) and the public-API e2e step."""
+    name = ""
+    dtype = "tf32"
+    l2 = ""
+    flops = 0.0       # FLOPs of one step
+    dom_flops = 0.0   # FLOPs of one launch of the dominant kernel
+    dom_kernel = ""
+
+    def __init__(self, args, rank):
+        self.args, self.rank = args, rank
+
+    def config(self) -> dict:
+        raise NotImplementedError
+
+    def host_inputs(self) -> dict:
+        raise NotImplementedError
+
+    def out_elems(self) -> int:
+        raise NotImplementedError
+
+    def setup(self, torch, local):
+        """Pinned host copies + device tensors."""
+        self.host = {k: torch.from_numpy(v).pin_memory() for k, v in self.host_inputs().items()}
+        self.dev_in = {k: v.to(f"cuda:{local}") for k, v in self.host.items()}
+        self.out_host = torch.empty(self.out_elems(), dtype=torch.float32).pin_memory()
+
+    def step(self, dev, sptr, ev=None):
+        raise NotImplementedError
+
+    def output(self):
+        raise NotImplementedError
+
+    def e2e_step(self, dev):
+        raise NotImplementedError
+
+    def e2e_bytes(self):
+        h2d = sum(v.numel() * 4 for v in self.host.values())
+        return h2d, self.out_elems() * 4
+
+    def cpu_sample(self, orc, target_s):
+        raise NotImplementedError
+
+    def extra(self, ms_step, ms_dom, peaks) -> dict:
+        return {}
+
+
+class BmmSoftmax(Workload):
+    name = "bmm_softmax"
+    l2 = "inputs 2 GiB + output 1 GiB > 126 MB L2 (no flush needed)"
+
+    def __init__(self, args, rank):
+        super().__init__(args, rank)
+        self.B, self.M, self.N, self.K = args.batch, 2048, 2048, 2048
+        self.flops = self.dom_flops = 2.0 * self.B * self.M * self.N * self.K
+        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256, K-major A, MN-major B>>"
+
+    def config(self):
+        return {"workload": "batch_matmul+softmax", "batch": self.B, "m": self.M, "n": self.N,
+                "k": self.K, "inputs": "N(0,1)*0.05 seeded", "softmax_rows": self.B * self.M,
+                "softmax_cols": self.N}
+
+    def host_inputs(self):
+        r = np.random.default_rng(1235 + 1000 * self.rank)
+        return {"a": _normal(r, self.B * self.M * self.K, 0.05),
+                "b": _normal(r, self.B * self.K * self.N, 0.05)}
+
+    def out_elems(self):
+        return self.B * self.M * self.N
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        self.C = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
+        self.S = torch.empty_like(self.C)
+
+    def step(self, dev, sptr, ev=None):
+        if ev is not None:
+            ev[0].record()
+        dev.launch_batch_matmul(self.dev_in["a"].data_ptr(), self.dev_in["b"].data_ptr(),
+                                self.C.data_ptr(), self.B, self.M, self.N, self.K, sptr)
+        if ev is not None:
+            ev[1].record()
+        dev.launch_softmax(self.C.data_ptr(), self.S.data_ptr(), self.B * self.M, self.N, sptr)
+
+    def output(self):
+        return self.S
+
+    def e2e_step(self, dev):
+        ga, gb = dev.upload(self.host["a"].numpy()), dev.upload(self.host["b"].numpy())
+        gc = dev.batch_matmul(ga, gb, self.B, self.M, self.N, self.K)
+        gs = dev.softmax(gc, self.B * self.M, self.N)
+        dev.read(gs, out=self.out_host.numpy())
+        for b in (ga, gb, gc, gs):
+            b.free()
+
+    def cpu_sample(self, orc, target_s):
+        r = np.random.default_rng(1235)
+        a = _normal(r, self.M * self.K, 0.05)
+        b = _normal(r, self.K * self.N, 0.05)
+        chunk, done, t, start = max(16, 2 * orc.num_threads()), 0, 0.0, 0
+        while t < target_s:
+            rows = min(chunk, self.M - start)
+            t0 = time.perf_counter()
+            c = orc.matmul(a[start * self.K:(start + rows) * self.K], b, rows, self.N, self.K,
+                           threads=True)
+            orc.softmax(c, rows, self.N, threads=True)
+            t += time.perf_counter() - t0
+            done += rows
+            start = (start + rows) % self.M
+        v = 2.0 * done * self.N * self.K / t / 1e12
+        return v, (f"{done} rows of batch item 0 (each: a 1x{self.K} by {self.K}x{self.N} "
+                   f"matmul row + its softmax), {t:.1f} s, extrapolated by FLOPs")
+
+    def extra(self, ms_step, ms_dom, peaks):
+        sm_ms = ms_step - ms_dom
+        nbytes = 2.0 * self.B * self.M * self.N * 4
+        return {"softmax": {"ms": sm_ms, "gbs": nbytes / (sm_ms * 1e-3) / 1e9,
+                            "frac_hbm": nbytes / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                            "note": "step time minus GEMM time"}}
+
+
+class Matmul(Workload):
+    name = "matmul"
+
+    def __init__(self, args, rank):
+        super().__init__(args, rank)
+        self.n = args.size
+        self.flops = self.dom_flops = 2.0 * self.n ** 3
+        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256|128, K-major A, MN-major B>>"
+        ws = 3 * self.n * self.n * 4
+        self.l2 = (f"working set {ws / 2**20:.1f} MiB "
+                   + ("> 126 MB L2" if ws > 126e6 else "fits in L2: inputs re-read from L2"))
+
+    def config(self):
+        return {"workload": "matmul", "m": self.n, "n": self.n, "k": self.n,
+                "inputs": "U[-1,1) seeded"}
+
+    def host_inputs(self):
+        r = np.random.default_rng(1234 + 1000 * self.rank)
+        return {"a": r.uniform(-1, 1, self.n * self.n).astype(np.float32),
+                "b": r.uniform(-1, 1, self.n * self.n).astype(np.float32)}
+
+    def out_elems(self):
+        return self.n * self.n
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        self.C = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
+
+    def step(self, dev, sptr, ev=None):
+        if ev is not None:
+            ev[0].record()
+        dev.launch_batch_matmul(self.dev_in["a"].data_ptr(), self.dev_in["b"].data_ptr(),
+                                self.C.data_ptr(), 1, self.n, self.n, self.n, sptr)
+        if ev is not None:
+            ev[1].record()
+
+    def output(self):
+        return self.C
+
+    def e2e_step(self, dev):
+        ga, gb = dev.upload(self.host["a"].numpy()), dev.upload(self.host["b"].numpy())
+        gc = dev.matmul(ga, gb, self.n, self.n, self.n)
+        dev.read(gc, out=self.out_host.numpy())
+        for b in (ga, gb, gc):
+            b.free()
+
+    def cpu_sample(self, orc, target_s):
+        a, b = self.host_inputs().values()
+        n = self.n
+        chunk, done, t, start = max(8, orc.num_threads()), 0, 0.0, 0
+        while t < target_s:
+            rows = min(chunk, n - start)
+            t0 = time.perf_counter()
+            orc.matmul(a[start * n:(start + rows) * n], b, rows, n, n, threads=True)
+            t += time.perf_counter() - t0
+            done += rows
+            start = (start + rows) % n
+        return 2.0 * done * n * n / t / 1e12, (f"{done} rows of the {n}^3 product "
+                                               f"(cpu_matmul), {t:.1f} s")
+
+
+class Sdpa(Workload):
+    name = "sdpa"
+    l2 = "Q, K, V, O 1 GiB > 126 MB L2"
+
+    def __init__(self, args, rank):
+        super().__init__(args, rank)
+        self.bh, self.s, self.d = args.bh, args.seq, 128
+        self.flops = self.dom_flops = 4.0 * self.bh * self.s * self.s * self.d
+        self.dom_kernel = "attention_tf32_kernel<128, non-causal>"
+
+    def config(self):
+        return {"workload": "scaled_dot_product_attention", "batch_heads": self.bh,
+                "seq_len": self.s, "d_k": self.d, "causal": False, "inputs": "N(0,1) seeded",
+                "flops": "4*BH*S^2*D (QK^T + PV)"}
+
+    def host_inputs(self):
+        r = np.random.default_rng(1236 + 1000 * self.rank)
+        n = self.bh * self.s * self.d
+        return {"q": _normal(r, n), "k": _normal(r, n), "v": _normal(r, n)}
+
+    def out_elems(self):
+        return self.bh * self.s * self.d
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        self.O = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
+
+    def step(self, dev, sptr, ev=None):
+        if ev is not None:
+            ev[0].record()
+        dev.launch_sdpa(self.dev_in["q"].data_ptr(), self.dev_in["k"].data_ptr(),
+                        self.dev_in["v"].data_ptr(), self.O.data_ptr(), self.bh, self.s, self.d,
+                        False, sptr)
+        if ev is not None:
+            ev[1].record()
+
+    def output(self):
+        return self.O
+
+    def e2e_step(self, dev):
+        g = [dev.upload(self.host[n].numpy()) for n in "qkv"]
+        go = dev.scaled_dot_product_attention(*g, self.bh, self.s, self.d)
+        dev.read(go, out=self.out_host.numpy())
+        for b in g + [go]:
+            b.free()
+
+    def cpu_sample(self, orc, target_s):
+        r = np.random.default_rng(1236)
+        hsz = self.s * self.d
+        heads = max(1, orc.num_threads())
+        q, k, v = (_normal(r, heads * hsz) for _ in range(3))
+        done, t = 0, 0.0
+        while t < target_s:
+            t0 = time.perf_counter()
+            orc.attention(q, k, v, heads, self.s, self.d, threads=True)
+            t += time.perf_counter() - t0
+            done += heads
+        return (4.0 * done * self.s * self.s * self.d / t / 1e12,
+                f"{done} heads of S={self.s}, D={self.d} (cpu_attention per head), {t:.1f} s")
+
+
+class Unet(Workload):
+    name = "unet"
+    l2 = "x 80 MiB + conv out 80 MiB + y 80 MiB > 126 MB L2"
+
+    def __init__(self, args, rank):
+        super().__init__(args, rank)
+        self.n, self.c, self.h, self.w, self.g = args.images, 320, 64, 64, 32
+        self.flops = self.dom_flops = 2.0 * self.n * self.c * self.h * self.w * self.c * 9
+        self.dom_kernel = "umma_tf32_kernel<ConvPolicy<160>> (implicit-GEMM conv2d)"
+
+    def config(self):
+        return {"workload": "unet_block conv2d3x3->group_norm->swish", "n": self.n,
+                "cin": self.c, "cout": self.c, "h": self.h, "w": self.w, "groups": self.g,
+                "eps": 1e-5, "inputs": "x N(0,1); W Kaiming-uniform U(+-sqrt(6/2880)); bias 0",
+                "flops": "conv only: 2*N*Cout*H*W*Cin*9"}
+
+    def host_inputs(self):
+        r = np.random.default_rng(1237 + 1000 * self.rank)
+        bound = np.float32(np.sqrt(6.0 / (self.c * 9)))
+        return {"x": _normal(r, self.n * self.c * self.h * self.w),
+                "w": r.uniform(-bound, bound, self.c * self.c * 9).astype(np.float32),
+                "gamma": np.ones(self.c, np.float32), "beta": np.zeros(self.c, np.float32)}
+
+    def out_elems(self):
+        return self.n * self.c * self.h * self.w
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        self.Y1 = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
+        self.Y = torch.empty_like(self.Y1)
+
+    def step(self, dev, sptr, ev=None):
+        d = self.dev_in
+        if ev is not None:
+            ev[0].record()
+        dev.launch_conv2d(d["x"].data_ptr(), d["w"].data_ptr(), 0, self.Y1.data_ptr(), self.n,
+                          self.c, self.h, self.w, self.c, 3, 3, 1, 1, 1, 1, 1, 1, 1, sptr)
+        if ev is not None:
+            ev[1].record()
+        dev.launch_group_norm(self.Y1.data_ptr(), d["gamma"].data_ptr(), d["beta"].data_ptr(),
+                              self.Y.data_ptr(), self.n, self.c, self.h * self.w, self.g, 1e-5,
+                              True, sptr)
+
+    def output(self):
+        return self.Y
+
+    def e2e_step(self, dev):
+        g = {k: dev.upload(v.numpy()) for k, v in self.host.items()}
+        y1 = dev.conv2d(g["x"], g["w"], None, self.n, self.c, self.h, self.w, self.c, 3, 3,
+                        (1, 1), (1, 1), (1, 1), 1)
+        y = dev.group_norm_swish(y1, g["gamma"], g["beta"], self.n, self.c, self.h * self.w,
+                                 self.g, 1e-5)
+        dev.read(y, out=self.out_host.numpy())
+        for b in list(g.values()) + [y1, y]:
+            b.free()
+
+    def cpu_sample(self, orc, target_s):
+        x, w, gamma, beta = self.host_inputs().values()
+        img = self.c * self.h * self.w
+        done, t = 0, 0.0
+        while t < target_s:
+            t0 = time.perf_counter()
+            y = orc.conv2d(x[:img], w, None, 1, self.c, self.h, self.w, self.c, 3, 3, (1, 1),
+                           (1, 1), (1, 1), 1, threads=True)
+            y = orc.group_norm(y, gamma, beta, 1, self.c, self.h * self.w, self.g, 1e-5,
+                               threads=True)
+            orc.elementwise("swish", y)
+            t += time.perf_counter() - t0
+            done += 1
+        return (2.0 * done * img * self.c * 9 / t / 1e12,
+                f"{done} image(s) of the block (cpu_conv2d + cpu_group_norm + swish), {t:.1f} s")
+
+    def extra(self, ms_step, ms_dom, peaks):
+        gn_ms = ms_step - ms_dom
+        nbytes = 2.0 * self.out_elems() * 4
+        return {"group_norm_swish": {"ms": gn_ms, "gbs": nbytes / (gn_ms * 1e-3) / 1e9,
+                                     "frac_hbm": nbytes / (gn_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                     "note": "step time minus conv time"}}
+
+
+WORKLOADS = {"bmm_softmax": BmmSoftmax, "matmul": Matmul, "sdpa": Sdpa, "unet": Unet}
 
 
 # -------------------------------------------------------------- arms -----
+def base_line(args, world, wl):
+    cfg = wl.config()
+    cfg.update({"parallelism": f"replicas{world}" if world > 1 else "single", "l2": wl.l2,
+                "precision": "tf32 multiply (operands rounded to nearest), fp32 accumulate, "
+                             "fp32 I/O", "gather": bool(args.gather)})
+    return {"metric": METRIC, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic", "config": cfg}
+
+
 def run_reference(args, world, rank):
-    """Reference arm: the reference's CPU path (the oracle restatement; the
-    Rust/wgpu crate cannot be built or run here) on the host cores."""
+    """Reference arm: the reference's own CPU path (the oracle restatement of its
+    CPU functions; the Rust/wgpu crate cannot be built or run here) on all host
+    cores; rank 0 only."""
     if rank != 0:
         return
     from oracle import oracle as orc
     orc.build()
-    cores = orc.num_threads()
-    per = []
-    rows_done = 0
+    wl = WORKLOADS[args.workload](args, 0)
+    vals, sample = [], ""
     for i in range(args.warmup + args.steps):
-        v, rows, _ = cpu_sample(orc, threads=True, target_s=args.ref_seconds)
+        v, sample = wl.cpu_sample(orc, args.ref_seconds)
         if i >= args.warmup:
-            per.append(v)
-            rows_done = rows
-    value = statistics.median(per)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": GEMM_FLOPS / (value * 1e12) * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_dict(args, world),
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": "port",
-                         "sample": f"{rows_done} rows of batch item 0 per step (each: a "
-                                   f"1x{K} by {K}x{N} matmul row + its softmax), "
-                                   "extrapolated by FLOPs"},
-        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
+            vals.append(v)
+    value = statistics.median(vals)
+    line = base_line(args, world, wl)
+    line.update({"impl": "reference", "value": value, "dtype": "f32",
+                 "ms_per_step": wl.flops / (value * 1e12) * 1e3,
+                 "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": orc.num_threads(),
+                                  "kind": "port", "sample": sample + " per step"},
+                 "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}})
     print(json.dumps(line), flush=True)
-
-
-def config_dict(args, world):
-    return {"workload": "batch_matmul+softmax", "batch": BATCH, "m": M, "n": N, "k": K,
-            "inputs": "N(0,1)*0.05 seeded", "softmax_rows": BATCH * M, "softmax_cols": N,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
-            "l2": "inputs 2 GiB + output 1 GiB > 126 MB L2 (no flush needed)",
-            "precision": "tf32 multiply, fp32 accumulate, fp32 I/O",
-            "gather": bool(args.gather)}
 
 
 def run_agpu(args, world, rank, local):
@@ -208,18 +506,8 @@ def run_agpu(args, world, rank, local):
     peaks = load_peaks()
     tf32_peak = peaks["bf16_tflops"] / 2.0
     dev = GpuDevice.gpu(local)
-
-    a_np, b_np = make_inputs(rank)
-    a_host = torch.from_numpy(a_np).pin_memory()
-    b_host = torch.from_numpy(b_np).pin_memory()
-    s_host = torch.empty(BATCH * M * N, dtype=torch.float32).pin_memory()
-    del a_np, b_np
-    A = a_host.to(f"cuda:{local}", non_blocking=False)
-    B = b_host.to(f"cuda:{local}", non_blocking=False)
-    C = torch.empty(BATCH * M * N, dtype=torch.float32, device=f"cuda:{local}")
-    S = torch.empty_like(C)
-    gathered = (torch.empty(world * BATCH * M * N, dtype=torch.float32,
-                            device=f"cuda:{local}") if (args.gather and world > 1) else None)
+    wl = WORKLOADS[args.workload](args, rank)
+    wl.setup(torch, local)
     # A dedicated stream: the library launches on it and the CUDA events are
     # recorded on it (handle 0, torch's legacy default stream, would mean
     # "the library's own stream" at the C ABI).
@@ -227,17 +515,16 @@ def run_agpu(args, world, rank, local):
     torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     assert sptr != 0
+    gathered = None
+    if args.gather and world > 1:
+        gathered = torch.empty(world * wl.out_elems(), dtype=torch.float32,
+                               device=f"cuda:{local}")
 
     def step(ev=None):
-        if ev is not None:
-            ev[0].record(stream)
-        dev.launch_batch_matmul(A.data_ptr(), B.data_ptr(), C.data_ptr(), BATCH, M, N, K, sptr)
-        if ev is not None:
-            ev[1].record(stream)
-        dev.launch_softmax(C.data_ptr(), S.data_ptr(), BATCH * M, N, sptr)
+        wl.step(dev, sptr, ev)
         if gathered is not None:
             import torch.distributed as dist
-            dist.all_gather_into_tensor(gathered, S)
+            dist.all_gather_into_tensor(gathered, wl.output())
 
     def barrier():
         if world > 1:
@@ -256,80 +543,62 @@ def run_agpu(args, world, rank, local):
     clocks = ClockSampler(local)
     clocks.start()
     launches0 = dev.launch_count
-    t_start.record(stream)
+    t_start.record()
     for i in range(args.steps):
         step(evs[i])
-    t_end.record(stream)
+    t_end.record()
     torch.cuda.synchronize()
     launches = dev.launch_count - launches0
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()
     total_ms = t_start.elapsed_time(t_end)
-    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
 
-    # ---------------------------------------------------------- e2e ----
-    # public API: upload (H2D from pinned memory), batch_matmul, softmax,
-    # read (D2H into pinned memory); wall clock includes every copy.
-    a_view, b_view, s_view = a_host.numpy(), b_host.numpy(), s_host.numpy()
+    # e2e through the public API with host buffers (pinned), every copy timed
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
-
-    def e2e_step():
-        ga, gb = dev.upload(a_view), dev.upload(b_view)
-        gc = dev.batch_matmul(ga, gb, BATCH, M, N, K)
-        gs = dev.softmax(gc, BATCH * M, N)
-        dev.read(gs, out=s_view)
-        for buf in (ga, gb, gc, gs):
-            buf.free()
-
-    e2e_step()
+    wl.e2e_step(dev)
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        e2e_step()
+        wl.e2e_step(dev)
     e2e_s = (time.perf_counter() - t0) / e2e_steps
 
-    # ------------------------------------------------ max over ranks ----
-    vals = torch.tensor([total_ms, e2e_s, gemm_ms], dtype=torch.float64, device=f"cuda:{local}")
+    vals = torch.tensor([total_ms, e2e_s, dom_ms], dtype=torch.float64, device=f"cuda:{local}")
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, e2e_s, gemm_ms = vals.tolist()
+    total_ms, e2e_s, dom_ms = vals.tolist()
     ms_per_step = total_ms / args.steps
-    value = world * GEMM_FLOPS / (ms_per_step * 1e-3) / 1e12
-    sm_ms = ms_per_step - gemm_ms
 
     if rank == 0:
-        achieved = GEMM_FLOPS / (gemm_ms * 1e-3) / 1e12
-        line = {
-            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
-            "data": "synthetic", "config": config_dict(args, world),
-            "e2e": {"value": world * GEMM_FLOPS / e2e_s / 1e12, "unit": "TFLOPS",
-                    "h2d_bytes_per_step": 2 * BATCH * M * K * 4,
-                    "d2h_bytes_per_step": BATCH * M * N * 4,
+        achieved = wl.dom_flops / (dom_ms * 1e-3) / 1e12
+        h2d, d2h = wl.e2e_bytes()
+        traffic = TRAFFIC_BYTES.get(wl.name)
+        if wl.name == "bmm_softmax" and args.batch != 64:
+            traffic = None
+        line = base_line(args, world, wl)
+        line.update({
+            "value": world * wl.flops / (ms_per_step * 1e-3) / 1e12,
+            "ms_per_step": ms_per_step,
+            "e2e": {"value": world * wl.flops / e2e_s / 1e12, "unit": "TFLOPS",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "s_per_step": e2e_s, "steps": e2e_steps},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak,
-                         "unit": "TFLOP/s", "frac": achieved / tf32_peak,
-                         "traffic": GEMM_TRAFFIC_BYTES,
-                         "kernel": "gemm_tf32_kernel<256,K-major A,MN-major B>",
+                         "unit": "TFLOP/s", "frac": achieved / tf32_peak, "traffic": traffic,
+                         "kernel": wl.dom_kernel,
                          "peak_note": f"TF32 dense = bf16 {peaks['source']} "
                                       f"{peaks['bf16_tflops']} / 2",
-                         "ms_per_launch": gemm_ms},
-            "softmax": {"ms": sm_ms, "gbs": SOFTMAX_BYTES / (sm_ms * 1e-3) / 1e9,
-                        "frac_hbm": SOFTMAX_BYTES / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                        "note": "step time minus GEMM time"},
+                         "ms_per_launch": dom_ms},
             "clocks": clk, "gpu_launches": launches,
-        }
+        })
+        line.update(wl.extra(ms_per_step, dom_ms, peaks))
         if world == 1 and not args.no_cpu_baseline:
             from oracle import oracle as orc
             orc.build()
-            v, rows, secs = cpu_sample(orc, threads=True, target_s=args.cpu_seconds)
-            line["cpu_baseline"] = {
-                "value": v, "unit": "TFLOPS", "cores": orc.num_threads(), "kind": "port",
-                "sample": f"{rows} rows of batch item 0 (each: a 1x{K} by {K}x{N} matmul row + "
-                          f"its softmax), {secs:.1f} s, extrapolated by FLOPs"}
+            v, sample = wl.cpu_sample(orc, args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "TFLOPS", "cores": orc.num_threads(),
+                                    "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -343,20 +612,21 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["agpu", "reference"], default="agpu")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bmm_softmax")
     ap.add_argument("--gather", action="store_true",
-                    help="NCCL all-gather of the softmax outputs inside each step")
+                    help="NCCL all-gather of the outputs inside each step")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64,
-                    help="batch count (64 = the headline workload; smaller only for "
-                         "profiler captures)")
+                    help="bmm_softmax batch count (64 = the headline workload; smaller only "
+                         "for profiler captures)")
+    ap.add_argument("--size", type=int, default=512, help="matmul M = N = K")
+    ap.add_argument("--bh", type=int, default=256, help="sdpa batch*heads (B8 x H32)")
+    ap.add_argument("--seq", type=int, default=2048, help="sdpa sequence length")
+    ap.add_argument("--images", type=int, default=16, help="unet batch N")
     args = ap.parse_args()
-    global BATCH, GEMM_FLOPS, SOFTMAX_BYTES
-    BATCH = args.batch
-    GEMM_FLOPS = 2.0 * BATCH * M * N * K
-    SOFTMAX_BYTES = 2.0 * BATCH * M * N * 4
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
