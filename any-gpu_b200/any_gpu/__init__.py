@@ -190,6 +190,14 @@ class GpuDevice:
         return self._new(_lib.load().agpu_gemm, a.handle, b.handle, batch, m, n, k,
                          int(trans_a), int(trans_b))
 
+    def gemm_ex(self, a, b, batch: int, m: int, n: int, k: int, bias=None, resid=None,
+                act: int = 0, trans_a: bool = False, trans_b: bool = False) -> GpuBuffer:
+        """C = act(op(A) op(B) + bias[col] + resid); act 0 none, 1 swish, 2 relu."""
+        return self._new(_lib.load().agpu_gemm_ex, a.handle, b.handle,
+                         bias.handle if bias is not None else None,
+                         resid.handle if resid is not None else None, batch, m, n, k,
+                         int(trans_a), int(trans_b), int(act))
+
     def softmax(self, x: GpuBuffer, rows: int, cols: int) -> GpuBuffer:
         """Reference: `softmax(input, rows, cols)` (src/ops/attention.rs:91)."""
         return self._new(_lib.load().agpu_softmax, x.handle, rows, cols)
@@ -256,6 +264,49 @@ class GpuDevice:
                     stream: int = 0) -> None:
         _check(_lib.load().agpu_launch_sdpa(self._h, q_ptr, k_ptr, v_ptr, o_ptr, bh, s, d,
                                             int(causal), stream or None))
+
+    # ----------------------------------------------------- LLaMA-layer ops --
+    def rmsnorm(self, x, w, rows: int, cols: int, eps: float) -> GpuBuffer:
+        return self._new(_lib.load().agpu_rmsnorm, x.handle, w.handle, rows, cols,
+                         C.c_float(eps))
+
+    def rope(self, x, batch: int, seq: int, heads: int, dim: int,
+             base: float = 10000.0) -> GpuBuffer:
+        return self._new(_lib.load().agpu_rope, x.handle, batch, seq, heads, dim,
+                         C.c_float(base))
+
+    def swish_mul(self, gate, up) -> GpuBuffer:
+        return self._new(_lib.load().agpu_swish_mul, gate.handle, up.handle)
+
+    def launch_gemm_ex(self, a_ptr, b_ptr, c_ptr, batch, m, n, k, trans_a=False,
+                       trans_b=False, bias_ptr=0, resid_ptr=0, act=0, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_gemm_ex(self._h, a_ptr, b_ptr, c_ptr, batch, m, n, k,
+                                               int(trans_a), int(trans_b), bias_ptr or None,
+                                               resid_ptr or None, int(act), stream or None))
+
+    def launch_sdpa_strided(self, q_ptr, k_ptr, v_ptr, o_ptr, batch, heads, seq, d, q_strides,
+                            k_strides, v_strides, o_strides, causal=False,
+                            stream: int = 0) -> None:
+        """*_strides = (seq_stride, head_stride, batch_stride) in elements."""
+        lay = [_lib.AttnLayout(*map(int, st)) for st in (q_strides, k_strides, v_strides,
+                                                          o_strides)]
+        _check(_lib.load().agpu_launch_sdpa_strided(self._h, q_ptr, k_ptr, v_ptr, o_ptr, batch,
+                                                    heads, seq, d, *[C.byref(x) for x in lay],
+                                                    int(causal), stream or None))
+
+    def launch_rmsnorm(self, x_ptr, w_ptr, y_ptr, rows, cols, eps, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_rmsnorm(self._h, x_ptr, w_ptr, y_ptr, rows, cols,
+                                               C.c_float(eps), stream or None))
+
+    def launch_rope(self, x_ptr, y_ptr, batch, seq, heads, dim, row_stride, base=10000.0,
+                    stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_rope(self._h, x_ptr, y_ptr, batch, seq, heads, dim,
+                                            row_stride, C.c_float(base), stream or None))
+
+    def launch_swish_mul(self, g_ptr, u_ptr, o_ptr, rows, cols, g_stride, u_stride, o_stride,
+                         stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_swish_mul(self._h, g_ptr, u_ptr, o_ptr, rows, cols,
+                                                 g_stride, u_stride, o_stride, stream or None))
 
     # --------------------------------------------------------- elementwise --
     def add(self, a, b): return self._new(_lib.load().agpu_add, a.handle, b.handle)

@@ -42,6 +42,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, P_buf]),
     "agpu_batch_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, P_buf]),
     "agpu_gemm": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, i32, i32, P_buf]),
+    "agpu_gemm_ex": (c_status, [c_dev, c_buf, c_buf, c_buf, c_buf, u32, u32, u32, u32, i32, i32,
+                                i32, P_buf]),
     "agpu_softmax": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
     "agpu_conv2d": (c_status, [c_dev, c_buf, c_buf, c_buf] + [u32] * 14 + [P_buf]),
     "agpu_conv_transpose2d": (c_status, [c_dev, c_buf, c_buf, c_buf] + [u32] * 16 + [P_buf]),
@@ -54,6 +56,9 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_scaled_dot_product_attention": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32,
                                                      P_buf]),
     "agpu_sdpa_causal": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, P_buf]),
+    "agpu_rmsnorm": (c_status, [c_dev, c_buf, c_buf, u32, u32, f32, P_buf]),
+    "agpu_rope": (c_status, [c_dev, c_buf, u32, u32, u32, u32, f32, P_buf]),
+    "agpu_swish_mul": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_add": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_sub": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_mul": (c_status, [c_dev, c_buf, c_buf, P_buf]),
@@ -78,10 +83,24 @@ SIGNATURES: dict[str, tuple] = {
                                           C.c_void_p]),
     "agpu_launch_sdpa": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32, u32, u32, i32,
                                                                  C.c_void_p]),
+    "agpu_launch_gemm_ex": (c_status, [c_dev] + [C.c_void_p] * 3 + [u32] * 4 + [i32, i32]
+                            + [C.c_void_p] * 2 + [i32, C.c_void_p]),
+    "agpu_launch_sdpa_strided": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 4
+                                 + [C.c_void_p] * 4 + [i32, C.c_void_p]),
+    "agpu_launch_rmsnorm": (c_status, [c_dev] + [C.c_void_p] * 3 + [u64, u32, f32, C.c_void_p]),
+    "agpu_launch_rope": (c_status, [c_dev, C.c_void_p, C.c_void_p, u32, u32, u32, u32, u64, f32,
+                                    C.c_void_p]),
+    "agpu_launch_swish_mul": (c_status, [c_dev] + [C.c_void_p] * 3 + [u64, u32, u64, u64, u64,
+                                                                      C.c_void_p]),
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
     "agpu_group_norm_noalloc": (c_status, [C.c_void_p] * 4 + [u32, u32, u32, u32, f32, i32,
                                                               C.c_void_p]),
 }
+
+class AttnLayout(C.Structure):
+    """agpu_attn_layout: element strides of one attention operand."""
+    _fields_ = [("seq_stride", u64), ("head_stride", u64), ("batch_stride", u64)]
+
 
 _LIB = None
 

@@ -286,6 +286,74 @@ extern "C" agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer
                          "group_norm_swish");
 }
 
+// --------------------------------------------------------- gemm epilogue --
+extern "C" agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                                    const agpu_buffer* bias, const agpu_buffer* resid,
+                                    uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                    int trans_a, int trans_b, int act, agpu_buffer** out) {
+  CHECK_DEV(dev, "gemm_ex");
+  CHECK_BUF(a, "gemm_ex", "A");
+  CHECK_BUF(b, "gemm_ex", "B");
+  CHECK_OUT(out, "gemm_ex");
+  CHECK_LEN(a, (uint64_t)batch * m * k, "gemm_ex", "A");
+  CHECK_LEN(b, (uint64_t)batch * k * n, "gemm_ex", "B");
+  if (bias) CHECK_LEN(bias, n, "gemm_ex", "bias");
+  if (resid) CHECK_LEN(resid, (uint64_t)batch * m * n, "gemm_ex", "resid");
+  if (act < 0 || act > 2) return fail(AGPU_ERR_INVALID, "gemm_ex: unknown activation %d", act);
+  GemmEpilogue ep;
+  ep.bias = bias ? bias->dptr : nullptr;
+  ep.resid = resid ? resid->dptr : nullptr;
+  ep.act = act;
+  return with_output(dev, (uint64_t)batch * m * n, out, [&](float* c) {
+    return launch_gemm_ex(dev, a->dptr, b->dptr, c, batch, m, n, k, trans_a != 0, trans_b != 0,
+                          ep, dev->stream);
+  });
+}
+
+// ------------------------------------------------------- LLaMA-layer ops --
+extern "C" agpu_status agpu_rmsnorm(agpu_device* dev, const agpu_buffer* x, const agpu_buffer* w,
+                                    uint32_t rows, uint32_t cols, float eps, agpu_buffer** out) {
+  CHECK_DEV(dev, "rmsnorm");
+  CHECK_BUF(x, "rmsnorm", "input");
+  CHECK_BUF(w, "rmsnorm", "weight");
+  CHECK_OUT(out, "rmsnorm");
+  CHECK_LEN(x, (uint64_t)rows * cols, "rmsnorm", "input");
+  CHECK_LEN(w, cols, "rmsnorm", "weight");
+  return with_output(dev, (uint64_t)rows * cols, out, [&](float* y) {
+    return launch_rmsnorm(dev, x->dptr, w->dptr, y, rows, cols, eps, dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_rope(agpu_device* dev, const agpu_buffer* x, uint32_t batch,
+                                 uint32_t seq, uint32_t heads, uint32_t dim, float base,
+                                 agpu_buffer** out) {
+  CHECK_DEV(dev, "rope");
+  CHECK_BUF(x, "rope", "input");
+  CHECK_OUT(out, "rope");
+  const uint64_t n = (uint64_t)batch * seq * heads * dim;
+  CHECK_LEN(x, n, "rope", "input");
+  if (dim % 2) return fail(AGPU_ERR_SHAPE, "rope: head dim %u is odd", dim);
+  return with_output(dev, n, out, [&](float* y) {
+    return launch_rope(dev, x->dptr, y, batch, seq, heads, dim, (uint64_t)heads * dim, base,
+                       dev->stream);
+  });
+}
+
+extern "C" agpu_status agpu_swish_mul(agpu_device* dev, const agpu_buffer* gate,
+                                      const agpu_buffer* up, agpu_buffer** out) {
+  CHECK_DEV(dev, "swish_mul");
+  CHECK_BUF(gate, "swish_mul", "gate");
+  CHECK_BUF(up, "swish_mul", "up");
+  CHECK_OUT(out, "swish_mul");
+  if (gate->len != up->len)
+    return fail(AGPU_ERR_SHAPE, "swish_mul: length mismatch (%llu vs %llu)",
+                (unsigned long long)gate->len, (unsigned long long)up->len);
+  return with_output(dev, gate->len, out, [&](float* o) {
+    return launch_swish_mul(dev, gate->dptr, up->dptr, o, 1, (uint32_t)gate->len, gate->len,
+                            up->len, gate->len, dev->stream);
+  });
+}
+
 // ------------------------------------------------------------------ sdpa --
 static agpu_status sdpa_impl(agpu_device* dev, const agpu_buffer* q, const agpu_buffer* k,
                              const agpu_buffer* v, uint32_t bh, uint32_t s, uint32_t d,
@@ -439,6 +507,65 @@ agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k, c
                              void* stream) {
   CHECK_DEV(dev, "launch_sdpa");
   return launch_attention(dev, q, k, v, out, bh, s, d, causal != 0, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
+                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a,
+                                int trans_b, const float* bias, const float* resid, int act,
+                                void* stream) {
+  CHECK_DEV(dev, "launch_gemm_ex");
+  if ((!a || !b || !c) && (uint64_t)batch * m * n)
+    return fail(AGPU_ERR_INVALID, "launch_gemm_ex: NULL pointer");
+  if (act < 0 || act > 2) return fail(AGPU_ERR_INVALID, "launch_gemm_ex: unknown activation");
+  GemmEpilogue ep;
+  ep.bias = bias;
+  ep.resid = resid;
+  ep.act = act;
+  return launch_gemm_ex(dev, a, b, c, batch, m, n, k, trans_a != 0, trans_b != 0, ep,
+                        pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_sdpa_strided(agpu_device* dev, const float* q, const float* k,
+                                     const float* v, float* out, uint32_t batch, uint32_t heads,
+                                     uint32_t seq, uint32_t d, const agpu_attn_layout* ql,
+                                     const agpu_attn_layout* kl, const agpu_attn_layout* vl,
+                                     const agpu_attn_layout* ol, int causal, void* stream) {
+  CHECK_DEV(dev, "launch_sdpa_strided");
+  if (!ql || !kl || !vl || !ol) return fail(AGPU_ERR_INVALID, "launch_sdpa_strided: NULL layout");
+  auto cv = [](const agpu_attn_layout* l, long long (&s)[3]) {
+    s[0] = (long long)l->seq_stride;
+    s[1] = (long long)l->head_stride;
+    s[2] = (long long)l->batch_stride;
+  };
+  long long qs[3], ks[3], vs[3], os[3];
+  cv(ql, qs); cv(kl, ks); cv(vl, vs); cv(ol, os);
+  return launch_attention_strided(dev, q, k, v, out, batch, heads, seq, d, qs, ks, vs, os,
+                                  causal != 0, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_rmsnorm(agpu_device* dev, const float* x, const float* w, float* y,
+                                uint64_t rows, uint32_t cols, float eps, void* stream) {
+  CHECK_DEV(dev, "launch_rmsnorm");
+  return launch_rmsnorm(dev, x, w, y, rows, cols, eps, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_rope(agpu_device* dev, const float* x, float* y, uint32_t batch,
+                             uint32_t seq, uint32_t heads, uint32_t dim, uint64_t row_stride,
+                             float base, void* stream) {
+  CHECK_DEV(dev, "launch_rope");
+  if (row_stride < (uint64_t)heads * dim)
+    return fail(AGPU_ERR_SHAPE, "launch_rope: row stride smaller than heads * dim");
+  return launch_rope(dev, x, y, batch, seq, heads, dim, row_stride, base,
+                     pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_swish_mul(agpu_device* dev, const float* gate, const float* up,
+                                  float* out, uint64_t rows, uint32_t cols, uint64_t gs,
+                                  uint64_t us, uint64_t os, void* stream) {
+  CHECK_DEV(dev, "launch_swish_mul");
+  if (gs < cols || us < cols || os < cols)
+    return fail(AGPU_ERR_SHAPE, "launch_swish_mul: row stride smaller than cols");
+  return launch_swish_mul(dev, gate, up, out, rows, cols, gs, us, os, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,

@@ -84,6 +84,15 @@ inline uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
                         uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                         bool a_trans, bool b_trans, cudaStream_t s);
+// Fused GEMM epilogue: C = act(A*B + bias[col] + resid[batch, row, col]).
+struct GemmEpilogue {
+  const float* bias = nullptr;   // [n] or null
+  const float* resid = nullptr;  // [batch, m, n] or null (may alias nothing but C's shape)
+  int act = 0;                   // 0 none, 1 swish, 2 relu
+};
+agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
+                           uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
+                           bool b_trans, const GemmEpilogue& ep, cudaStream_t s);
 agpu_status launch_softmax(agpu_device* dev, const float* x, float* y, uint64_t rows,
                            uint32_t cols, cudaStream_t s);
 
@@ -92,6 +101,19 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
                               uint32_t spatial, uint32_t groups, float eps, bool swish,
                               cudaStream_t s);
 
+agpu_status launch_rmsnorm(agpu_device* dev, const float* x, const float* w, float* y,
+                           uint64_t rows, uint32_t cols, float eps, cudaStream_t s);
+agpu_status launch_rope(agpu_device* dev, const float* x, float* y, uint32_t batch, uint32_t seq,
+                        uint32_t heads, uint32_t dim, uint64_t row_stride, float base,
+                        cudaStream_t s);
+agpu_status launch_swish_mul(agpu_device* dev, const float* gate, const float* up, float* out,
+                             uint64_t rows, uint32_t cols, uint64_t gs, uint64_t us, uint64_t os,
+                             cudaStream_t s);
+agpu_status launch_attention_strided(agpu_device* dev, const float* q, const float* k,
+                                     const float* v, float* o, uint32_t B, uint32_t H,
+                                     uint32_t s, uint32_t d, const long long (&qs)[3],
+                                     const long long (&ks)[3], const long long (&vs)[3],
+                                     const long long (&os)[3], bool causal, cudaStream_t st);
 agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
                              cudaStream_t st);

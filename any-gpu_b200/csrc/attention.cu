@@ -31,10 +31,6 @@
 
 namespace agpu {
 
-agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
-                             uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
-                             uint32_t box_outer, bool mn_major, bool round_tf32);
-
 namespace {
 
 constexpr int QT = 128;     // query rows per CTA
@@ -56,6 +52,12 @@ __device__ __forceinline__ uint32_t round_tf32(float x) {
   return u & 0xFFFFE000u;
 }
 
+// Output strides (elements) and which input maps order heads before sequence.
+struct AttnOut {
+  long long s, h, b;
+  int hs;  // bit 0: q, bit 1: k, bit 2: v
+};
+
 template <int D>
 struct AttnCfg {
   static constexpr int Q_BYTES = QT * D * 4;
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(192, 1)
     attention_tf32_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, float* __restrict__ out,
-                          int S, float scale_log2, unsigned int* status) {
+                          int S, float scale_log2, AttnOut ol, unsigned int* status) {
   using C = AttnCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -94,8 +96,14 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.y;
+  const int head = blockIdx.y, bat = blockIdx.z;
   const int q0 = blockIdx.x * QT;
+  // 4-D maps {d, s, h, b}, or {d, h, s, b} when the head stride is the smaller
+  // one (e.g. [batch, seq, heads, d] activations); the box is rows x 32 dims.
+  auto load = [&](void* dst, const CUtensorMap* m, uint64_t* bar, int d0, int s0, bool hs) {
+    if (hs) ptx::tma_load_4d(dst, m, bar, d0, head, s0, bat);
+    else ptx::tma_load_4d(dst, m, bar, d0, s0, head, bat);
+  };
   const int nb_all = (S + KT - 1) / KT;
   const int nb = CAUSAL ? min(nb_all, (q0 + QT - 1) / KT + 1) : nb_all;
 
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(192, 1)
       ptx::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c)
-        ptx::tma_load_3d(sq + c * QT * 128, &tm_q, q_full, c * 32, q0, bh);
+        load(sq + c * QT * 128, &tm_q, q_full, c * 32, q0, ol.hs & 1);
       long long issued = 0;
       for (int j = 0; j < nb; ++j) {
         const int st = j & 1;
@@ -139,11 +147,11 @@ __global__ void __launch_bounds__(192, 1)
         ptx::mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          ptx::tma_load_3d(stage_k(st) + c * KT * 128, &tm_k, &k_full[st], c * 32, j * KT, bh);
+          load(stage_k(st) + c * KT * 128, &tm_k, &k_full[st], c * 32, j * KT, ol.hs & 2);
         ptx::mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
-          ptx::tma_load_3d(stage_v(st) + c * KT * 128, &tm_v, &v_full[st], c * 32, j * KT, bh);
+          load(stage_v(st) + c * KT * 128, &tm_v, &v_full[st], c * 32, j * KT, ol.hs & 4);
         ++issued;
       }
       // never exit with loads in flight into this CTA's shared memory
@@ -272,7 +280,7 @@ __global__ void __launch_bounds__(192, 1)
     if (ok && nb > 0 && ptx::mbar_wait(o_done, (nb - 1) & 1, status, 0x20a, abort_flag)) {
       ptx::tc_fence_after();
       const float inv = 1.0f / l;
-      float* orow = out + ((long long)bh * S + qrow) * D;
+      float* orow = out + (long long)bat * ol.b + (long long)head * ol.h + (long long)qrow * ol.s;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -299,6 +307,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// (seq, head, batch) element strides of Q, K, V, O.
+struct AttnStrides {
+  long long q[3], k[3], v[3], o[3];
+};
+
 // ----------------------------------------------------------------- SIMT --
 // One warp per query row; keys streamed, online softmax, O in registers
 // (lane owns head dims lane, lane+32, ...).  Exact fp32, any head dim <= 256.
@@ -306,15 +319,18 @@ template <bool CAUSAL>
 __global__ void __launch_bounds__(256) attention_simt_kernel(const float* __restrict__ Q,
                                                              const float* __restrict__ K,
                                                              const float* __restrict__ V,
-                                                             float* __restrict__ O, int BH, int S,
-                                                             int D, float scale) {
+                                                             float* __restrict__ O, int B, int H,
+                                                             int S, int D, float scale,
+                                                             AttnStrides st) {
   const long long gw = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
-  if (gw >= (long long)BH * S) return;
-  const int bh = (int)(gw / S), i = (int)(gw % S);
-  const float* q = Q + ((long long)bh * S + i) * D;
-  const float* kb = K + (long long)bh * S * D;
-  const float* vb = V + (long long)bh * S * D;
+  if (gw >= (long long)B * H * S) return;
+  const int i = (int)(gw % S);
+  const int h = (int)((gw / S) % H);
+  const int b = (int)(gw / ((long long)S * H));
+  const float* q = Q + b * st.q[2] + h * st.q[1] + i * st.q[0];
+  const float* kb = K + b * st.k[2] + h * st.k[1];
+  const float* vb = V + b * st.v[2] + h * st.v[1];
   float qr[8], acc[8];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
@@ -329,7 +345,7 @@ __global__ void __launch_bounds__(256) attention_simt_kernel(const float* __rest
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const int d = lane + 32 * c;
-      if (d < D) s = fmaf(qr[c], kb[(long long)j * D + d], s);
+      if (d < D) s = fmaf(qr[c], kb[j * st.k[0] + d], s);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -340,11 +356,11 @@ __global__ void __launch_bounds__(256) attention_simt_kernel(const float* __rest
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const int d = lane + 32 * c;
-      acc[c] = acc[c] * a + (d < D ? p * vb[(long long)j * D + d] : 0.f);
+      acc[c] = acc[c] * a + (d < D ? p * vb[j * st.v[0] + d] : 0.f);
     }
     m = mn;
   }
-  float* o = O + ((long long)bh * S + i) * D;
+  float* o = O + b * st.o[2] + h * st.o[1] + i * st.o[0];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int d = lane + 32 * c;
@@ -352,50 +368,121 @@ __global__ void __launch_bounds__(256) attention_simt_kernel(const float* __rest
   }
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4-D map of one attention operand with element strides (seq, head, batch);
+// the smaller of the seq / head strides becomes dimension 1.  Elements are
+// rounded to tf32 (nearest-even) by the TMA unit.  Sets *hs when dimension 1
+// is the head.
+agpu_status make_attn_map(CUtensorMap* map, const float* base, int D, int S, int H, int B,
+                          const long long (&st)[3], uint32_t rows, bool mn_major, bool* hs) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  *hs = st[1] < st[0];
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], es[4] = {1, 1, 1, 1};
+  dims[0] = D;
+  box[0] = 32;
+  if (*hs) {
+    dims[1] = H; strides[0] = st[1] * 4; box[1] = 1;
+    dims[2] = S; strides[1] = st[0] * 4; box[2] = rows;
+  } else {
+    dims[1] = S; strides[0] = st[0] * 4; box[1] = rows;
+    dims[2] = H; strides[1] = st[1] * 4; box[2] = 1;
+  }
+  dims[3] = B; strides[2] = (B > 1 ? st[2] : (long long)std::max(st[0] * S, st[1] * H)) * 4;
+  box[3] = 1;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 4, const_cast<float*>(base), dims,
+                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(AGPU_ERR_CUDA, "sdpa: tensor map encode failed (%d); strides must be "
+                "multiples of 4 elements", (int)r);
+  return AGPU_OK;
+}
+
 template <int D, bool CAUSAL>
 agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, const float* v,
-                             float* o, int bh, int s, cudaStream_t st) {
+                             float* o, int B, int H, int s, const AttnStrides& sd,
+                             cudaStream_t st) {
   using C = AttnCfg<D>;
   CUtensorMap tq, tk, tv;
-  // operands rounded to tf32 (nearest-even) by the TMA unit on load
-  AGPU_TRY(make_tmap_f32_3d(&tq, q, D, s, bh, (uint64_t)s * D, 32, QT, false, true));
-  AGPU_TRY(make_tmap_f32_3d(&tk, k, D, s, bh, (uint64_t)s * D, 32, KT, false, true));
-  AGPU_TRY(make_tmap_f32_3d(&tv, v, D, s, bh, (uint64_t)s * D, 32, KT, true, true));
+  bool hq, hk, hv;
+  AGPU_TRY(make_attn_map(&tq, q, D, s, H, B, sd.q, QT, false, &hq));
+  AGPU_TRY(make_attn_map(&tk, k, D, s, H, B, sd.k, KT, false, &hk));
+  AGPU_TRY(make_attn_map(&tv, v, D, s, H, B, sd.v, KT, true, &hv));
+  AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hq ? 1 : 0) | (hk ? 2 : 0) | (hv ? 4 : 0)};
   auto kern = attention_tf32_kernel<D, CAUSAL>;
   AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-  dim3 grid((unsigned)ceil_div(s, QT), (unsigned)bh);
+  dim3 grid((unsigned)ceil_div(s, QT), (unsigned)H, (unsigned)B);
   const float scale_log2 = (1.0f / sqrtf((float)D)) * kLog2e;
-  kern<<<grid, 192, C::SMEM, st>>>(tq, tk, tv, o, s, scale_log2, dev->d_status);
+  kern<<<grid, 192, C::SMEM, st>>>(tq, tk, tv, o, s, scale_log2, ol, dev->d_status);
   return after_launch(dev, "attention_tf32_kernel");
 }
 
 }  // namespace
 
-agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
-                             float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
-                             cudaStream_t st) {
-  if ((uint64_t)bh * s * d == 0) return AGPU_OK;
+agpu_status launch_attention_strided(agpu_device* dev, const float* q, const float* k,
+                                     const float* v, float* o, uint32_t B, uint32_t H,
+                                     uint32_t s, uint32_t d, const long long (&qs)[3],
+                                     const long long (&ks)[3], const long long (&vs)[3],
+                                     const long long (&os)[3], bool causal, cudaStream_t st) {
+  if ((uint64_t)B * H * s * d == 0) return AGPU_OK;
+  AttnStrides sd;
+  for (int i = 0; i < 3; ++i) {
+    sd.q[i] = qs[i]; sd.k[i] = ks[i]; sd.v[i] = vs[i]; sd.o[i] = os[i];
+  }
+  bool pitch_ok = true;
+  for (int i = 0; i < 3; ++i)
+    pitch_ok = pitch_ok && sd.q[i] % 4 == 0 && sd.k[i] % 4 == 0 && sd.v[i] % 4 == 0 &&
+               sd.o[i] % 4 == 0;
   const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15u) == 0;
   // fp32-level accuracy modes (3xTF32, FFMA) take the exact SIMT kernel
-  const bool tc = dev->precision == AGPU_PREC_TF32 && aligned && (d == 64 || d == 128) &&
-                  s >= 64 && bh <= 65535;
+  const bool tc = dev->precision == AGPU_PREC_TF32 && aligned && pitch_ok &&
+                  (d == 64 || d == 128) && s >= 64 && H <= 65535 && B <= 65535;
   if (tc) {
     if (d == 128)
-      return causal ? run_attention_tc<128, true>(dev, q, k, v, o, bh, s, st)
-                    : run_attention_tc<128, false>(dev, q, k, v, o, bh, s, st);
-    return causal ? run_attention_tc<64, true>(dev, q, k, v, o, bh, s, st)
-                  : run_attention_tc<64, false>(dev, q, k, v, o, bh, s, st);
+      return causal ? run_attention_tc<128, true>(dev, q, k, v, o, B, H, s, sd, st)
+                    : run_attention_tc<128, false>(dev, q, k, v, o, B, H, s, sd, st);
+    return causal ? run_attention_tc<64, true>(dev, q, k, v, o, B, H, s, sd, st)
+                  : run_attention_tc<64, false>(dev, q, k, v, o, B, H, s, sd, st);
   }
   if (d > 256) return fail(AGPU_ERR_UNSUPPORTED, "sdpa: head dim %u > 256", d);
-  const long long warps = (long long)bh * s;
+  const long long warps = (long long)B * H * s;
   const unsigned blocks = (unsigned)ceil_div((uint64_t)warps * 32, 256);
   const float scale = 1.0f / sqrtf((float)d);
   if (causal)
-    attention_simt_kernel<true><<<blocks, 256, 0, st>>>(q, k, v, o, bh, s, d, scale);
+    attention_simt_kernel<true><<<blocks, 256, 0, st>>>(q, k, v, o, B, H, s, d, scale, sd);
   else
-    attention_simt_kernel<false><<<blocks, 256, 0, st>>>(q, k, v, o, bh, s, d, scale);
+    attention_simt_kernel<false><<<blocks, 256, 0, st>>>(q, k, v, o, B, H, s, d, scale, sd);
   return after_launch(dev, "attention_simt_kernel");
+}
+
+// Contiguous [bh, s, d] operands: heads = bh, batch = 1.
+agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
+                             float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
+                             cudaStream_t st) {
+  const long long c[3] = {(long long)d, (long long)s * d, (long long)bh * s * d};
+  return launch_attention_strided(dev, q, k, v, o, 1, bh, s, d, c, c, c, c, causal, st);
 }
 
 }  // namespace agpu

@@ -94,7 +94,7 @@ struct ConvPolicy {
   __device__ bool col_live(const Tile& t, int col0) const { return t.oc0 + col0 < cout; }
 
   __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float*,
-                        int, bool accumulate) const {
+                        int, bool accumulate, bool) const {
     const int oh = t.oh0 + row / BW, ow = t.ow0 + row % BW;
     if (oh >= Ho || ow >= Wo) return;
     const long long plane = (long long)Ho * Wo;

@@ -39,6 +39,12 @@ using umma::kEpiStride;
 
 namespace {
 
+__device__ __forceinline__ float epi_act(float x, int act) {
+  if (act == 1) return x / (1.0f + expf(-x));  // swish, src/ops/elementwise.rs:87
+  if (act == 2) return fmaxf(x, 0.0f);         // relu
+  return x;
+}
+
 // Row-major (batched) GEMM: tiles 128 x BN walk batch-major with a 16-row-
 // block group swizzle (L2 reuse of the B column block across the group).
 template <int BN_, bool A_MN_, bool B_MN_>
@@ -49,6 +55,10 @@ struct GemmPolicy {
   long long tiles;
   float* C;
   long long c_batch;  // M * N
+  // fused epilogue (applied once): C = act(A*B + bias[col] + resid[row, col])
+  const float* bias;   // [N] or null (Linear bias, the reference's add_per_col)
+  const float* resid;  // [batch, M, N] or null (residual add)
+  int act;             // 0 none, 1 swish, 2 relu
 
   struct Tile { int b, m0, n0; };
 
@@ -95,7 +105,7 @@ struct GemmPolicy {
   // warp transposes its 32x32 block through shared memory so that each
   // store instruction writes four full 128-byte row segments.
   __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float* stg,
-                        int lane, bool accumulate) const {
+                        int lane, bool accumulate, bool last) const {
     float4* srow = reinterpret_cast<float4*>(stg + lane * kEpiStride);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -111,10 +121,25 @@ struct GemmPolicy {
       const int grow = row_base + r;
       float4 val = *reinterpret_cast<const float4*>(stg + r * kEpiStride + (lane & 7) * 4);
       if (grow < M && col < N) {
-        float4* dst = reinterpret_cast<float4*>(Cb + (long long)grow * N + col);
+        const long long off = (long long)grow * N + col;
+        float4* dst = reinterpret_cast<float4*>(Cb + off);
         if (accumulate) {
           const float4 o = *dst;
           val.x += o.x; val.y += o.y; val.z += o.z; val.w += o.w;
+        } else {
+          if (bias) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + col));
+            val.x += bb.x; val.y += bb.y; val.z += bb.z; val.w += bb.w;
+          }
+          if (resid) {
+            const float4 rr =
+                __ldg(reinterpret_cast<const float4*>(resid + (long long)t.b * c_batch + off));
+            val.x += rr.x; val.y += rr.y; val.z += rr.z; val.w += rr.w;
+          }
+        }
+        if (last && act) {
+          val.x = epi_act(val.x, act); val.y = epi_act(val.y, act);
+          val.z = epi_act(val.z, act); val.w = epi_act(val.w, act);
         }
         *dst = val;
       }
@@ -130,7 +155,7 @@ template <bool AT, bool BT>
 __global__ void __launch_bounds__(256) gemm_ffma_kernel(const float* __restrict__ A,
                                                         const float* __restrict__ B,
                                                         float* __restrict__ C, int M, int N,
-                                                        int K) {
+                                                        int K, GemmEpilogue ep) {
   __shared__ float As[16][64 + 4];
   __shared__ float Bs[16][64 + 4];
   const int b = blockIdx.z;
@@ -174,7 +199,12 @@ __global__ void __launch_bounds__(256) gemm_ffma_kernel(const float* __restrict_
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int gn = n0 + tx * 4 + j;
-      if (gn < N) C[(long long)gm * N + gn] = acc[i][j];
+      if (gn < N) {
+        float v = acc[i][j];
+        if (ep.bias) v += ep.bias[gn];
+        if (ep.resid) v += ep.resid[(long long)b * M * N + (long long)gm * N + gn];
+        C[(long long)gm * N + gn] = epi_act(v, ep.act);
+      }
     }
   }
 }
@@ -230,7 +260,8 @@ agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner
 
 template <int BN, bool A_MN, bool B_MN, bool X3>
 static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, float* c,
-                          uint32_t batch, uint32_t m, uint32_t n, uint32_t k, cudaStream_t s) {
+                          uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                          const GemmEpilogue& ep, cudaStream_t s) {
   using P = GemmPolicy<BN, A_MN, B_MN>;
   using Cfg = umma::Cfg<BN, X3>;
   CUtensorMap ta, tb;
@@ -251,6 +282,9 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
   pol.C = c;
   pol.c_batch = (long long)m * n;
+  pol.bias = ep.bias;
+  pol.resid = ep.resid;
+  pol.act = ep.act;
   auto kern = umma::umma_tf32_kernel<P, X3>;
   AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
   const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
@@ -261,29 +295,29 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
 template <bool X3>
 static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at,
-                               bool bt, cudaStream_t s) {
+                               bool bt, const GemmEpilogue& ep, cudaStream_t s) {
   const bool wide = n > 128;
   // B is MN-major unless stored transposed ([N,K]).
   if (wide) {
-    if (!at && !bt) return run_tc<256, false, true, X3>(dev, a, b, c, batch, m, n, k, s);
-    if (!at && bt) return run_tc<256, false, false, X3>(dev, a, b, c, batch, m, n, k, s);
-    if (at && !bt) return run_tc<256, true, true, X3>(dev, a, b, c, batch, m, n, k, s);
-    return run_tc<256, true, false, X3>(dev, a, b, c, batch, m, n, k, s);
+    if (!at && !bt) return run_tc<256, false, true, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (!at && bt) return run_tc<256, false, false, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (at && !bt) return run_tc<256, true, true, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+    return run_tc<256, true, false, X3>(dev, a, b, c, batch, m, n, k, ep, s);
   }
-  if (!at && !bt) return run_tc<128, false, true, X3>(dev, a, b, c, batch, m, n, k, s);
-  if (!at && bt) return run_tc<128, false, false, X3>(dev, a, b, c, batch, m, n, k, s);
-  if (at && !bt) return run_tc<128, true, true, X3>(dev, a, b, c, batch, m, n, k, s);
-  return run_tc<128, true, false, X3>(dev, a, b, c, batch, m, n, k, s);
+  if (!at && !bt) return run_tc<128, false, true, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+  if (!at && bt) return run_tc<128, false, false, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+  if (at && !bt) return run_tc<128, true, true, X3>(dev, a, b, c, batch, m, n, k, ep, s);
+  return run_tc<128, true, false, X3>(dev, a, b, c, batch, m, n, k, ep, s);
 }
 
 static agpu_status run_ffma(agpu_device* dev, const float* a, const float* b, float* c,
                             uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at, bool bt,
-                            cudaStream_t s) {
+                            const GemmEpilogue& ep, cudaStream_t s) {
   dim3 grid((unsigned)ceil_div(n, 64), (unsigned)ceil_div(m, 64), batch);
-  if (!at && !bt) gemm_ffma_kernel<false, false><<<grid, 256, 0, s>>>(a, b, c, m, n, k);
-  else if (!at && bt) gemm_ffma_kernel<false, true><<<grid, 256, 0, s>>>(a, b, c, m, n, k);
-  else if (at && !bt) gemm_ffma_kernel<true, false><<<grid, 256, 0, s>>>(a, b, c, m, n, k);
-  else gemm_ffma_kernel<true, true><<<grid, 256, 0, s>>>(a, b, c, m, n, k);
+  if (!at && !bt) gemm_ffma_kernel<false, false><<<grid, 256, 0, s>>>(a, b, c, m, n, k, ep);
+  else if (!at && bt) gemm_ffma_kernel<false, true><<<grid, 256, 0, s>>>(a, b, c, m, n, k, ep);
+  else if (at && !bt) gemm_ffma_kernel<true, false><<<grid, 256, 0, s>>>(a, b, c, m, n, k, ep);
+  else gemm_ffma_kernel<true, true><<<grid, 256, 0, s>>>(a, b, c, m, n, k, ep);
   return after_launch(dev, "gemm_ffma_kernel");
 }
 
@@ -296,21 +330,30 @@ bool gemm_tc_eligible(const float* a, const float* b, const float* c, uint32_t m
   return mis == 0 && (k % 4 == 0) && (n % 4 == 0) && (m % 4 == 0) && k >= 8;
 }
 
-agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
-                        uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
-                        bool b_trans, cudaStream_t s) {
+agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
+                           uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
+                           bool b_trans, const GemmEpilogue& ep, cudaStream_t s) {
   if (batch == 0 || m == 0 || n == 0) return AGPU_OK;
-  if (k == 0) {
+  const bool has_ep = ep.bias || ep.resid || ep.act;
+  if (k == 0 && !has_ep) {
     AGPU_CUDA(cudaMemsetAsync(c, 0, (size_t)batch * m * n * sizeof(float), s));
     return AGPU_OK;
   }
   const agpu_precision p = dev->precision;
   const bool tiny = (uint64_t)m * n * k * batch < (1ull << 15);
-  if (p == AGPU_PREC_FFMA || tiny || !gemm_tc_eligible(a, b, c, m, n, k))
-    return run_ffma(dev, a, b, c, batch, m, n, k, a_trans, b_trans, s);
+  const bool vec_ep = (reinterpret_cast<uintptr_t>(ep.bias) |
+                       reinterpret_cast<uintptr_t>(ep.resid)) % 16 == 0;
+  if (p == AGPU_PREC_FFMA || tiny || k == 0 || !vec_ep || !gemm_tc_eligible(a, b, c, m, n, k))
+    return run_ffma(dev, a, b, c, batch, m, n, k, a_trans, b_trans, ep, s);
   if (p == AGPU_PREC_TF32X3)
-    return dispatch_tc<true>(dev, a, b, c, batch, m, n, k, a_trans, b_trans, s);
-  return dispatch_tc<false>(dev, a, b, c, batch, m, n, k, a_trans, b_trans, s);
+    return dispatch_tc<true>(dev, a, b, c, batch, m, n, k, a_trans, b_trans, ep, s);
+  return dispatch_tc<false>(dev, a, b, c, batch, m, n, k, a_trans, b_trans, ep, s);
+}
+
+agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
+                        uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
+                        bool b_trans, cudaStream_t s) {
+  return launch_gemm_ex(dev, a, b, c, batch, m, n, k, a_trans, b_trans, GemmEpilogue{}, s);
 }
 
 }  // namespace agpu

@@ -85,11 +85,12 @@ __device__ __forceinline__ void split_tf32(uint32_t* hi, uint32_t* lo, int words
 //   void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
 //             uint64_t* bar, const Tile&, int kb) const;       // issues STAGE_BYTES of TMA
 //   void store(const Tile&, int row, int col0, const uint32_t (&v)[32], float* stg,
-//              int lane, bool accumulate) const;
+//              int lane, bool accumulate, bool last) const;
 //                                 // row = accumulator lane 0..127, cols col0..col0+31;
 //                                 // called by all 32 lanes of a warp together;
 //                                 // accumulate: add to the value stored for the
-//                                 // previous K segment of this tile
+//                                 // previous K segment of this tile; last:
+//                                 // this is the tile's final K segment
 //   bool col_live(const Tile&, int col0) const;  // warp-uniform: chunk has any valid column
 template <class P, bool X3>
 __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
           uint32_t v[32];
           ptx::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
           ptx::tmem_wait_ld();
-          pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, k0 > 0);
+          pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, k0 > 0, k0 + kseg >= num_k);
         }
         ptx::tc_fence_before();
         ptx::mbar_arrive(&tempty[acc]);

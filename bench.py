@@ -12,9 +12,11 @@ Other workloads (`--workload`), each one of the benchmark configurations:
   sdpa     scaled_dot_product_attention, B8 H32 S2048 D128, non-causal, N(0,1)
   unet     conv2d 3x3 s1 p1 (N16, 320->320, 64x64, Kaiming-uniform W, bias 0)
            -> group_norm (32 groups, eps 1e-5, gamma 1, beta 0) -> swish
+  llama    LLaMA-style decoder layer forward: B32 S2048 d4096 H32x128 FFN 11008,
+           RoPE base 1e4, W ~ N(0,0.02), x ~ N(0,1)
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl agpu|reference]
-                    [--workload bmm_softmax|matmul|sdpa|unet]
+                    [--workload bmm_softmax|matmul|sdpa|unet|llama]
 
 One process per GPU (torchrun for N > 1).  Every rank runs the full workload on
 its own GPU ("scaling": "weak": batches/heads/images are independent, no
@@ -455,7 +457,116 @@ class Unet(Workload):
                                      "note": "step time minus conv time"}}
 
 
-WORKLOADS = {"bmm_softmax": BmmSoftmax, "matmul": Matmul, "sdpa": Sdpa, "unet": Unet}
+class Llama(Workload):
+    name = "llama"
+    l2 = "activations ~19 GB > 126 MB L2"
+
+    def __init__(self, args, rank):
+        super().__init__(args, rank)
+        from any_gpu.llama import LlamaDims
+        self.dims = LlamaDims(batch=args.llama_batch, seq=2048, d_model=4096, heads=32,
+                              ffn=11008)
+        dm = self.dims
+        self.flops = dm.gemm_flops() + dm.attention_flops()
+        self.dom_flops = 2.0 * dm.tokens * dm.d_model * 2 * dm.ffn
+        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256, K-major A, MN-major B>> (gate/up)"
+
+    def config(self):
+        dm = self.dims
+        return {"workload": "llama_decoder_layer_forward", "batch": dm.batch, "seq": dm.seq,
+                "d_model": dm.d_model, "heads": dm.heads, "head_dim": dm.head_dim,
+                "ffn": dm.ffn, "rope_base": dm.rope_base, "causal": dm.causal,
+                "inputs": "x N(0,1); W N(0,0.02); norm weights 1",
+                "flops": "2*T*(4d^2+3dF) + 4*B*H*S^2*Dh"}
+
+    def host_inputs(self):
+        dm = self.dims
+        d, Fd = dm.d_model, dm.ffn
+        r = np.random.default_rng(1239 + 1000 * self.rank)
+        return {"x": _normal(r, dm.tokens * d), "attn_norm": np.ones(d, np.float32),
+                "ffn_norm": np.ones(d, np.float32), "wqkv": _normal(r, d * 3 * d, 0.02),
+                "wo": _normal(r, d * d, 0.02), "wgu": _normal(r, d * 2 * Fd, 0.02),
+                "wd": _normal(r, Fd * d, 0.02)}
+
+    def out_elems(self):
+        return self.dims.tokens * self.dims.d_model
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        self.ws = {k: torch.empty(n, dtype=torch.float32, device=f"cuda:{local}")
+                   for k, n in self.dims.workspace_elems().items()}
+        self.Y = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
+
+    def step(self, dev, sptr, ev=None):
+        from any_gpu.llama import layer_forward
+        w = {k: v.data_ptr() for k, v in self.dev_in.items() if k != "x"}
+        ws = {k: v.data_ptr() for k, v in self.ws.items()}
+        if ev is None:
+            layer_forward(dev, self.dims, self.dev_in["x"].data_ptr(), w, ws, self.Y.data_ptr(),
+                          sptr)
+            return
+        # same sequence with the gate/up GEMM bracketed by events
+        dm = self.dims
+        T, d, Fd = dm.tokens, dm.d_model, dm.ffn
+        dev_hook = _EventHook(dev, ev, target=2)
+        layer_forward(dev_hook, self.dims, self.dev_in["x"].data_ptr(), w, ws,
+                      self.Y.data_ptr(), sptr)
+
+    def output(self):
+        return self.Y
+
+    def e2e_step(self, dev):
+        from any_gpu.llama import layer_forward
+        g = {k: dev.upload(v.numpy()) for k, v in self.host.items()}
+        ws = {k: dev.alloc(n) for k, n in self.dims.workspace_elems().items()}
+        y = dev.alloc(self.out_elems())
+        layer_forward(dev, self.dims, g["x"].device_ptr,
+                      {k: b.device_ptr for k, b in g.items() if k != "x"},
+                      {k: b.device_ptr for k, b in ws.items()}, y.device_ptr)
+        dev.read(y, out=self.out_host.numpy())
+        for b in list(g.values()) + list(ws.values()) + [y]:
+            b.free()
+
+    def cpu_sample(self, orc, target_s):
+        dm = self.dims
+        d = dm.d_model
+        r = np.random.default_rng(1239)
+        x = _normal(r, 64 * d)
+        wqkv = _normal(r, d * 3 * d, 0.02)
+        done, t = 0, 0.0
+        rows = max(8, orc.num_threads())
+        while t < target_s:
+            t0 = time.perf_counter()
+            orc.matmul(x[: rows * d], wqkv, rows, 3 * d, d, threads=True)
+            t += time.perf_counter() - t0
+            done += rows
+        return (2.0 * done * d * 3 * d / t / 1e12,
+                f"{done} token rows of the Wqkv projection (cpu_matmul), {t:.1f} s, "
+                "the layer's dominant op, extrapolated by FLOPs")
+
+
+class _EventHook:
+    """Wraps a GpuDevice so that the `target`-th launch_gemm_ex of a layer is
+    bracketed by the two CUDA events in `ev` (0-based: 2 = the gate/up GEMM)."""
+
+    def __init__(self, dev, ev, target):
+        self._dev, self._ev, self._target, self._n = dev, ev, target, 0
+
+    def __getattr__(self, name):
+        return getattr(self._dev, name)
+
+    def launch_gemm_ex(self, *a, **k):
+        hit = self._n == self._target
+        self._n += 1
+        if hit:
+            self._ev[0].record()
+        self._dev.launch_gemm_ex(*a, **k)
+        if hit:
+            self._ev[1].record()
+
+
+WORKLOADS = {"bmm_softmax": BmmSoftmax, "matmul": Matmul, "sdpa": Sdpa, "unet": Unet,
+             "llama": Llama}
 
 
 # -------------------------------------------------------------- arms -----
@@ -626,6 +737,7 @@ def main():
     ap.add_argument("--bh", type=int, default=256, help="sdpa batch*heads (B8 x H32)")
     ap.add_argument("--seq", type=int, default=2048, help="sdpa sequence length")
     ap.add_argument("--images", type=int, default=16, help="unet batch N")
+    ap.add_argument("--llama-batch", type=int, default=32, help="llama sequences of 2048")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":

@@ -123,6 +123,16 @@ AGPU_API agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agp
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a,
                                int trans_b, agpu_buffer** out);
 
+/* gemm with a fused epilogue: C = act(op(A) op(B) + bias[col] + resid), act
+ * 0 = none, 1 = swish, 2 = relu; bias ([n]) and resid ([batch, m, n]) may be
+ * NULL.  The bias term is the reference's Linear bias add_per_col
+ * (src/ops/tensor_ops.rs:336-352) and swish its activation
+ * (src/ops/elementwise.rs:77-89), applied while the tile is in registers. */
+AGPU_API agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                                  const agpu_buffer* bias, const agpu_buffer* resid,
+                                  uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                  int trans_a, int trans_b, int act, agpu_buffer** out);
+
 /* ----------------------------------------------------------- attention ---- */
 /* GpuDevice::softmax (src/ops/attention.rs:91-145): row softmax of [rows, cols]. */
 AGPU_API agpu_status agpu_softmax(agpu_device* dev, const agpu_buffer* x, uint32_t rows,
@@ -196,6 +206,22 @@ AGPU_API agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
                                       uint32_t batch_heads, uint32_t seq_len, uint32_t d_k,
                                       agpu_buffer** out);
 
+/* ------------------------------------------------- LLaMA-layer ops -------- */
+/* No counterparts in the reference (its ops have no RMSNorm or RoPE); they
+ * complete the decoder layer of the benchmark configs from the ops above. */
+/* RMSNorm over rows of `cols`: y = x / sqrt(mean(x^2) + eps) * w[col]. */
+AGPU_API agpu_status agpu_rmsnorm(agpu_device* dev, const agpu_buffer* x, const agpu_buffer* w,
+                                  uint32_t rows, uint32_t cols, float eps, agpu_buffer** out);
+/* Rotary embedding (rotate-half) of x [batch, seq, heads, dim], position =
+ * seq index, angle = pos * base^(-2i/dim). */
+AGPU_API agpu_status agpu_rope(agpu_device* dev, const agpu_buffer* x, uint32_t batch,
+                               uint32_t seq, uint32_t heads, uint32_t dim, float base,
+                               agpu_buffer** out);
+/* SwiGLU product swish(gate) * up, one pass (the reference composes
+ * swish, src/ops/elementwise.rs:211, and mul, :198). Equal lengths. */
+AGPU_API agpu_status agpu_swish_mul(agpu_device* dev, const agpu_buffer* gate,
+                                    const agpu_buffer* up, agpu_buffer** out);
+
 /* --------------------------------------------------------- elementwise ---- */
 /* src/ops/elementwise.rs:188-250.  Binary ops require equal lengths. */
 AGPU_API agpu_status agpu_add(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
@@ -255,6 +281,37 @@ AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, co
 AGPU_API agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k,
                                       const float* v, float* out, uint32_t batch_heads,
                                       uint32_t seq_len, uint32_t d_k, int causal, void* stream);
+AGPU_API agpu_status agpu_launch_gemm_ex(agpu_device* dev, const float* a, const float* b,
+                                         float* c, uint32_t batch, uint32_t m, uint32_t n,
+                                         uint32_t k, int trans_a, int trans_b, const float* bias,
+                                         const float* resid, int act, void* stream);
+/* Element strides of one attention operand laid out as [batch, seq, heads, d]
+ * in any order (d contiguous): e.g. contiguous [bh, s, d] is
+ * {d, s*d, bh*s*d} with heads = bh, batch = 1; the Q part of a packed
+ * [batch, seq, 3, heads, d] projection is {3*heads*d, d, seq*3*heads*d}. */
+typedef struct agpu_attn_layout {
+  uint64_t seq_stride, head_stride, batch_stride;
+} agpu_attn_layout;
+AGPU_API agpu_status agpu_launch_sdpa_strided(agpu_device* dev, const float* q, const float* k,
+                                              const float* v, float* out, uint32_t batch,
+                                              uint32_t heads, uint32_t seq_len, uint32_t d_k,
+                                              const agpu_attn_layout* q_layout,
+                                              const agpu_attn_layout* k_layout,
+                                              const agpu_attn_layout* v_layout,
+                                              const agpu_attn_layout* out_layout, int causal,
+                                              void* stream);
+AGPU_API agpu_status agpu_launch_rmsnorm(agpu_device* dev, const float* x, const float* w,
+                                         float* y, uint64_t rows, uint32_t cols, float eps,
+                                         void* stream);
+/* rows of x / y are row_stride elements apart (in place allowed), heads
+ * `dim` apart inside a row. */
+AGPU_API agpu_status agpu_launch_rope(agpu_device* dev, const float* x, float* y, uint32_t batch,
+                                      uint32_t seq, uint32_t heads, uint32_t dim,
+                                      uint64_t row_stride, float base, void* stream);
+AGPU_API agpu_status agpu_launch_swish_mul(agpu_device* dev, const float* gate, const float* up,
+                                           float* out, uint64_t rows, uint32_t cols,
+                                           uint64_t gate_stride, uint64_t up_stride,
+                                           uint64_t out_stride, void* stream);
 AGPU_API agpu_status agpu_launch_softmax(agpu_device* dev, const float* x, float* y,
                                          uint64_t rows, uint32_t cols, void* stream);
 
