@@ -26,10 +26,12 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "agpu_internal.cuh"
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
+#include "umma2_kernel.cuh"
 
 namespace agpu {
 
@@ -145,6 +147,56 @@ struct GemmPolicy {
       }
     }
     __syncwarp();
+  }
+};
+
+// CTA-pair GEMM tile: 256 x 256; CTA `rank` of the pair stages rows
+// m0 + 128*rank .. +127 of A and columns n0 + 128*rank .. +127 of B.
+template <bool A_MN_, bool B_MN_>
+struct GemmPairPolicy : GemmPolicy<256, A_MN_, B_MN_> {
+  using Base = GemmPolicy<256, A_MN_, B_MN_>;
+  using Tile = typename Base::Tile;
+  static constexpr int PM = 2 * BM;  // tile rows of the pair
+
+  __device__ Tile tile(long long t) const {
+    const long long per_batch = (long long)this->tiles_m * this->tiles_n;
+    Tile r;
+    r.b = (int)(t / per_batch);
+    const int q = (int)(t % per_batch);
+    constexpr int G = 8;
+    const int span = G * this->tiles_n;
+    const int first_m = (q / span) * G;
+    const int gsize = min(this->tiles_m - first_m, G);
+    const int in_group = q % span;
+    r.m0 = (first_m + in_group % gsize) * PM;
+    r.n0 = (in_group / gsize) * 256;
+    return r;
+  }
+
+  __device__ Tile rank_tile(const Tile& t, int rank) const {
+    Tile r = t;
+    r.m0 += BM * rank;
+    return r;
+  }
+
+  __device__ void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
+                       uint32_t lbar, const Tile& t, int kb, int rank) const {
+    const int k0 = kb * BK;
+    const int m = t.m0 + BM * rank, n = t.n0 + 128 * rank;
+    if (!A_MN_) {
+      ptx::tma_load_3d_pair(sa, ta, lbar, k0, m, t.b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < BM / 32; ++j)
+        ptx::tma_load_3d_pair(sa + j * BK * 128, ta, lbar, m + 32 * j, k0, t.b);
+    }
+    if (!B_MN_) {
+      ptx::tma_load_3d_pair(sb, tb, lbar, k0, n, t.b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 128 / 32; ++j)
+        ptx::tma_load_3d_pair(sb + j * BK * 128, tb, lbar, n + 32 * j, k0, t.b);
+    }
   }
 };
 
@@ -292,11 +344,71 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   return after_launch(dev, "gemm_tf32 (umma_tf32_kernel)");
 }
 
+template <bool A_MN, bool B_MN>
+static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b, float* c,
+                               uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                               const GemmEpilogue& ep, cudaStream_t s) {
+  using P = GemmPairPolicy<A_MN, B_MN>;
+  using Cfg = umma::PairCfg<256>;
+  CUtensorMap ta, tb;
+  if (!A_MN)
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, true));
+  else
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, true));
+  if (B_MN)
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, true));
+  else
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, 128, false, true));
+  P pol;
+  pol.M = m; pol.N = n; pol.K = k;
+  pol.tiles_m = (int)ceil_div(m, P::PM);
+  pol.tiles_n = (int)ceil_div(n, 256);
+  pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
+  pol.C = c;
+  pol.c_batch = (long long)m * n;
+  pol.bias = ep.bias;
+  pol.resid = ep.resid;
+  pol.act = ep.act;
+  auto kern = umma::umma_tf32_pair_kernel<P>;
+  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+  const long long ctas = std::min<long long>(2 * pol.tiles, dev->sm_count & ~1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AGPU_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, pol, dev->d_status));
+  return after_launch(dev, "gemm_tf32 (umma_tf32_pair_kernel)");
+}
+
+// The CTA-pair kernel serves TF32 GEMMs with at least one full 256 x 256 tile;
+// AGPU_GEMM_PAIR=0 in the environment selects the single-CTA kernel instead.
+static bool use_pair(uint32_t m, uint32_t n) {
+  static const bool enabled = [] {
+    const char* e = getenv("AGPU_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return enabled && m >= 256 && n >= 256;
+}
+
 template <bool X3>
 static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at,
                                bool bt, const GemmEpilogue& ep, cudaStream_t s) {
   const bool wide = n > 128;
+  if (!X3 && use_pair(m, n)) {
+    if (!at && !bt) return run_tc_pair<false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (!at && bt) return run_tc_pair<false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (at && !bt) return run_tc_pair<true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    return run_tc_pair<true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+  }
   // B is MN-major unless stored transposed ([N,K]).
   if (wide) {
     if (!at && !bt) return run_tc<256, false, true, X3>(dev, a, b, c, batch, m, n, k, ep, s);
