@@ -20,10 +20,12 @@
 //      N tile = BN output channels; the epilogue adds the bias and writes
 //      NCHW rows (lanes = consecutive output pixels -> coalesced stores).
 #include <algorithm>
+#include <type_traits>
 
 #include "agpu_internal.cuh"
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
+#include "umma2_kernel.cuh"
 
 namespace agpu {
 
@@ -112,6 +114,41 @@ struct ConvPolicy {
         }
       }
     }
+  }
+};
+
+// CTA-pair conv tile: 256 output pixels (2*BH rows x BW columns) x BN output
+// channels; CTA `rank` stages rows oh0 + rank*BH .. of the pixels and weight
+// rows oc0 + rank*BN/2 .. of the tile.
+template <int BN_>
+struct ConvPairPolicy : ConvPolicy<BN_> {
+  using Base = ConvPolicy<BN_>;
+  using Tile = typename Base::Tile;
+
+  __device__ Tile tile(long long t) const {
+    Tile r;
+    r.oc0 = (int)(t % this->tiles_n) * BN_;
+    long long q = t / this->tiles_n;
+    r.ow0 = (int)(q % this->tiles_w) * this->BW;
+    q /= this->tiles_w;
+    r.oh0 = (int)(q % this->tiles_h) * 2 * this->BH;
+    r.n = (int)(q / this->tiles_h);
+    return r;
+  }
+
+  __device__ Tile rank_tile(const Tile& t, int rank) const {
+    Tile r = t;
+    r.oh0 += rank * this->BH;
+    return r;
+  }
+
+  __device__ void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
+                       uint32_t lbar, const Tile& t, int kb, int rank) const {
+    const int tap = kb / this->cblocks, cb = kb % this->cblocks;
+    const int kh = tap / this->KW, kw = tap % this->KW;
+    ptx::tma_load_4d_pair(sa, ta, lbar, cb * BK, t.ow0 + kw * this->dw - this->pw,
+                          t.oh0 + rank * this->BH + kh * this->dh - this->ph, t.n);
+    ptx::tma_load_3d_pair(sb, tb, lbar, tap * this->cw + cb * BK, t.oc0 + rank * (BN_ / 2), 0);
   }
 };
 
@@ -281,11 +318,11 @@ unsigned grid_for(const agpu_device* dev, long long work) {
   return (unsigned)std::max<long long>(1, std::min<long long>(want, (long long)dev->sm_count * 16));
 }
 
-template <int BN, bool X3>
+template <int BN, bool X3, bool PAIR>
 agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
                         const float* bias, float* y, cudaStream_t s) {
-  using P = ConvPolicy<BN>;
-  using Cfg = umma::Cfg<BN, X3>;
+  static_assert(!(X3 && PAIR), "the CTA-pair kernel is TF32 only");
+  using P = typename std::conditional<PAIR, ConvPairPolicy<BN>, ConvPolicy<BN>>::type;
   const int Cs = (p.cin + 3) / 4 * 4;
   const int Cw = (p.cin + BK - 1) / BK * BK;
   const uint64_t xs_elems = (uint64_t)p.n * p.h * p.w * Cs;
@@ -312,7 +349,7 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   pol.BW = bw;
   pol.BH = 128 / bw;
   pol.tiles_w = (int)ceil_div(p.wo, pol.BW);
-  pol.tiles_h = (int)ceil_div(p.ho, pol.BH);
+  pol.tiles_h = (int)ceil_div(p.ho, (PAIR ? 2 : 1) * pol.BH);
   pol.tiles_n = (int)ceil_div(p.cout, BN);
   pol.cblocks = Cw / BK;
   pol.taps = p.kh * p.kw;
@@ -341,15 +378,39 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     }
   }
   st = make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
-                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, BN, false, !X3);
+                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, PAIR ? BN / 2 : BN, false, !X3);
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
-  auto kern = umma::umma_tf32_kernel<P, X3>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Cfg::SMEM);
-  if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
-  const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
-  kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
-  st = after_launch(dev, "conv2d_tf32 (umma_tf32_kernel)");
+  if constexpr (PAIR) {
+    using Cfg = umma::PairCfg<BN>;
+    auto kern = umma::umma_tf32_pair_kernel<P>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM);
+    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<long long>(2 * pol.tiles, dev->sm_count & ~1), 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, pol, dev->d_status);
+    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv pair launch"); }
+    st = after_launch(dev, "conv2d_tf32 (umma_tf32_pair_kernel)");
+  } else {
+    using Cfg = umma::Cfg<BN, X3>;
+    auto kern = umma::umma_tf32_kernel<P, X3>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM);
+    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
+    const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
+    kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
+    st = after_launch(dev, "conv2d_tf32 (umma_tf32_kernel)");
+  }
   pool_free(dev, scratch, s);
   return st;
 }
@@ -358,10 +419,19 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
 template <bool X3>
 agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float* x,
                              const float* w, const float* bias, float* y, cudaStream_t s) {
-  if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3>(dev, p, x, w, bias, y, s);
-  if (p.cout >= 256) return run_conv_tc<256, X3>(dev, p, x, w, bias, y, s);
-  if (p.cout > 96) return run_conv_tc<128, X3>(dev, p, x, w, bias, y, s);
-  return run_conv_tc<64, X3>(dev, p, x, w, bias, y, s);
+  // TF32 convs with at least two 128-pixel tiles per image run on CTA pairs
+  constexpr bool PAIR = !X3;
+  if (PAIR && (long long)p.ho * p.wo >= 256) {
+    if (p.cout % 160 == 0 && p.cout % 256 != 0)
+      return run_conv_tc<160, X3, PAIR>(dev, p, x, w, bias, y, s);
+    if (p.cout >= 256) return run_conv_tc<256, X3, PAIR>(dev, p, x, w, bias, y, s);
+    if (p.cout > 96) return run_conv_tc<128, X3, PAIR>(dev, p, x, w, bias, y, s);
+    return run_conv_tc<64, X3, PAIR>(dev, p, x, w, bias, y, s);
+  }
+  if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3, false>(dev, p, x, w, bias, y, s);
+  if (p.cout >= 256) return run_conv_tc<256, X3, false>(dev, p, x, w, bias, y, s);
+  if (p.cout > 96) return run_conv_tc<128, X3, false>(dev, p, x, w, bias, y, s);
+  return run_conv_tc<64, X3, false>(dev, p, x, w, bias, y, s);
 }
 
 }  // namespace
