@@ -248,6 +248,17 @@ class GpuDevice:
         return self._new(_lib.load().agpu_group_norm_swish, x.handle, gamma.handle, beta.handle,
                          batch, channels, spatial, groups, C.c_float(eps))
 
+    def group_norm_backward(self, grad_out, x, gamma, batch: int, channels: int, spatial: int,
+                            groups: int, eps: float):
+        """Reference: `group_norm_backward(grad_out, input, gamma, batch, channels, spatial,
+        groups, eps) -> (d_input, d_gamma, d_beta)` (src/ops/norm.rs:282)."""
+        outs = [C.c_void_p() for _ in range(3)]
+        _check(_lib.load().agpu_group_norm_backward(self._h, grad_out.handle, x.handle,
+                                                    gamma.handle, batch, channels, spatial,
+                                                    groups, C.c_float(eps),
+                                                    *[C.byref(o) for o in outs]))
+        return tuple(GpuBuffer(o.value, self) for o in outs)
+
     # ---------------------------------------------------------------- sdpa --
     def scaled_dot_product_attention(self, q, k, v, batch_heads: int, seq_len: int,
                                      d_k: int) -> GpuBuffer:
@@ -354,6 +365,12 @@ class GpuDevice:
                                               batch, in_c, in_h, in_w, out_c, kh, kw, stride_h,
                                               stride_w, pad_h, pad_w, dil_h, dil_w, groups,
                                               stream or None))
+
+    def launch_group_norm_backward(self, dy_ptr, x_ptr, g_ptr, dx_ptr, dg_ptr, db_ptr, batch,
+                                   channels, spatial, groups, eps, stream=0):
+        _check(_lib.load().agpu_launch_group_norm_backward(
+            self._h, dy_ptr, x_ptr, g_ptr, dx_ptr, dg_ptr, db_ptr, batch, channels, spatial,
+            groups, C.c_float(eps), stream))
 
     def launch_group_norm(self, x_ptr, g_ptr, b_ptr, y_ptr, batch, channels, spatial, groups,
                           eps, swish=False, stream: int = 0) -> None:

@@ -53,6 +53,8 @@ SIGNATURES: dict[str, tuple] = {
                                    P_buf]),
     "agpu_group_norm_swish": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, u32, f32,
                                          P_buf]),
+    "agpu_group_norm_backward": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, u32, f32,
+                                            P_buf, P_buf, P_buf]),
     "agpu_scaled_dot_product_attention": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32,
                                                      P_buf]),
     "agpu_sdpa_causal": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, P_buf]),
@@ -81,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_group_norm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
                                           C.c_void_p, u32, u32, u32, u32, f32, i32,
                                           C.c_void_p]),
+    "agpu_launch_group_norm_backward": (c_status, [c_dev] + [C.c_void_p] * 6 +
+                                        [u32, u32, u32, u32, f32, C.c_void_p]),
     "agpu_launch_sdpa": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32, u32, u32, i32,
                                                                  C.c_void_p]),
     "agpu_launch_gemm_ex": (c_status, [c_dev] + [C.c_void_p] * 3 + [u32] * 4 + [i32, i32]

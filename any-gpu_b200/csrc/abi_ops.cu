@@ -286,6 +286,49 @@ extern "C" agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer
                          "group_norm_swish");
 }
 
+extern "C" agpu_status agpu_group_norm_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                                const agpu_buffer* input,
+                                                const agpu_buffer* gamma, uint32_t batch,
+                                                uint32_t channels, uint32_t spatial,
+                                                uint32_t groups, float eps,
+                                                agpu_buffer** d_input, agpu_buffer** d_gamma,
+                                                agpu_buffer** d_beta) {
+  const char* fn = "group_norm_backward";
+  if (!dev) return fail(AGPU_ERR_INVALID, "%s: NULL device", fn);
+  if (!grad_out || !input || !gamma) return fail(AGPU_ERR_INVALID, "%s: input is NULL", fn);
+  if (!d_input || !d_gamma || !d_beta) return fail(AGPU_ERR_INVALID, "%s: out is NULL", fn);
+  *d_input = *d_gamma = *d_beta = nullptr;
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  // src/ops/norm.rs:291-294
+  const uint64_t total = (uint64_t)batch * channels * spatial;
+  if (input->len != total || grad_out->len != total)
+    return fail(AGPU_ERR_SHAPE, "%s: input/grad_out must have %llu elems (got %llu, %llu)", fn,
+                (unsigned long long)total, (unsigned long long)input->len,
+                (unsigned long long)grad_out->len);
+  if (gamma->len != channels)
+    return fail(AGPU_ERR_SHAPE, "%s: gamma must have %u elems", fn, channels);
+  if (groups == 0 || channels % groups != 0)
+    return fail(AGPU_ERR_SHAPE, "%s: channels must be divisible by groups", fn);
+  agpu_buffer *di = nullptr, *dg = nullptr, *db = nullptr;
+  agpu_status st = new_buffer(dev, total, &di);
+  if (st == AGPU_OK) st = new_buffer(dev, channels, &dg);
+  if (st == AGPU_OK) st = new_buffer(dev, channels, &db);
+  if (st == AGPU_OK)
+    st = launch_group_norm_backward(dev, grad_out->dptr, input->dptr, gamma->dptr, di->dptr,
+                                    dg->dptr, db->dptr, batch, channels, spatial, groups, eps,
+                                    dev->stream);
+  if (st != AGPU_OK) {
+    if (di) agpu_buffer_free(di);
+    if (dg) agpu_buffer_free(dg);
+    if (db) agpu_buffer_free(db);
+    return st;
+  }
+  *d_input = di;
+  *d_gamma = dg;
+  *d_beta = db;
+  return AGPU_OK;
+}
+
 // --------------------------------------------------------- gemm epilogue --
 extern "C" agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
                                     const agpu_buffer* bias, const agpu_buffer* resid,
@@ -500,6 +543,18 @@ agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float
     return fail(AGPU_ERR_SHAPE, "launch_group_norm: channels must be divisible by groups");
   return launch_group_norm(dev, x, gamma, beta, y, batch, channels, spatial, groups, eps,
                            apply_swish != 0, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_group_norm_backward(agpu_device* dev, const float* grad_out,
+                                            const float* input, const float* gamma,
+                                            float* d_input, float* d_gamma, float* d_beta,
+                                            uint32_t batch, uint32_t channels, uint32_t spatial,
+                                            uint32_t groups, float eps, void* stream) {
+  CHECK_DEV(dev, "launch_group_norm_backward");
+  if (groups == 0 || channels % groups != 0)
+    return fail(AGPU_ERR_SHAPE, "launch_group_norm_backward: channels must be divisible by groups");
+  return launch_group_norm_backward(dev, grad_out, input, gamma, d_input, d_gamma, d_beta, batch,
+                                    channels, spatial, groups, eps, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k, const float* v,

@@ -100,6 +100,11 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
                               const float* beta, float* y, uint32_t batch, uint32_t channels,
                               uint32_t spatial, uint32_t groups, float eps, bool swish,
                               cudaStream_t s);
+agpu_status launch_group_norm_backward(agpu_device* dev, const float* dy, const float* x,
+                                       const float* gamma, float* dx, float* dgamma,
+                                       float* dbeta, uint32_t batch, uint32_t channels,
+                                       uint32_t spatial, uint32_t groups, float eps,
+                                       cudaStream_t s);
 
 agpu_status launch_rmsnorm(agpu_device* dev, const float* x, const float* w, float* y,
                            uint64_t rows, uint32_t cols, float eps, cudaStream_t s);

@@ -20,6 +20,7 @@
 //      N tile = BN output channels; the epilogue adds the bias and writes
 //      NCHW rows (lanes = consecutive output pixels -> coalesced stores).
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "agpu_internal.cuh"
@@ -118,8 +119,8 @@ struct ConvPolicy {
 };
 
 // CTA-pair conv tile: 256 output pixels (2*BH rows x BW columns) x BN output
-// channels; CTA `rank` stages rows oh0 + rank*BH .. of the pixels and weight
-// rows oc0 + rank*BN/2 .. of the tile.
+// channels; CTA `rank` stages rows oh0 + rank*BH .. of the pixels and, per MMA
+// sub-block s (two for BN > 256), weight rows oc0 + s*MMA_N + rank*MMA_N/2 ..
 template <int BN_>
 struct ConvPairPolicy : ConvPolicy<BN_> {
   using Base = ConvPolicy<BN_>;
@@ -148,7 +149,11 @@ struct ConvPairPolicy : ConvPolicy<BN_> {
     const int kh = tap / this->KW, kw = tap % this->KW;
     ptx::tma_load_4d_pair(sa, ta, lbar, cb * BK, t.ow0 + kw * this->dw - this->pw,
                           t.oh0 + rank * this->BH + kh * this->dh - this->ph, t.n);
-    ptx::tma_load_3d_pair(sb, tb, lbar, tap * this->cw + cb * BK, t.oc0 + rank * (BN_ / 2), 0);
+    constexpr int HALF = umma::PairCfg<BN_>::MMA_N / 2;
+#pragma unroll
+    for (int sub = 0; sub < umma::PairCfg<BN_>::NMMA; ++sub)
+      ptx::tma_load_3d_pair(sb + sub * HALF * 128, tb, lbar, tap * this->cw + cb * BK,
+                            t.oc0 + sub * 2 * HALF + rank * HALF, 0);
   }
 };
 
@@ -184,6 +189,24 @@ __global__ void weight_khwc_kernel(const float* __restrict__ w, float* __restric
     const int kh = (int)(r % KH);
     const int oc = (int)(r / KH);
     w2[i] = c < Cin ? w[(((long long)oc * Cin + c) * KH + kh) * KW + kw] : 0.0f;
+  }
+}
+
+// Same relayout, one CTA per output channel: the channel's Cin*KH*KW weights
+// are read contiguously into shared memory and written tap-major, so both the
+// reads and the writes are coalesced.
+__global__ void __launch_bounds__(256) weight_khwc_smem_kernel(const float* __restrict__ w,
+                                                              float* __restrict__ w2, int Cin,
+                                                              int taps, int Cw) {
+  extern __shared__ float row[];  // [Cin][taps]
+  const int oc = blockIdx.x;
+  const float* src = w + (long long)oc * Cin * taps;
+  for (int i = threadIdx.x; i < Cin * taps; i += blockDim.x) row[i] = __ldg(src + i);
+  __syncthreads();
+  float* dst = w2 + (long long)oc * taps * Cw;
+  for (int i = threadIdx.x; i < taps * Cw; i += blockDim.x) {
+    const int t = i / Cw, c = i % Cw;
+    dst[i] = c < Cin ? row[c * taps + t] : 0.0f;
   }
 }
 
@@ -334,8 +357,12 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   {
     dim3 grid((unsigned)ceil_div((uint64_t)p.h * p.w, 32), (unsigned)ceil_div(Cs, 32), p.n);
     nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xs, p.cin, p.h * p.w, Cs);
-    weight_khwc_kernel<<<grid_for(dev, (long long)w2_elems), 256, 0, s>>>(w, w2, p.cout, p.cin,
-                                                                          p.kh, p.kw, Cw);
+    const int taps = p.kh * p.kw;
+    if ((long long)p.cin * taps * 4 <= 48 * 1024)
+      weight_khwc_smem_kernel<<<p.cout, 256, p.cin * taps * 4, s>>>(w, w2, p.cin, taps, Cw);
+    else
+      weight_khwc_kernel<<<grid_for(dev, (long long)w2_elems), 256, 0, s>>>(w, w2, p.cout,
+                                                                            p.cin, p.kh, p.kw, Cw);
   }
   agpu_status st = after_launch(dev, "conv staging kernels", 2);
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
@@ -378,7 +405,8 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     }
   }
   st = make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
-                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK, PAIR ? BN / 2 : BN, false, !X3);
+                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK,
+                        PAIR ? umma::PairCfg<BN>::MMA_N / 2 : BN, false, !X3);
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
   if constexpr (PAIR) {
     using Cfg = umma::PairCfg<BN>;
@@ -419,14 +447,24 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
 template <bool X3>
 agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float* x,
                              const float* w, const float* bias, float* y, cudaStream_t s) {
-  // TF32 convs with at least two 128-pixel tiles per image run on CTA pairs
+  // TF32 convs with at least two 128-pixel tiles per image run on CTA pairs;
+  // output-channel counts that are multiples of 320 take 256 x 320 tiles (two
+  // MMAs of N 160: fewer TMA bytes per FLOP than 256 x 160).
+  // AGPU_CONV_WIDE=0 keeps them on 256 x 160 tiles.
   constexpr bool PAIR = !X3;
-  if (PAIR && (long long)p.ho * p.wo >= 256) {
-    if (p.cout % 160 == 0 && p.cout % 256 != 0)
-      return run_conv_tc<160, X3, PAIR>(dev, p, x, w, bias, y, s);
-    if (p.cout >= 256) return run_conv_tc<256, X3, PAIR>(dev, p, x, w, bias, y, s);
-    if (p.cout > 96) return run_conv_tc<128, X3, PAIR>(dev, p, x, w, bias, y, s);
-    return run_conv_tc<64, X3, PAIR>(dev, p, x, w, bias, y, s);
+  static const bool wide = [] {
+    const char* e = getenv("AGPU_CONV_WIDE");
+    return !(e && e[0] == '0');
+  }();
+  if constexpr (PAIR) {
+    if ((long long)p.ho * p.wo >= 256) {
+      if (wide && p.cout % 320 == 0) return run_conv_tc<320, X3, true>(dev, p, x, w, bias, y, s);
+      if (p.cout % 160 == 0 && p.cout % 256 != 0)
+        return run_conv_tc<160, X3, true>(dev, p, x, w, bias, y, s);
+      if (p.cout >= 256) return run_conv_tc<256, X3, true>(dev, p, x, w, bias, y, s);
+      if (p.cout > 96) return run_conv_tc<128, X3, true>(dev, p, x, w, bias, y, s);
+      return run_conv_tc<64, X3, true>(dev, p, x, w, bias, y, s);
+    }
   }
   if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3, false>(dev, p, x, w, bias, y, s);
   if (p.cout >= 256) return run_conv_tc<256, X3, false>(dev, p, x, w, bias, y, s);

@@ -150,13 +150,16 @@ struct GemmPolicy {
   }
 };
 
-// CTA-pair GEMM tile: 256 x 256; CTA `rank` of the pair stages rows
-// m0 + 128*rank .. +127 of A and columns n0 + 128*rank .. +127 of B.
-template <bool A_MN_, bool B_MN_>
-struct GemmPairPolicy : GemmPolicy<256, A_MN_, B_MN_> {
-  using Base = GemmPolicy<256, A_MN_, B_MN_>;
+// CTA-pair GEMM tile: 256 x BN (BN = 256, or 512 as two MMAs of N 256);
+// CTA `rank` of the pair stages rows m0 + 128*rank .. +127 of A and, per
+// MMA sub-block s, columns n0 + s*MMA_N + rank*MMA_N/2 .. of B.
+template <int BN_, bool A_MN_, bool B_MN_>
+struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
+  using Base = GemmPolicy<BN_, A_MN_, B_MN_>;
   using Tile = typename Base::Tile;
+  using Cfg = umma::PairCfg<BN_>;
   static constexpr int PM = 2 * BM;  // tile rows of the pair
+  static constexpr int HALF = Cfg::MMA_N / 2;  // B columns per CTA per sub-block
 
   __device__ Tile tile(long long t) const {
     const long long per_batch = (long long)this->tiles_m * this->tiles_n;
@@ -169,7 +172,7 @@ struct GemmPairPolicy : GemmPolicy<256, A_MN_, B_MN_> {
     const int gsize = min(this->tiles_m - first_m, G);
     const int in_group = q % span;
     r.m0 = (first_m + in_group % gsize) * PM;
-    r.n0 = (in_group / gsize) * 256;
+    r.n0 = (in_group / gsize) * BN_;
     return r;
   }
 
@@ -182,7 +185,7 @@ struct GemmPairPolicy : GemmPolicy<256, A_MN_, B_MN_> {
   __device__ void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
                        uint32_t lbar, const Tile& t, int kb, int rank) const {
     const int k0 = kb * BK;
-    const int m = t.m0 + BM * rank, n = t.n0 + 128 * rank;
+    const int m = t.m0 + BM * rank;
     if (!A_MN_) {
       ptx::tma_load_3d_pair(sa, ta, lbar, k0, m, t.b);
     } else {
@@ -190,12 +193,17 @@ struct GemmPairPolicy : GemmPolicy<256, A_MN_, B_MN_> {
       for (int j = 0; j < BM / 32; ++j)
         ptx::tma_load_3d_pair(sa + j * BK * 128, ta, lbar, m + 32 * j, k0, t.b);
     }
-    if (!B_MN_) {
-      ptx::tma_load_3d_pair(sb, tb, lbar, k0, n, t.b);
-    } else {
 #pragma unroll
-      for (int j = 0; j < 128 / 32; ++j)
-        ptx::tma_load_3d_pair(sb + j * BK * 128, tb, lbar, n + 32 * j, k0, t.b);
+    for (int sub = 0; sub < Cfg::NMMA; ++sub) {
+      const int n = t.n0 + sub * Cfg::MMA_N + HALF * rank;
+      if (!B_MN_) {
+        ptx::tma_load_3d_pair(sb + sub * HALF * 128, tb, lbar, k0, n, t.b);
+      } else {
+#pragma unroll
+        for (int j = 0; j < HALF / 32; ++j)
+          ptx::tma_load_3d_pair(sb + (sub * (HALF / 32) + j) * BK * 128, tb, lbar, n + 32 * j,
+                                k0, t.b);
+      }
     }
   }
 };
@@ -344,12 +352,12 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   return after_launch(dev, "gemm_tf32 (umma_tf32_kernel)");
 }
 
-template <bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN>
 static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                const GemmEpilogue& ep, cudaStream_t s) {
-  using P = GemmPairPolicy<A_MN, B_MN>;
-  using Cfg = umma::PairCfg<256>;
+  using P = GemmPairPolicy<BN, A_MN, B_MN>;
+  using Cfg = umma::PairCfg<BN>;
   CUtensorMap ta, tb;
   if (!A_MN)
     AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, true));
@@ -358,11 +366,11 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   if (B_MN)
     AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, true));
   else
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, 128, false, true));
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, P::HALF, false, true));
   P pol;
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, P::PM);
-  pol.tiles_n = (int)ceil_div(n, 256);
+  pol.tiles_n = (int)ceil_div(n, BN);
   pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
   pol.C = c;
   pol.c_batch = (long long)m * n;
@@ -398,16 +406,49 @@ static bool use_pair(uint32_t m, uint32_t n) {
   return enabled && m >= 256 && n >= 256;
 }
 
+// 256 x 512 pair tiles move a third fewer TMA bytes per FLOP than 256 x 256
+// but have half as many tiles and a single-buffered accumulator, so the
+// tensor core idles while a tile's 128 x 512 fp32 per CTA drains (about
+// 12k SM cycles when every SM writes at once, against 46 cycles per unit of
+// K of MMA work).  Take them when the estimated throughput -- tile-wave fill
+// x column fill x that drain factor x the kernel efficiency measured for
+// each width (0.99 wide at 8192^3, 0.88 for 256 x 256) -- is higher.
+// AGPU_GEMM_WIDE=0 disables them.
+static bool use_wide(const agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n,
+                     uint32_t k) {
+  static const bool enabled = [] {
+    const char* e = getenv("AGPU_GEMM_WIDE");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || n < 512) return false;
+  const long long pairs = std::max(1, dev->sm_count / 2);
+  const long long tm = ceil_div(m, 256);
+  auto score = [&](long long bn, double eff) {
+    const long long tn = ceil_div(n, bn);
+    const long long tiles = tm * tn * batch;
+    const double waves = (double)tiles / (double)(ceil_div(tiles, pairs) * pairs);
+    return eff * waves * (double)n / (double)(tn * bn);
+  };
+  const double mma = 46.4 * (double)k, drain = 12000.0;
+  return score(512, 0.99 * mma / (mma + drain)) > score(256, 0.88);
+}
+
 template <bool X3>
 static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at,
                                bool bt, const GemmEpilogue& ep, cudaStream_t s) {
   const bool wide = n > 128;
   if (!X3 && use_pair(m, n)) {
-    if (!at && !bt) return run_tc_pair<false, true>(dev, a, b, c, batch, m, n, k, ep, s);
-    if (!at && bt) return run_tc_pair<false, false>(dev, a, b, c, batch, m, n, k, ep, s);
-    if (at && !bt) return run_tc_pair<true, true>(dev, a, b, c, batch, m, n, k, ep, s);
-    return run_tc_pair<true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (use_wide(dev, batch, m, n, k)) {
+      if (!at && !bt) return run_tc_pair<512, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (!at && bt) return run_tc_pair<512, false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (at && !bt) return run_tc_pair<512, true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+      return run_tc_pair<512, true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    }
+    if (!at && !bt) return run_tc_pair<256, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (!at && bt) return run_tc_pair<256, false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (at && !bt) return run_tc_pair<256, true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    return run_tc_pair<256, true, false>(dev, a, b, c, batch, m, n, k, ep, s);
   }
   // B is MN-major unless stored transposed ([N,K]).
   if (wide) {

@@ -67,16 +67,32 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: for barriers that threads of the
+// other CTA of a pair arrive on (release.cluster), so their writes before the
+// arrive are visible after the wait.
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // writes `code` into *status) if it did not within the time limit, or if
 // another thread of the CTA already flagged an abort in *abort_flag.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned int* status, unsigned int code,
                                           volatile int* abort_flag) {
-  if (mbar_test(bar, parity)) return true;
+  if (CLUSTER ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
   unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_test(bar, parity)) return true;
+    if (CLUSTER ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
@@ -125,6 +141,32 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
   asm volatile(
       "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(m),
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Store two floats into a peer CTA's shared memory (cluster address from
+// mapa) and count their 8 bytes on the peer's mbarrier (also a cluster
+// address): an exchange that needs no cluster-wide memory fence.
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float a, float b,
+                                            uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+      ::"r"(cluster_addr), "f"(a), "f"(b), "r"(cluster_bar)
+      : "memory");
+}
+
+// Named barrier over `count` threads (a multiple of 32), id 1..15.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Plain (untiled) bulk copy global -> this CTA's shared memory, completion
+// counted in bytes on `bar`.  Both addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -292,6 +334,16 @@ __device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d_tmem, uint64_t adesc
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D(tmem, both CTAs) (+)= A(tmem, 128 rows per CTA) * B(smem, N/2 per CTA).
+__device__ __forceinline__ void mma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive (once all prior MMAs of the pair completed) on the mbarrier at the

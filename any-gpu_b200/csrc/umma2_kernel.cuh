@@ -27,9 +27,19 @@
 namespace agpu {
 namespace umma {
 
+// Tiles wider than one MMA (BN > 256) issue NMMA = 2 MMAs of N = BN/2 per K
+// step into adjacent TMEM columns; B is then staged as NMMA sub-blocks of
+// MMA_N/2 columns per CTA (sub-block s of CTA r = tile columns
+// s*MMA_N + r*MMA_N/2 ..).  An accumulator of 2*BN > 512 columns cannot be
+// double-buffered: the MMA then waits for the epilogue between tiles, which
+// the wider tile amortises (and it halves the TMA bytes per FLOP of B).
 template <int BN_>
 struct PairCfg {
   static constexpr int BN = BN_;             // tile columns (both CTAs)
+  static constexpr int NMMA = BN > 256 ? 2 : 1;
+  static constexpr int MMA_N = BN / NMMA;
+  static constexpr int ACC = 2 * BN <= 512 ? 2 : 1;      // accumulator buffers
+  static_assert(BN % NMMA == 0 && MMA_N % 16 == 0 && MMA_N <= 256, "pair tile width");
   static constexpr int A_BYTES = BM * BK * 4;            // 128 rows per CTA
   static constexpr int B_BYTES = (BN / 2) * BK * 4;      // BN/2 columns per CTA
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -40,7 +50,7 @@ struct PairCfg {
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int RING_BYTES = STAGE_BYTES * STAGES;
   static constexpr int SMEM = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = ACC * BN <= 256 ? 256 : 512;
   static constexpr int THREADS = 192;
 };
 
@@ -48,6 +58,7 @@ struct PairCfg {
 //   void load(ta, tb, sa, sb, uint32_t leader_bar, const Tile&, int kb, int rank) const;
 //       issues this CTA's STAGE_BYTES with tma_load_*_pair(..., leader_bar, ...)
 //   Tile rank_tile(const Tile&, int rank) const;   // the CTA's 128-row half
+// and, for BN > 256, the B sub-block layout described at PairCfg.
 template <class P>
 __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     umma_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -138,14 +149,16 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = ptx::make_idesc_tf32(2 * BM, BN, P::A_MN, P::B_MN);
+      constexpr uint32_t idesc = ptx::make_idesc_tf32(2 * BM, C::MMA_N, P::A_MN, P::B_MN);
+      // byte offset of B sub-block s in a stage (MN-major: 32-column chunks)
+      constexpr uint32_t b_sub = P::B_MN ? (C::MMA_N / 2 / 32) * BK * 128 : (C::MMA_N / 2) * 128;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       for (long long t = cluster_id; t < num_tiles && ok; t += n_clusters, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = local % C::ACC;
+        const uint32_t acc_phase = (local / C::ACC) & 1;
         if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, status, 0x302, abort_flag)) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -158,9 +171,12 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t a_off = P::A_MN ? kk * 1024 : kk * 32;
             const uint32_t b_off = P::B_MN ? kk * 1024 : kk * 32;
-            ptx::mma_tf32_ss_pair(d_tmem, operand_desc<P::A_MN>(a_addr + a_off),
-                                  operand_desc<P::B_MN>(b_addr + b_off), idesc,
-                                  (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int sub = 0; sub < C::NMMA; ++sub)
+              ptx::mma_tf32_ss_pair(d_tmem + sub * C::MMA_N,
+                                    operand_desc<P::A_MN>(a_addr + a_off),
+                                    operand_desc<P::B_MN>(b_addr + sub * b_sub + b_off), idesc,
+                                    (kb > 0 || kk > 0) ? 1u : 0u);
           }
           ptx::mma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -177,8 +193,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     int local = 0;
     for (long long t = cluster_id; t < num_tiles; t += n_clusters, ++local) {
       const auto tile = pol.rank_tile(pol.tile(t), rank);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = local % C::ACC;
+      const uint32_t acc_phase = (local / C::ACC) & 1;
       if (!ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x305, abort_flag)) break;
       ptx::tc_fence_after();
 #pragma unroll 1

@@ -189,7 +189,7 @@ class BmmSoftmax(Workload):
         super().__init__(args, rank)
         self.B, self.M, self.N, self.K = args.batch, 2048, 2048, 2048
         self.flops = self.dom_flops = 2.0 * self.B * self.M * self.N * self.K
-        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256, K-major A, MN-major B>>"
+        self.dom_kernel = "umma_tf32_pair_kernel<GemmPairPolicy<K-major A, MN-major B>> (256x256 CTA-pair tiles)"
 
     def config(self):
         return {"workload": "batch_matmul+softmax", "batch": self.B, "m": self.M, "n": self.N,
@@ -262,7 +262,7 @@ class Matmul(Workload):
         super().__init__(args, rank)
         self.n = args.size
         self.flops = self.dom_flops = 2.0 * self.n ** 3
-        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256|128, K-major A, MN-major B>>"
+        self.dom_kernel = "umma_tf32_pair_kernel<GemmPairPolicy> (m, n >= 256) or umma_tf32_kernel<GemmPolicy<256|128>>"
         ws = 3 * self.n * self.n * 4
         self.l2 = (f"working set {ws / 2**20:.1f} MiB "
                    + ("> 126 MB L2" if ws > 126e6 else "fits in L2: inputs re-read from L2"))
@@ -385,7 +385,7 @@ class Unet(Workload):
         super().__init__(args, rank)
         self.n, self.c, self.h, self.w, self.g = args.images, 320, 64, 64, 32
         self.flops = self.dom_flops = 2.0 * self.n * self.c * self.h * self.w * self.c * 9
-        self.dom_kernel = "umma_tf32_kernel<ConvPolicy<160>> (implicit-GEMM conv2d)"
+        self.dom_kernel = "umma_tf32_pair_kernel<ConvPairPolicy<160>> (implicit-GEMM conv2d)"
 
     def config(self):
         return {"workload": "unet_block conv2d3x3->group_norm->swish", "n": self.n,
@@ -469,7 +469,7 @@ class Llama(Workload):
         dm = self.dims
         self.flops = dm.gemm_flops() + dm.attention_flops()
         self.dom_flops = 2.0 * dm.tokens * dm.d_model * 2 * dm.ffn
-        self.dom_kernel = "umma_tf32_kernel<GemmPolicy<256, K-major A, MN-major B>> (gate/up)"
+        self.dom_kernel = "umma_tf32_pair_kernel<GemmPairPolicy<K-major A, MN-major B>> (gate/up)"
 
     def config(self):
         dm = self.dims

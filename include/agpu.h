@@ -190,6 +190,18 @@ AGPU_API agpu_status agpu_group_norm_swish(agpu_device* dev, const agpu_buffer* 
                                            uint32_t batch, uint32_t channels, uint32_t spatial,
                                            uint32_t groups, float eps, agpu_buffer** out);
 
+/* GpuDevice::group_norm_backward (src/ops/norm.rs:282-438): gradients of
+ * group_norm with respect to its input, gamma and beta, statistics recomputed
+ * from `input`.  d_input [batch, channels, spatial], d_gamma and d_beta
+ * [channels] are new buffers.  Size mismatches and channels % groups != 0
+ * -> AGPU_ERR_SHAPE (src/ops/norm.rs:291-294). */
+AGPU_API agpu_status agpu_group_norm_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                              const agpu_buffer* input, const agpu_buffer* gamma,
+                                              uint32_t batch, uint32_t channels,
+                                              uint32_t spatial, uint32_t groups, float eps,
+                                              agpu_buffer** d_input, agpu_buffer** d_gamma,
+                                              agpu_buffer** d_beta);
+
 /* ------------------------------------------------------------- sdpa ------- */
 /* GpuDevice::scaled_dot_product_attention (src/ops/attention.rs:149-169):
  * softmax(Q K^T / sqrt(d_k)) V per head, non-causal; Q, K, V, out are
@@ -278,6 +290,12 @@ AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, co
                                             const float* beta, float* y, uint32_t batch,
                                             uint32_t channels, uint32_t spatial, uint32_t groups,
                                             float eps, int apply_swish, void* stream);
+AGPU_API agpu_status agpu_launch_group_norm_backward(agpu_device* dev, const float* grad_out,
+                                                     const float* input, const float* gamma,
+                                                     float* d_input, float* d_gamma,
+                                                     float* d_beta, uint32_t batch,
+                                                     uint32_t channels, uint32_t spatial,
+                                                     uint32_t groups, float eps, void* stream);
 AGPU_API agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k,
                                       const float* v, float* out, uint32_t batch_heads,
                                       uint32_t seq_len, uint32_t d_k, int causal, void* stream);

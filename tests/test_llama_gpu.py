@@ -74,7 +74,7 @@ def test_gemm_fused_epilogue(dev, orc, prec, tol, act):
 def test_sdpa_strided_packed_qkv(dev, orc):
     """Q, K, V read in place from a packed [B, S, 3, H, D] projection, output
     written as [B, S, H, D] (the layer's layout) -- tensor-core and SIMT paths."""
-    for (B, S, H, D) in [(2, 200, 3, 128), (1, 70, 2, 64), (2, 9, 2, 16)]:
+    for (B, S, H, D) in [(2, 200, 3, 128), (2, 300, 2, 128), (1, 70, 2, 64), (2, 9, 2, 16)]:
         r = np.random.default_rng(S)
         qkv = r.standard_normal(B * S * 3 * H * D).astype(np.float32)
         Q = dev.upload(qkv)

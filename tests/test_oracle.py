@@ -142,3 +142,29 @@ def test_oracle_rmsnorm_rope(orc):
     X = xr.reshape(3, 2, 8)
     np.testing.assert_allclose(y[..., :4] ** 2 + y[..., 4:] ** 2,
                                X[..., :4] ** 2 + X[..., 4:] ** 2, rtol=1e-5)
+
+
+def gn_backward_f64(dy, x, gamma, n, c, s, g, eps):
+    """Gradients of group_norm from torch autograd in float64: an implementation
+    independent of the reference's shaders (which have no tests of their own)."""
+    import torch
+    X = torch.tensor(np.asarray(x, np.float64).reshape(n, c, s), requires_grad=True)
+    G = torch.tensor(np.asarray(gamma, np.float64), requires_grad=True)
+    B = torch.zeros(c, dtype=torch.float64, requires_grad=True)
+    Y = torch.nn.functional.group_norm(X, g, G, B, eps)
+    Y.backward(torch.tensor(np.asarray(dy, np.float64).reshape(n, c, s)))
+    return X.grad.numpy().ravel(), G.grad.numpy(), B.grad.numpy()
+
+
+@pytest.mark.parametrize("n,c,s,g", [(2, 4, 3, 2), (2, 6, 37, 3), (1, 8, 64, 1)])
+def test_oracle_group_norm_backward_vs_autograd(orc, n, c, s, g):
+    """The oracle's restatement of SHADER_GN_BACK_* (src/ops/norm.rs:97-205)
+    against torch autograd in float64."""
+    r = np.random.default_rng(n * 100 + s)
+    x = r.standard_normal(n * c * s).astype(np.float32)
+    dy = r.standard_normal(n * c * s).astype(np.float32)
+    gamma = (1 + 0.2 * r.standard_normal(c)).astype(np.float32)
+    got = orc.group_norm_backward(dy, x, gamma, n, c, s, g, 1e-5)
+    want = gn_backward_f64(dy, x, gamma, n, c, s, g, 1e-5)
+    for a, b in zip(got, want):
+        assert orc.rel_fro(a, b) <= 1e-4

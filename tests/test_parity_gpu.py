@@ -196,7 +196,9 @@ def _gn64(x, gamma, beta, n, c, s, g, eps):
 
 
 @pytest.mark.parametrize("swish", [False, True])
-@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block (cluster of 4 CTAs)
+@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block (5 CTAs x 8 float4)
+                                     (2, 40, 4096, 8),       # 5 CTAs x 4 float4 per thread
+                                     (1, 64, 4096, 2),       # 8 CTAs x 16 float4 per thread
                                      (2, 64, 1024, 32),      # 2 channels x 1024 per group
                                      (3, 12, 37, 4),         # spatial % 4 != 0: chunked path
                                      (1, 4, 300000, 2),      # 600k-element groups: chunked
@@ -220,6 +222,45 @@ def test_group_norm_parity(dev, orc, n, c, s, g, swish):
     err_orc = orc.rel_fro(want, ref64)
     assert orc.rel_fro(got, ref64) <= max(1e-5, err_orc)
     assert orc.rel_fro(got, want) <= 1e-5 + err_orc
+
+
+@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block shape
+                                     (1, 4, 10000, 2),       # rows of 3 chunks (4096 each)
+                                     (3, 12, 37, 4),         # ragged rows
+                                     (2, 64, 1, 32),         # one element per row
+                                     (2, 6, 8, 6)])          # per-channel groups
+def test_group_norm_backward_parity(dev, orc, n, c, s, g):
+    """group_norm_backward (src/ops/norm.rs:282) against the oracle's
+    restatement of the reference shaders and against torch autograd in
+    float64; the GPU must be within 1e-5 of float64 or as close as the
+    oracle (the shaders' E[x^2]-mean^2 and sequential fp32 sums drift)."""
+    from test_oracle import gn_backward_f64
+    r = np.random.default_rng(n * c + s + 7)
+    x = r.standard_normal(n * c * s).astype(np.float32)
+    dy = r.standard_normal(n * c * s).astype(np.float32)
+    gamma = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    outs = dev.group_norm_backward(dev.upload(dy), dev.upload(x), dev.upload(gamma), n, c, s, g,
+                                   1e-5)
+    got = [dev.read(o) for o in outs]
+    want = orc.group_norm_backward(dy, x, gamma, n, c, s, g, 1e-5)
+    ref = gn_backward_f64(dy, x, gamma, n, c, s, g, 1e-5)
+    for name, a, b, f in zip(("d_input", "d_gamma", "d_beta"), got, want, ref):
+        err_orc = orc.rel_fro(b, f)
+        assert orc.rel_fro(a, f) <= max(1e-5, err_orc), name
+        assert orc.rel_fro(a, b) <= 1e-5 + err_orc, name
+
+
+def test_group_norm_backward_errors(dev):
+    from any_gpu import AnyGpuError
+    ones = lambda k: dev.upload(np.ones(k, np.float32))
+    cases = [((ones(16), ones(10), ones(4)), (1, 4, 4, 2)),   # input size mismatch
+             ((ones(10), ones(16), ones(4)), (1, 4, 4, 2)),   # grad_out size mismatch
+             ((ones(16), ones(16), ones(3)), (1, 4, 4, 2)),   # gamma size
+             ((ones(5), ones(5), ones(5)), (1, 5, 1, 2))]     # channels % groups
+    for (go, x, gm), args in cases:
+        with pytest.raises(AnyGpuError) as e:
+            dev.group_norm_backward(go, x, gm, *args, 1e-5)
+        assert e.value.status == 1
 
 
 def test_group_norm_errors(dev):
@@ -328,7 +369,7 @@ def _attn64(q, k, v, bh, s, d, causal=False, rows=None):
 
 
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("bh,s,d", [(4, 256, 128), (2, 200, 64), (3, 64, 128), (2, 333, 128),
+@pytest.mark.parametrize("bh,s,d", [(4, 256, 128), (2, 200, 64), (3, 64, 128), (6, 128, 128), (2, 333, 128),
                                     (1, 1000, 64), (5, 7, 16), (2, 65, 32)])
 def test_sdpa_parity(dev, orc, bh, s, d, causal):
     """Tensor-core flash kernel (d 64/128) and the SIMT kernel (other d) against
