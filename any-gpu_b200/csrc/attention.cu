@@ -503,10 +503,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // and S runs at N = 128, the tensor core's full-rate width (at N = 64 it
 // reaches about two thirds).  Q and P stay in each CTA's tensor memory.
 // Barriers counted by both CTAs live in the leader (loads signal its k_full/
-// v_full; Q loaders and softmax threads arrive on its q_full, p_full, o_free
-// through cluster addresses); the leader's commits multicast to both CTAs'
-// kv_empty, s_full, q_empty, o_done and o_full.
+// v_full; one lane per softmax warp arrives on its q_full, p_full, o_free,
+// through a cluster address from the peer); the leader's commits multicast
+// to both CTAs' kv_empty, s_full, q_empty, o_done and o_full.  320 threads:
+// TMA warp, MMA warp, 8 softmax warps, which also write the next tile's Q
+// into tensor memory as soon as the current tile's last S is consumed.
 constexpr int KB = 128;  // keys per block (pair)
+constexpr int kPairAttnThreads = 64 + 256;  // TMA, MMA, 8 softmax warps
 constexpr int KH = 64;   // keys per CTA in S
 
 template <int D>
@@ -526,7 +529,7 @@ struct PairAttnCfg {
 };
 
 template <int D, bool CAUSAL>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kPairAttnThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, AttnQ qin,
                           float* __restrict__ out, int S, float scale_log2, AttnOut ol,
@@ -542,12 +545,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* v_full = k_full + STAGES;        // [STAGES] leader
   uint64_t* kv_empty = v_full + STAGES;      // [STAGES] both
   uint64_t* s_full = kv_empty + STAGES;      // [2] both
-  uint64_t* p_full = s_full + 2;             // [2] leader: 512 softmax threads
-  uint64_t* q_full = p_full + 2;             // [1] leader: 256 Q-loader threads
+  uint64_t* p_full = s_full + 2;             // [2] leader: one arrive per softmax warp
+  uint64_t* q_full = p_full + 2;             // [1] leader: one arrive per softmax warp
   uint64_t* q_empty = q_full + 1;            // [1] both
   uint64_t* o_done = q_empty + 1;            // [1] both: one phase per P V
   uint64_t* o_full = o_done + 1;             // [1] both: one phase per tile
-  uint64_t* o_free = o_full + 1;             // [1] leader: 512 softmax threads
+  uint64_t* o_free = o_full + 1;             // [1] leader: one arrive per softmax warp
   uint64_t* drain = o_free + 1;              // [1] leader
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -559,6 +562,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const bool leader = rank == 0;
   const long long cluster_id = blockIdx.x / 2, n_clusters = gridDim.x / 2;
   auto lead = [&](uint64_t* bar) { return ptx::mapa(ptx::smem_u32(bar), 0); };
+  // One arrive per warp on a leader barrier, after every lane's prior work:
+  // a CTA-scope arrive in the leader, a cluster-scope release in the peer (a
+  // release per thread showed up as membar stalls).
+  auto warp_arrive = [&](uint64_t* bar) {
+    __syncwarp();
+    if (lane == 0) {
+      if (leader) ptx::mbar_arrive(bar);
+      else ptx::mbar_arrive_cluster(lead(bar));
+    }
+  };
   auto load = [&](void* dst, const CUtensorMap* m, uint32_t bar, int d0, int s0, int head,
                   int bat, bool hs) {
     if (hs) ptx::tma_load_4d_pair(dst, m, bar, d0, head, s0, bat);
@@ -579,13 +592,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&s_full[i], 1);
-      ptx::mbar_init(&p_full[i], 512);
+      ptx::mbar_init(&p_full[i], 16);  // 8 softmax warps per CTA
     }
-    ptx::mbar_init(q_full, 256);
+    ptx::mbar_init(q_full, 16);      // 8 softmax warps per CTA write Q
     ptx::mbar_init(q_empty, 1);
     ptx::mbar_init(o_done, 1);
     ptx::mbar_init(o_full, 1);
-    ptx::mbar_init(o_free, 512);
+    ptx::mbar_init(o_free, 16);
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -725,39 +738,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mma_commit_pair(drain, 0x1);
       ptx::mbar_wait(drain, 0, status, 0x226, nullptr);
     }
-  } else if (warp >= 10) {
-    // -------------------------------------------------------- Q loaders --
-    const int qd = warp & 3;
-    const int row = qd * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-    int i = 0;
-    for (long long t = cluster_id; t < tiles.total; t += n_clusters, ++i) {
-      int q0, head, bat;
-      tiles.get(t, CAUSAL, q0, head, bat);
-      if (!__all_sync(0xffffffffu, ptx::mbar_wait(q_empty, (uint32_t)((i & 1) ^ 1), status,
-                                                  0x22d, abort_flag)))
-        break;
-      const int qrow = q0 + rank * QT + row;
-      const float* qr = qin.p + (long long)bat * qin.b + (long long)head * qin.h +
-                        (long long)qrow * qin.s;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (qrow < S) f = __ldg(reinterpret_cast<const float4*>(qr + c * 32) + k);
-          r[4 * k] = round_tf32(f.x * scale_log2);
-          r[4 * k + 1] = round_tf32(f.y * scale_log2);
-          r[4 * k + 2] = round_tf32(f.z * scale_log2);
-          r[4 * k + 3] = round_tf32(f.w * scale_log2);
-        }
-        ptx::tmem_st32(tmem + lane_off + C::Q_COL + c * 32, r);
-      }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive_cluster(lead(q_full));
-    }
   } else {
     // ------------------------------------------------------ softmax rows --
     // As in the single-CTA kernel, with 64 of a block's 128 columns per
@@ -768,8 +748,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     constexpr int HC = KB / 2, HD = D / 2;
     bool ok = true;
+    // This thread's half of its Q row for tile t (local tile i), times
+    // scale * log2(e) (scores come out in base 2) and rounded to tf32, into
+    // tensor memory -- once the previous tile's S MMAs are done with it.
+    auto load_q = [&](long long t, int i) {
+      if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(q_empty, (uint32_t)((i & 1) ^ 1),
+                                                          status, 0x22d, abort_flag));
+      if (!ok) return;
+      int q0, head, bat;
+      tiles.get(t, CAUSAL, q0, head, bat);
+      const int qrow = q0 + rank * QT + row;
+      const float* qr = qin.p + (long long)bat * qin.b + (long long)head * qin.h +
+                        (long long)qrow * qin.s + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (qrow < S) f = __ldg(reinterpret_cast<const float4*>(qr + c * 32) + k);
+          r[4 * k] = round_tf32(f.x * scale_log2);
+          r[4 * k + 1] = round_tf32(f.y * scale_log2);
+          r[4 * k + 2] = round_tf32(f.z * scale_log2);
+          r[4 * k + 3] = round_tf32(f.w * scale_log2);
+        }
+        ptx::tmem_st32(tmem + lane_off + C::Q_COL + h * HD + c * 32, r);
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      warp_arrive(q_full);
+    };
     long long g = 0;
     int tile_i = 0;
+    if (cluster_id < tiles.total) load_q(cluster_id, 0);
     for (long long t = cluster_id; t < tiles.total; t += n_clusters, ++tile_i) {
       int q0, head, bat;
       tiles.get(t, CAUSAL, q0, head, bat);
@@ -860,9 +871,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           ptx::tmem_st32(sbase + 32, v1);
           ptx::tmem_wait_st();
           ptx::tc_fence_before();
-          ptx::mbar_arrive_cluster(lead(&p_full[sb]));
+          warp_arrive(&p_full[sb]);
         }
       }
+      // the next tile's Q (the MMA warp can start its S while O drains)
+      if (t + n_clusters < tiles.total) load_q(t + n_clusters, tile_i + 1);
       lsum[h * 128 + row] = l;
       ptx::named_bar_sync(1 + q, 64);
       l += lsum[(h ^ 1) * 128 + row];
@@ -889,7 +902,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive_cluster(lead(o_free));
+        warp_arrive(o_free);
       }
     }
   }
@@ -1063,7 +1076,7 @@ agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k,
   const float scale_log2 = (1.0f / sqrtf((float)D)) * kLog2e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.blockDim = dim3(kPairAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -27,6 +27,7 @@
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
 #include "umma2_kernel.cuh"
+#include "pair_launch.cuh"
 
 namespace agpu {
 
@@ -409,26 +410,8 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
                         PAIR ? umma::PairCfg<BN>::MMA_N / 2 : BN, false, !X3);
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
   if constexpr (PAIR) {
-    using Cfg = umma::PairCfg<BN>;
-    auto kern = umma::umma_tf32_pair_kernel<P>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::SMEM);
-    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::min<long long>(2 * pol.tiles, dev->sm_count & ~1), 1, 1);
-    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::SMEM;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, pol, dev->d_status);
-    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv pair launch"); }
-    st = after_launch(dev, "conv2d_tf32 (umma_tf32_pair_kernel)");
+    st = launch_pair(dev, ta, tb, pol, pol.tiles, s,
+                     "conv2d_tf32 (umma_tf32_pair_kernel)");
   } else {
     using Cfg = umma::Cfg<BN, X3>;
     auto kern = umma::umma_tf32_kernel<P, X3>;

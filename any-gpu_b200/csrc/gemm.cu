@@ -32,6 +32,7 @@
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
 #include "umma2_kernel.cuh"
+#include "pair_launch.cuh"
 
 namespace agpu {
 
@@ -357,7 +358,6 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                const GemmEpilogue& ep, cudaStream_t s) {
   using P = GemmPairPolicy<BN, A_MN, B_MN>;
-  using Cfg = umma::PairCfg<BN>;
   CUtensorMap ta, tb;
   if (!A_MN)
     AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, true));
@@ -377,23 +377,8 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
-  auto kern = umma::umma_tf32_pair_kernel<P>;
-  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-  const long long ctas = std::min<long long>(2 * pol.tiles, dev->sm_count & ~1);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas, 1, 1);
-  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  AGPU_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, pol, dev->d_status));
-  return after_launch(dev, "gemm_tf32 (umma_tf32_pair_kernel)");
+  return launch_pair(dev, ta, tb, pol, pol.tiles, s,
+                     "gemm_tf32 (umma_tf32_pair_kernel)");
 }
 
 // The CTA-pair kernel serves TF32 GEMMs with at least one full 256 x 256 tile;

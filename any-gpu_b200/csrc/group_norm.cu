@@ -724,11 +724,7 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) &
                         15u) == 0;
   // One CTA per group with the group in registers, up to 48K elements.
-  static const bool stream_first = [] {
-    const char* e = getenv("AGPU_GN_PATH");
-    return e && e[0] == 's';
-  }();
-  if (!stream_first && aligned && spatial % 4 == 0 && gsize <= 1024LL * 12 * 4 &&
+  if (aligned && spatial % 4 == 0 && gsize <= 1024LL * 12 * 4 &&
       groups_total < (1LL << 31)) {
     const unsigned grid = (unsigned)groups_total;
     const int sp = (int)spatial, cp = (int)cpg, gr = (int)groups;

@@ -10,8 +10,8 @@
 //   both CTAs  warp 0: TMA of the CTA's halves; completion is signalled on the
 //              leader CTA's full barrier (cp.async.bulk.tensor .cta_group::2),
 //              no multicast.  warps 2-5: drain this CTA's TMEM rows (128 of
-//              the tile's 256) and arrive on the leader's "accumulator empty"
-//              barrier.  warp 1 allocates tensor memory for the pair.
+//              the tile's 256) and arrive (one lane per warp) on the leader's
+//              "accumulator empty" barrier.  warp 1 allocates tensor memory for the pair.
 //   leader     warp 1 lane 0 issues tcgen05.mma.cta_group::2 (M 256) and
 //              commits to the barriers of both CTAs (commit multicast mask).
 //
@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&tfull[i], 1);
-      ptx::mbar_init(&tempty[i], 2 * kEpiWarps * 32);
+      ptx::mbar_init(&tempty[i], 2 * kEpiWarps);  // one arrive per epilogue warp
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
       for (long long t = cluster_id; t < num_tiles && ok; t += n_clusters, ++local) {
         const int acc = local % C::ACC;
         const uint32_t acc_phase = (local / C::ACC) & 1;
-        if (!ptx::mbar_wait(&tempty[acc], acc_phase ^ 1, status, 0x302, abort_flag)) break;
+        // the peer's epilogue warps arrive with cluster-scope release
+        if (!ptx::mbar_wait<true>(&tempty[acc], acc_phase ^ 1, status, 0x302, abort_flag)) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_k; ++kb) {
@@ -195,7 +196,11 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
       const auto tile = pol.rank_tile(pol.tile(t), rank);
       const int acc = local % C::ACC;
       const uint32_t acc_phase = (local / C::ACC) & 1;
-      if (!ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x305, abort_flag)) break;
+      // warp-uniform: every lane takes the same exit (the arrive below and
+      // the policy's store use warp-wide syncs)
+      if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x305,
+                                                  abort_flag)))
+        break;
       ptx::tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -206,7 +211,11 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
         pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, false, true);
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(&tempty[acc]), 0));
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) ptx::mbar_arrive(&tempty[acc]);
+        else ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(&tempty[acc]), 0));
+      }
     }
   }
 

@@ -236,7 +236,9 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
       for (int k0 = 0; k0 < num_k; k0 += kseg, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x105, abort_flag)) {
+        // warp-uniform exit: the policy's store uses warp-wide syncs
+        if (!__all_sync(0xffffffffu,
+                        ptx::mbar_wait(&tfull[acc], acc_phase, status, 0x105, abort_flag))) {
           ok = false;
           break;
         }

@@ -324,7 +324,7 @@ class Sdpa(Workload):
         super().__init__(args, rank)
         self.bh, self.s, self.d = args.bh, args.seq, 128
         self.flops = self.dom_flops = 4.0 * self.bh * self.s * self.s * self.d
-        self.dom_kernel = "attention_tf32_kernel<128, non-causal>"
+        self.dom_kernel = "attention_pair_kernel<128, non-causal> (CTA-pair flash attention)"
 
     def config(self):
         return {"workload": "scaled_dot_product_attention", "batch_heads": self.bh,
