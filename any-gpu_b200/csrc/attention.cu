@@ -666,12 +666,14 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
                             abort_flag))
           return false;
         ptx::tc_fence_after();
-        const uint32_t k_addr = ptx::smem_u32(stage_k(st));
+        // one descriptor per block; a K-slice moves its 14-bit start address
+        // (bytes / 16) by a compile-time offset, no carry (smem < 256 KB)
+        const uint64_t bd0 = umma::operand_desc<false>(ptx::smem_u32(stage_k(st)));
         const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)(g & 1) * KB;
 #pragma unroll
         for (int kk = 0; kk < D / 8; ++kk) {
-          const uint32_t off = (kk % 4) * 32;  // 8 fp32 inside the 128-byte row
-          const uint64_t bd = umma::operand_desc<false>(k_addr + (kk / 4) * KH * 128 + off);
+          constexpr int kChunk = KH * 128;  // one 32-dim chunk of the K half
+          const uint64_t bd = bd0 + (uint64_t)(((kk / 4) * kChunk + (kk % 4) * 32) >> 4);
           ptx::mma_tf32_ts_pair(d_tmem, tmem + C::Q_COL + kk * 8, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         ptx::mma_commit_pair(&s_full[g & 1], 0x3);
@@ -690,15 +692,14 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
             !ptx::mbar_wait<true>(o_free, (uint32_t)((i - 1) & 1), status, 0x22c, abort_flag))
           return false;
         ptx::tc_fence_after();
-        const uint32_t v_addr = ptx::smem_u32(stage_v(st));
+        // V chunk c (32 head dims x 128 keys, 16 KB) at c * KB * 128; 8 keys = 1024 B
+        const uint64_t bd0 = ptx::make_sdesc(ptx::smem_u32(stage_v(st)), KB * 128, 512, 1);
         const uint32_t p_tmem = tmem + C::S_COL + (uint32_t)(g & 1) * KB;
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < KB / 8; ++kk) {
-          // V chunk c (32 head dims x 128 keys, 16 KB) at c * KB * 128; 8 keys = 1024 B
-          const uint64_t bd = ptx::make_sdesc(v_addr + kk * 1024, KB * 128, 512, 1);
-          ptx::mma_tf32_ts_pair(tmem + C::O_COL, p_tmem + kk * 8, bd, idesc_o,
-                                (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < KB / 8; ++kk)
+          ptx::mma_tf32_ts_pair(tmem + C::O_COL, p_tmem + kk * 8, bd0 + (uint64_t)(kk * 64),
+                                idesc_o, kk > 0 ? 1u : acc0);
         ptx::mma_commit_pair(&kv_empty[st], 0x3);
         ptx::mma_commit_pair(o_done, 0x3);
         return true;
