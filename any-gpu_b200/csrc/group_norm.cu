@@ -5,35 +5,23 @@
 // one thread per (n, g) group, SHADER_GN_NORM applies (x-mean)*rstd*gamma+beta
 // per element.  Same definition here, B200 layout:
 //
-//  * Streaming cluster path (group fits on-chip): a persistent grid of
-//    thread-block clusters, CL CTAs per cluster, walks the (n, g) groups; each
-//    CTA owns one 1/CL slice of every group.  Slices are brought in by bulk
-//    copies (cp.async.bulk) into a 2-4 deep shared-memory ring, so the reads
-//    of the next groups are in flight while the current one is reduced and
-//    written: x is read from HBM once, y written once.  Each CTA reduces its
-//    slice to (mean, M2) (Chan merges up the warps), pushes the pair into
-//    every peer's shared memory with st.async, which completes on the peer's
-//    mbarrier -- no cluster barrier, so no fence waits on the previous
-//    group's stores -- and all CTAs merge the CL pairs in the same order.  The variance is computed from centered
-//    values, which is the reference's quantity without the E[x^2]-mean^2
-//    cancellation.
-//  * Chunked path (any size): kernel 1 writes per-chunk (mean, M2) partials
-//    into scratch, kernel 2 merges a group's partials with Chan's formula in
-//    a fixed order and normalises its chunk.
+//  * Chunked, two kernels: kernel 1 reduces each 8192-element chunk of a
+//    group to (mean, M2) -- the exact chunk mean, then the centered sum of
+//    squares, two plain block sums (no E[x^2]-mean^2 cancellation); kernel 2
+//    loads its chunk, merges the group's chunk summaries with Chan's formula
+//    in a fixed order in every thread (while its loads are in flight), and
+//    normalises.  x is read twice; a tensor up to the 126 MB L2 is mostly
+//    served from L2 the second time.  Measured against a single-pass kernel
+//    holding each group in registers (one 1024-thread CTA per group) and a
+//    persistent cluster kernel streaming slices through shared memory, both
+//    latency-bound, this is the fastest (UNet block: 49.8 vs 58.7 vs 91 us).
+//    Float4 loads when x, y are 16-byte aligned and spatial % 4 == 0, a
+//    scalar pair of kernels otherwise.
 //  * `swish` fuses the UNet block's activation, y = z / (1 + exp(-z))
 //    (src/ops/elementwise.rs:77-89), into the store.
-#include <cooperative_groups.h>
-
 #include <algorithm>
-#include <cstdlib>
-#include <map>
-#include <mutex>
-#include <tuple>
 
 #include "agpu_internal.cuh"
-#include "ptx.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace agpu {
 
@@ -64,74 +52,6 @@ __device__ __forceinline__ float act_fast(float z, bool swish) {
   return swish ? __fdividef(z, 1.0f + __expf(-z)) : z;
 }
 
-// One CTA of T threads per (n, g) group, the whole group in registers (VEC
-// float4 per thread): every SM issues one burst of loads for its group, two
-// block reductions give the exact mean and the centered M2, then the group is
-// normalised and stored.  No cluster, no exchange: CTAs of different groups
-// overlap each other's phases.
-template <int T>
-__device__ __forceinline__ float group_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __syncthreads();  // red is free (previous reduction fully read)
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float s = lane < T / 32 ? red[lane] : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  return s;  // same value in every thread (same butterfly order)
-}
-
-template <bool SWISH, int T, int VEC>
-__global__ void __launch_bounds__(T, 1) gn_group_kernel(
-    const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
-    float* __restrict__ y, int spatial, int cpg, int groups, float eps) {
-  __shared__ float red[32];
-  const long long grp = blockIdx.x;
-  const int g = (int)(grp % groups);
-  const int gsize = cpg * spatial;
-  const int nvec = gsize / 4;
-  const float4* src = reinterpret_cast<const float4*>(x + grp * gsize);
-  float4 v[VEC];
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    const int i = threadIdx.x + j * T;
-    if (i < nvec) {
-      v[j] = __ldcs(src + i);
-      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    }
-  }
-  const float mean = group_sum<T>(s, red) / (float)gsize;
-  float q = 0.f;
-#pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    const int i = threadIdx.x + j * T;
-    if (i < nvec) {
-      const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
-      q += (a * a + b * b) + (c * c + d * d);
-    }
-  }
-  const float rstd = 1.0f / sqrtf(group_sum<T>(q, red) / (float)gsize + eps);
-  float4* dst = reinterpret_cast<float4*>(y + grp * gsize);
-  const unsigned sp = (unsigned)spatial;
-#pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    const int i = threadIdx.x + j * T;
-    if (i < nvec) {
-      const int ch = g * cpg + (int)((4u * (unsigned)i) / sp);  // spatial % 4 == 0
-      const float ga = __ldg(gamma + ch) * rstd, be = __ldg(beta + ch);
-      float4 o;
-      o.x = act_fast((v[j].x - mean) * ga + be, SWISH);
-      o.y = act_fast((v[j].y - mean) * ga + be, SWISH);
-      o.z = act_fast((v[j].z - mean) * ga + be, SWISH);
-      o.w = act_fast((v[j].w - mean) * ga + be, SWISH);
-      __stcs(dst + i, o);
-    }
-  }
-}
-
 // Chan et al. merge of two (count, mean, M2) summaries.
 __device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, float nb, float mb,
                                            float m2b) {
@@ -142,134 +62,6 @@ __device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, flo
   mean += d * f;
   m2 += m2b + d * d * n * f;
   n = nt;
-}
-
-// Persistent: grid.x = CL * clusters, cluster (CL,1,1).  slice = elements per
-// CTA (multiple of 4); stages = ring depth (>= 3).
-//
-// Iteration li normalises group li and, before that, reduces group li+1 and
-// sends its summary, so the exchange of group li's summaries has a whole
-// iteration to land: no CTA waits on a slower peer in steady state.  A CTA's
-// summary of group k goes to slot k % 4 of every peer (st.async, completing
-// on the peer's xbar[k % 4]); four slots are enough because a CTA sends
-// summary k+1 only after it received everyone's summary k-1, which each peer
-// sent after finishing iteration k-3, i.e. after it last read slot (k+1) % 4.
-template <bool SWISH>
-__global__ void __launch_bounds__(kThreads) gn_stream_kernel(
-    const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
-    float* __restrict__ y, long long groups_total, int spatial, int cpg, int groups, float eps,
-    int slice, int stages, unsigned int* status) {
-  constexpr int NS = 4;
-  cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(128) uint8_t gn_smem[];
-  __shared__ float3 wpart[kThreads / 32];       // per-warp (count, mean, M2)
-  __shared__ __align__(8) float2 part[NS][8];   // [slot][rank]: (mean, M2)
-  __shared__ __align__(8) uint64_t xbar[NS];    // completes when all CL pairs landed
-  float* ring = reinterpret_cast<float*>(gn_smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(gn_smem + (size_t)stages * slice * 4);
-  const int CL = (int)cluster.num_blocks();
-  const int rank = (int)cluster.block_rank();
-  const long long cid = blockIdx.x / CL, ncl = gridDim.x / CL;
-  const long long n_local = cid < groups_total ? (groups_total - cid + ncl - 1) / ncl : 0;
-  const int gsize = cpg * spatial;  // < 2^31: bounded by the launcher
-  const uint32_t bytes = (uint32_t)slice * 4u;
-  const int nvec = slice / 4;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) ptx::mbar_init(&full[i], 1);
-    for (int i = 0; i < NS; ++i) ptx::mbar_init(&xbar[i], 1);
-    ptx::fence_mbar_init();
-  }
-  cluster.sync();  // every CTA's barriers exist before any peer signals them
-  auto issue = [&](long long li) {
-    if (li >= n_local) return;
-    const long long grp = cid + li * ncl;
-    const int st = (int)(li % stages);
-    ptx::mbar_arrive_expect_tx(&full[st], bytes);
-    ptx::bulk_load(ring + (size_t)st * slice, x + grp * gsize + (long long)rank * slice, bytes,
-                   &full[st]);
-  };
-  // Reduce the slice of local group li (already in its stage) and send the
-  // (mean, M2) summary to every CTA of the cluster.  A timed-out wait is
-  // recorded and the summary is sent anyway, so no peer waits for one that
-  // never comes.
-  auto reduce_send = [&](long long li) {
-    const int st = (int)(li % stages);
-    if (threadIdx.x == 0) ptx::mbar_arrive_expect_tx(&xbar[li % NS], (uint32_t)(8 * CL));
-    ptx::mbar_wait(&full[st], (uint32_t)((li / stages) & 1), status, 0x401, nullptr);
-    const float4* src = reinterpret_cast<const float4*>(ring + (size_t)st * slice);
-    float s = 0.f, cnt = 0.f;
-    for (int i = threadIdx.x; i < nvec; i += kThreads) {
-      const float4 v = src[i];
-      s += (v.x + v.y) + (v.z + v.w);
-      cnt += 4.f;
-    }
-    float mean = cnt > 0.f ? s / cnt : 0.f, m2 = 0.f;
-    for (int i = threadIdx.x; i < nvec; i += kThreads) {
-      const float4 v = src[i];
-      const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
-      m2 += (a * a + b * b) + (c * c + d * d);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float nb = __shfl_xor_sync(0xffffffffu, cnt, o);
-      const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
-      const float qb = __shfl_xor_sync(0xffffffffu, m2, o);
-      if (lane & o) {  // lower lane's summary first: both partners get the same bits
-        float n2 = nb, mean2 = mb, m22 = qb;
-        chan_merge(n2, mean2, m22, cnt, mean, m2);
-        cnt = n2; mean = mean2; m2 = m22;
-      } else {
-        chan_merge(cnt, mean, m2, nb, mb, qb);
-      }
-    }
-    if (lane == 0) wpart[warp] = make_float3(cnt, mean, m2);
-    __syncthreads();
-    if (threadIdx.x < CL) {
-      float n = 0.f, mn = 0.f, q = 0.f;
-      for (int w = 0; w < kThreads / 32; ++w) chan_merge(n, mn, q, wpart[w].x, wpart[w].y, wpart[w].z);
-      const uint32_t peer = threadIdx.x;
-      ptx::st_async_v2(ptx::mapa(ptx::smem_u32(&part[li % NS][rank]), peer), mn, q,
-                       ptx::mapa(ptx::smem_u32(&xbar[li % NS]), peer));
-    }
-    __syncthreads();  // wpart is reused by the next reduction
-  };
-
-  if (threadIdx.x == 0)
-    for (int i = 0; i < stages - 1; ++i) issue(i);
-  if (n_local > 0) reduce_send(0);
-  for (long long li = 0; li < n_local; ++li) {
-    // the stage of li + stages - 1 was freed at the end of iteration li - 1
-    if (threadIdx.x == 0) issue(li + stages - 1);
-    if (li + 1 < n_local) reduce_send(li + 1);
-    const int slot = (int)(li % NS);
-    ptx::mbar_wait(&xbar[slot], (uint32_t)((li / NS) & 1), status, 0x402, nullptr);
-    // equal-count merge of the CL slices, same order in every CTA
-    float gn = 0.f, gmean = 0.f, gm2 = 0.f;
-    for (int r = 0; r < CL; ++r)
-      chan_merge(gn, gmean, gm2, (float)slice, part[slot][r].x, part[slot][r].y);
-    const float rstd = 1.0f / sqrtf(gm2 / (float)gsize + eps);
-
-    const long long grp = cid + li * ncl;
-    const int g = (int)(grp % groups);
-    const float4* src = reinterpret_cast<const float4*>(ring + (size_t)(li % stages) * slice);
-    float4* dst = reinterpret_cast<float4*>(y + grp * gsize + (long long)rank * slice);
-    const unsigned e0 = (unsigned)(rank * slice);  // element offset inside the group
-    const unsigned sp = (unsigned)spatial;
-    for (int i = threadIdx.x; i < nvec; i += kThreads) {
-      const float4 v = src[i];
-      const int ch = g * cpg + (int)((e0 + 4u * (unsigned)i) / sp);  // spatial % 4 == 0
-      const float ga = __ldg(gamma + ch) * rstd, be = __ldg(beta + ch);
-      float4 o;
-      o.x = act_fast((v.x - gmean) * ga + be, SWISH);
-      o.y = act_fast((v.y - gmean) * ga + be, SWISH);
-      o.z = act_fast((v.z - gmean) * ga + be, SWISH);
-      o.w = act_fast((v.w - gmean) * ga + be, SWISH);
-      __stcs(dst + i, o);
-    }
-    __syncthreads();  // stage li is free for the copy issued next iteration
-  }
 }
 
 // ------------------------------------------------------- chunked fallback --
@@ -343,52 +135,35 @@ constexpr int kChunkVec = 8;  // float4 per thread: 8192-element chunks
 __global__ void __launch_bounds__(kThreads) gn_partial_vec_kernel(const float* __restrict__ x,
                                                                   float2* __restrict__ partials,
                                                                   long long gsize, int chunk) {
-  __shared__ float3 wpart[kThreads / 32];
+  __shared__ float red[kThreads / 32];
   const long long grp = blockIdx.y;
   const long long c0 = (long long)blockIdx.x * chunk;
-  const int nvec = (int)(std::min<long long>(c0 + chunk, gsize) - c0) / 4;
+  const int n = (int)(std::min<long long>(c0 + chunk, gsize) - c0);
+  const int nvec = n / 4;
   const float4* src = reinterpret_cast<const float4*>(x + grp * gsize + c0);
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   float4 v[kChunkVec];
-  float s = 0.f, cnt = 0.f;
+  float s = 0.f;
 #pragma unroll
   for (int j = 0; j < kChunkVec; ++j) {
     const int i = threadIdx.x + j * kThreads;
     if (i < nvec) {
       v[j] = src[i];  // default caching: the apply kernel re-reads this chunk
       s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-      cnt += 4.f;
     }
   }
-  float mean = cnt > 0.f ? s / cnt : 0.f, m2 = 0.f;
+  // exact chunk mean, then the centered M2: two plain block sums
+  const float mean = block_sum(s, red) / (float)n;
+  float q = 0.f;
 #pragma unroll
   for (int j = 0; j < kChunkVec; ++j) {
     const int i = threadIdx.x + j * kThreads;
     if (i < nvec) {
       const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
-      m2 += (a * a + b * b) + (c * c + d * d);
+      q += (a * a + b * b) + (c * c + d * d);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float nb = __shfl_xor_sync(0xffffffffu, cnt, o);
-    const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
-    const float qb = __shfl_xor_sync(0xffffffffu, m2, o);
-    if (lane & o) {  // lower lane's summary first: both partners get the same bits
-      float n2 = nb, mean2 = mb, m22 = qb;
-      chan_merge(n2, mean2, m22, cnt, mean, m2);
-      cnt = n2; mean = mean2; m2 = m22;
-    } else {
-      chan_merge(cnt, mean, m2, nb, mb, qb);
-    }
-  }
-  if (lane == 0) wpart[warp] = make_float3(cnt, mean, m2);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float n = 0.f, mn = 0.f, q = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) chan_merge(n, mn, q, wpart[w].x, wpart[w].y, wpart[w].z);
-    partials[grp * gridDim.x + blockIdx.x] = make_float2(mn, q);
-  }
+  q = block_sum(q, red);
+  if (threadIdx.x == 0) partials[grp * gridDim.x + blockIdx.x] = make_float2(mean, q);
 }
 
 template <bool SWISH>
@@ -396,7 +171,6 @@ __global__ void __launch_bounds__(kThreads) gn_apply_vec_kernel(
     const float* __restrict__ x, const float2* __restrict__ partials,
     const float* __restrict__ gamma, const float* __restrict__ beta, float* __restrict__ y,
     long long gsize, int chunk, int nchunks, int spatial, int cpg, int groups, float eps) {
-  __shared__ float stat[2];
   const long long grp = blockIdx.y;
   const int g = (int)(grp % groups);
   const long long c0 = (long long)blockIdx.x * chunk;
@@ -408,23 +182,16 @@ __global__ void __launch_bounds__(kThreads) gn_apply_vec_kernel(
     const int i = threadIdx.x + j * kThreads;
     if (i < nvec) v[j] = __ldcs(src + i);  // last use of x
   }
-  if (threadIdx.x == 0) {
-    double n = 0.0, mean = 0.0, m2 = 0.0;
-    for (int c = 0; c < nchunks; ++c) {
-      const float2 p = partials[grp * nchunks + c];
-      const double nb = (double)(std::min<long long>((long long)(c + 1) * chunk, gsize) -
-                                 (long long)c * chunk);
-      const double delta = (double)p.x - mean;
-      const double nt = n + nb;
-      mean += delta * nb / nt;
-      m2 += (double)p.y + delta * delta * n * nb / nt;
-      n = nt;
-    }
-    stat[0] = (float)mean;
-    stat[1] = (float)(1.0 / sqrt(m2 / n + (double)eps));
+  // every thread merges the group's chunk summaries (Chan et al., fixed
+  // order), while its loads are in flight
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float2 p = __ldg(partials + grp * nchunks + c);
+    const float nb = (float)(std::min<long long>((long long)(c + 1) * chunk, gsize) -
+                             (long long)c * chunk);
+    chan_merge(n, mean, m2, nb, p.x, p.y);
   }
-  __syncthreads();
-  const float mean = stat[0], rstd = stat[1];
+  const float rstd = 1.0f / sqrtf(m2 / n + eps);
   float4* dst = reinterpret_cast<float4*>(y + grp * gsize + c0);
 #pragma unroll
   for (int j = 0; j < kChunkVec; ++j) {
@@ -440,54 +207,6 @@ __global__ void __launch_bounds__(kThreads) gn_apply_vec_kernel(
       __stcs(dst + i, o);
     }
   }
-}
-
-constexpr int kStreamSmem = 100 * 1024;  // ring budget: two CTAs per SM
-constexpr int kSliceMax = 16 * 1024;      // floats per CTA slice (64 KiB)
-
-template <bool SWISH>
-agpu_status launch_stream(agpu_device* dev, const float* x, const float* gamma,
-                          const float* beta, float* y, long long groups_total, int spatial,
-                          int cpg, int groups, float eps, int cl, int slice, cudaStream_t s) {
-  const int bytes = slice * 4;
-  const int stages = std::max(3, std::min(6, kStreamSmem / bytes));
-  const int smem = stages * bytes + stages * 8;
-  auto kern = gn_stream_kernel<SWISH>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3((unsigned)cl, 1, 1);
-  // co-resident clusters for (device, CL, ring size), looked up once
-  static std::mutex mu;
-  static std::map<std::tuple<int, int, int>, int> fits;
-  int active = 0;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    const auto key = std::make_tuple(dev->ordinal, cl, smem);
-    auto it = fits.find(key);
-    if (it == fits.end()) {
-      // one limit for every ring size (3 x 64 KiB slices is the largest)
-      AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     3 * kSliceMax * 4 + 64));
-      AGPU_CUDA(cudaOccupancyMaxActiveClusters(&active, kern, &cfg));
-      it = fits.emplace(key, active).first;
-    }
-    active = it->second;
-  }
-  if (active < 1) return fail(AGPU_ERR_UNSUPPORTED, "group_norm: cluster of %d does not fit", cl);
-  const long long clusters = std::min<long long>(groups_total, active);
-  cfg.gridDim = dim3((unsigned)(clusters * cl), 1, 1);
-  AGPU_CUDA(cudaLaunchKernelEx(&cfg, kern, x, gamma, beta, y, groups_total, spatial, cpg, groups,
-                               eps, slice, stages, dev->d_status));
-  return after_launch(dev, "gn_stream_kernel");
 }
 
 // The two chunked kernels (vectorised when `vec`), partials in `partials`.
@@ -723,44 +442,6 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
   const long long groups_total = (long long)batch * groups;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) &
                         15u) == 0;
-  // One CTA per group with the group in registers, up to 48K elements.
-  if (aligned && spatial % 4 == 0 && gsize <= 1024LL * 12 * 4 &&
-      groups_total < (1LL << 31)) {
-    const unsigned grid = (unsigned)groups_total;
-    const int sp = (int)spatial, cp = (int)cpg, gr = (int)groups;
-#define AGPU_GN_GROUP(T, V)                                                                    \
-    if (gsize <= (long long)(T) * (V) * 4) {                                                   \
-      if (swish) gn_group_kernel<true, T, V><<<grid, T, 0, s>>>(x, gamma, beta, y, sp, cp, gr, eps); \
-      else gn_group_kernel<false, T, V><<<grid, T, 0, s>>>(x, gamma, beta, y, sp, cp, gr, eps); \
-      return after_launch(dev, "gn_group_kernel");                                            \
-    }
-    AGPU_GN_GROUP(256, 4)
-    AGPU_GN_GROUP(256, 8)
-    AGPU_GN_GROUP(512, 8)
-    AGPU_GN_GROUP(1024, 8)
-    AGPU_GN_GROUP(1024, 12)
-#undef AGPU_GN_GROUP
-  }
-  // Streaming cluster path: a group split over CL <= 8 CTAs, each slice a
-  // multiple of 4 elements.  Prefer the smallest CL whose slice is at most
-  // 24 KiB (a ring of four or more slices per CTA, two CTAs per SM), else the
-  // smallest CL whose slice fits 64 KiB.
-  if (aligned && spatial % 4 == 0 && gsize <= 8LL * kSliceMax) {
-    int pick = 0;
-    for (int pass = 0; pass < 2 && !pick; ++pass) {
-      const long long cap = pass == 0 ? 6 * 1024 : kSliceMax;
-      for (int cl = 1; cl <= 8; ++cl) {
-        if (gsize % (4LL * cl) == 0 && gsize / cl <= cap) { pick = cl; break; }
-      }
-    }
-    if (pick) {
-      const int sl = (int)(gsize / pick);
-      return swish ? launch_stream<true>(dev, x, gamma, beta, y, groups_total, (int)spatial,
-                                         (int)cpg, (int)groups, eps, pick, sl, s)
-                   : launch_stream<false>(dev, x, gamma, beta, y, groups_total, (int)spatial,
-                                          (int)cpg, (int)groups, eps, pick, sl, s);
-    }
-  }
   // Chunked path with a scratch array of per-chunk partials.
   const int chunk = 8192;
   const long long nchunks = (long long)group_norm_chunk_count((uint64_t)gsize);

@@ -144,30 +144,9 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
       : "memory");
 }
 
-// Store two floats into a peer CTA's shared memory (cluster address from
-// mapa) and count their 8 bytes on the peer's mbarrier (also a cluster
-// address): an exchange that needs no cluster-wide memory fence.
-__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float a, float b,
-                                            uint32_t cluster_bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
-      ::"r"(cluster_addr), "f"(a), "f"(b), "r"(cluster_bar)
-      : "memory");
-}
-
 // Named barrier over `count` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// Plain (untiled) bulk copy global -> this CTA's shared memory, completion
-// counted in bytes on `bar`.  Both addresses 16-byte aligned, bytes % 16 == 0.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit() {

@@ -196,9 +196,9 @@ def _gn64(x, gamma, beta, n, c, s, g, eps):
 
 
 @pytest.mark.parametrize("swish", [False, True])
-@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block (5 CTAs x 8 float4)
-                                     (2, 40, 4096, 8),       # 5 CTAs x 4 float4 per thread
-                                     (1, 64, 4096, 2),       # 8 CTAs x 16 float4 per thread
+@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block: 5 chunks per group
+                                     (2, 40, 4096, 8),       # ragged last chunk (20480)
+                                     (1, 64, 4096, 2),       # 16 chunks per group
                                      (2, 64, 1024, 32),      # 2 channels x 1024 per group
                                      (3, 12, 37, 4),         # spatial % 4 != 0: chunked path
                                      (1, 4, 300000, 2),      # 600k-element groups: chunked
