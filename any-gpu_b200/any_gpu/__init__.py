@@ -184,6 +184,12 @@ class GpuDevice:
         """Reference: `batch_matmul(a,b,batch,m,n,k)` (src/ops/conv.rs:426)."""
         return self._new(_lib.load().agpu_batch_matmul, a.handle, b.handle, batch, m, n, k)
 
+    def batch_matmul_softmax(self, a, b, batch: int, m: int, n: int, k: int) -> GpuBuffer:
+        """batch_matmul then a row softmax over the result, in one call (the
+        softmax runs in place on the product)."""
+        return self._new(_lib.load().agpu_batch_matmul_softmax, a.handle, b.handle, batch, m,
+                         n, k)
+
     def gemm(self, a, b, batch: int, m: int, n: int, k: int, trans_a: bool = False,
              trans_b: bool = False) -> GpuBuffer:
         """C[b] = op(A[b]) op(B[b]); op = transpose when trans_* (autograd backward GEMMs)."""

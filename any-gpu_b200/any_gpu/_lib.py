@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_buffer_device_ptr": (C.c_void_p, [c_buf]),
     "agpu_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, P_buf]),
     "agpu_batch_matmul": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, P_buf]),
+    "agpu_batch_matmul_softmax": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, P_buf]),
     "agpu_gemm": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, u32, i32, i32, P_buf]),
     "agpu_gemm_ex": (c_status, [c_dev, c_buf, c_buf, c_buf, c_buf, u32, u32, u32, u32, i32, i32,
                                 i32, P_buf]),

@@ -111,6 +111,23 @@ agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a, const agpu
   });
 }
 
+agpu_status agpu_batch_matmul_softmax(agpu_device* dev, const agpu_buffer* a,
+                                      const agpu_buffer* b, uint32_t batch, uint32_t m,
+                                      uint32_t n, uint32_t k, agpu_buffer** out) {
+  CHECK_DEV(dev, "batch_matmul_softmax");
+  CHECK_BUF(a, "batch_matmul_softmax", "A");
+  CHECK_BUF(b, "batch_matmul_softmax", "B");
+  CHECK_OUT(out, "batch_matmul_softmax");
+  // src/ops/conv.rs:427-428
+  CHECK_LEN(a, (uint64_t)batch * m * k, "batch_matmul_softmax", "A");
+  CHECK_LEN(b, (uint64_t)batch * k * n, "batch_matmul_softmax", "B");
+  return with_output(dev, (uint64_t)batch * m * n, out, [&](float* c) {
+    AGPU_TRY(launch_gemm(dev, a->dptr, b->dptr, c, batch, m, n, k, false, false, dev->stream));
+    // each row is read completely before any of it is written: in place is exact
+    return launch_softmax(dev, c, c, (uint64_t)batch * m, n, dev->stream);
+  });
+}
+
 agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
                       uint32_t batch, uint32_t m, uint32_t n, uint32_t k, int trans_a, int trans_b,
                       agpu_buffer** out) {

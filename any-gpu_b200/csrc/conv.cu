@@ -211,6 +211,24 @@ __global__ void __launch_bounds__(256) weight_khwc_smem_kernel(const float* __re
   }
 }
 
+// conv_transpose2d weight W [Cin, Cout, KH, KW] -> the equivalent conv2d
+// weight W' [Cout, Cin, KH, KW] with both taps reversed:
+// W'[o, i, a, b] = W[i, o, KH-1-a, KW-1-b].
+__global__ void weight_flip_kernel(const float* __restrict__ w, float* __restrict__ w2, int cin,
+                                   int cout, int kh, int kw) {
+  const long long total = (long long)cin * cout * kh * kw;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i % kw);
+    long long r = i / kw;
+    const int a = (int)(r % kh);
+    r /= kh;
+    const int ic = (int)(r % cin);
+    const int oc = (int)(r / cin);
+    w2[i] = w[(((long long)ic * cout + oc) * kh + (kh - 1 - a)) * kw + (kw - 1 - b)];
+  }
+}
+
 // Direct convolution, one thread per output (exact fp32; any stride,
 // dilation, groups) -- same arithmetic order as the reference shader.
 __global__ void conv2d_direct_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -482,6 +500,27 @@ agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const
                                     cudaStream_t s) {
   const long long total = (long long)p.n * p.cout * p.ho * p.wo;
   if (total == 0) return AGPU_OK;
+  // Stride 1, one group, no output padding: conv_transpose2d(x, W, pad p) is
+  // conv2d(x, W', pad d*(k-1) - p) with W' the channel-swapped, tap-reversed
+  // weight (src/ops/conv.rs:277-290: oh = ih - p + kh*d, so ih = oh + p - kh*d
+  // = oh - p' + (k-1-kh)*d), which runs on the tensor-core implicit GEMM.
+  // The exact fp32 mode keeps the direct kernel (the reference's sum order).
+  const int php = p.dh * (p.kh - 1) - p.ph, pwp = p.dw * (p.kw - 1) - p.pw;
+  ConvParams q{p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, 1, 1, php, pwp, p.dh, p.dw, 1, p.ho,
+               p.wo};
+  if (dev->precision != AGPU_PREC_FFMA && p.sh == 1 && p.sw == 1 && p.groups == 1 && php >= 0 &&
+      pwp >= 0 && p.ho == p.h + p.dh * (p.kh - 1) - 2 * p.ph &&
+      p.wo == p.w + p.dw * (p.kw - 1) - 2 * p.pw && conv_tc_eligible(q)) {
+    const long long wn = (long long)p.cin * p.cout * p.kh * p.kw;
+    void* buf = nullptr;
+    AGPU_TRY(pool_alloc(dev, (uint64_t)wn * sizeof(float), &buf, s));
+    float* w2 = static_cast<float*>(buf);
+    weight_flip_kernel<<<grid_for(dev, wn), 256, 0, s>>>(w, w2, p.cin, p.cout, p.kh, p.kw);
+    agpu_status st = after_launch(dev, "weight_flip_kernel");
+    if (st == AGPU_OK) st = launch_conv2d(dev, q, x, w2, bias, y, s);
+    pool_free(dev, buf, s);
+    return st;
+  }
   conv_transpose2d_kernel<<<grid_for(dev, total), 256, 0, s>>>(
       x, w, bias, y, p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, p.sh, p.sw, p.ph, p.pw, p.dh, p.dw,
       p.groups, p.ho, p.wo);

@@ -113,6 +113,13 @@ AGPU_API agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a,
                                        const agpu_buffer* b, uint32_t batch, uint32_t m,
                                        uint32_t n, uint32_t k, agpu_buffer** out);
 
+/* batch_matmul followed by a row softmax over the last dim of the result (the
+ * batch_matmul + softmax workload), in one call and one output buffer: the
+ * softmax runs in place on the product.  Same shape checks as batch_matmul. */
+AGPU_API agpu_status agpu_batch_matmul_softmax(agpu_device* dev, const agpu_buffer* a,
+                                               const agpu_buffer* b, uint32_t batch, uint32_t m,
+                                               uint32_t n, uint32_t k, agpu_buffer** out);
+
 /* General (batched) GEMM with optional transposed operands, the kernels the
  * reference's autograd backward reaches through transpose + matmul
  * (src/autograd.rs:357-366): dA = dC * B^T (trans_b), dB = A^T * dC (trans_a).

@@ -263,6 +263,23 @@ def test_group_norm_backward_errors(dev):
         assert e.value.status == 1
 
 
+@pytest.mark.parametrize("batch,m,n,k", [(3, 300, 264, 520), (2, 256, 2048, 256)])
+def test_batch_matmul_softmax(dev, orc, batch, m, n, k):
+    """The fused entry point equals batch_matmul followed by softmax."""
+    r = np.random.default_rng(m + n)
+    a = (r.standard_normal(batch * m * k) * 0.05).astype(np.float32)
+    b = (r.standard_normal(batch * k * n) * 0.05).astype(np.float32)
+    got = dev.read(dev.batch_matmul_softmax(dev.upload(a), dev.upload(b), batch, m, n, k))
+    prod = np.concatenate([orc.matmul(a[i * m * k:(i + 1) * m * k], b[i * k * n:(i + 1) * k * n],
+                                      m, n, k, threads=True) for i in range(batch)])
+    want = orc.softmax(prod, batch * m, n, threads=True)
+    assert orc.rel_fro(got, want) <= 1e-3
+    # and exactly the two separate calls
+    sep = dev.read(dev.softmax(dev.batch_matmul(dev.upload(a), dev.upload(b), batch, m, n, k),
+                               batch * m, n))
+    np.testing.assert_array_equal(got, sep)
+
+
 def test_group_norm_errors(dev):
     from any_gpu import AnyGpuError
     x = dev.upload(np.ones(10, np.float32))
@@ -351,6 +368,30 @@ def test_conv_backward_ops_parity(dev, orc):
         want = orc.conv_transpose2d(x, wt, bias, n, cin, h, w, cout, k, k, (s, s), (p, p),
                                     (op_, op_), (d, d), g)
         assert orc.rel_fro(got, want) <= 1e-5
+
+
+@pytest.mark.parametrize("prec,tol", [("tf32", 1e-3), ("tf32x3", 1e-5)])
+@pytest.mark.parametrize("p,d,bias", [(1, 1, True), (2, 2, False), (0, 1, True)])
+def test_conv_transpose2d_tensor_core(dev, orc, prec, tol, p, d, bias):
+    """Stride-1 conv_transpose2d (the conv backward's input gradient) on the
+    tensor-core implicit GEMM: conv2d with the channel-swapped, tap-reversed
+    weight and padding d*(k-1)-p, against the oracle's restatement of the
+    reference shader."""
+    n, cin, h, w, cout, k = 2, 96, 32, 24, 64, 3
+    r = np.random.default_rng(p * 10 + d)
+    x = r.standard_normal(n * cin * h * w).astype(np.float32)
+    wt = (r.standard_normal(cin * cout * k * k) * 0.05).astype(np.float32)
+    b = r.standard_normal(cout).astype(np.float32) if bias else None
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.conv_transpose2d(dev.upload(x), dev.upload(wt),
+                                            dev.upload(b) if bias else None, n, cin, h, w, cout,
+                                            k, k, (1, 1), (p, p), (0, 0), (d, d), 1))
+    finally:
+        dev.set_precision("tf32")
+    want = orc.conv_transpose2d(x, wt, b, n, cin, h, w, cout, k, k, (1, 1), (p, p), (0, 0),
+                                (d, d), 1)
+    assert orc.rel_fro(got, want) <= tol
 
 
 def _attn64(q, k, v, bh, s, d, causal=False, rows=None):
