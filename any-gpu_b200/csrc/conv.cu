@@ -158,6 +158,91 @@ struct ConvPairPolicy : ConvPolicy<BN_> {
   }
 };
 
+// Weight gradient (conv2d_grad_weight, stride 1) as implicit GEMMs, one per
+// kernel tap: dW_tap[oc, ic] = sum over pixels of gy[oc, pix] * x_tap[pix, ic]
+// with x_tap the input shifted by the tap.  A = gy read in place (K-major:
+// 32 consecutive output pixels of one row per K-block), B = the NHWC-staged
+// input (MN-major: 32 channels x the same 32 pixels, shifted by the tap, the
+// halo zero-filled by TMA).  The pixel sum (N*Ho*Wo long) is split into
+// `segs` K ranges so the few output tiles fill the GPU; each range writes its
+// partial tile to a workspace [seg][Cout][tap][Cin] and a second kernel sums
+// the ranges in order into dW [Cout][Cin][KH][KW].
+template <int BN_>
+struct WgradPolicy {
+  static constexpr int BN = BN_;
+  static constexpr bool A_MN = false, B_MN = true;
+  int cout, cin, kw, ph, pw, dh, dw, wo;
+  int bpr, bpi, n_img;           // K-blocks per output row / per image, images
+  int tiles_m, tiles_n, taps, segs, kper;
+  long long tiles;
+  float* ws;                     // [segs][cout][taps][cin]
+
+  struct Tile { int oc0, tap, ic0, seg; };
+
+  __device__ long long num_tiles() const { return tiles; }
+  __device__ int num_k() const { return kper; }
+
+  // output-channel tiles innermost: consecutive CTAs share the shifted input
+  __device__ Tile tile(long long t) const {
+    Tile r;
+    r.oc0 = (int)(t % tiles_m) * BM;
+    long long q = t / tiles_m;
+    r.ic0 = (int)(q % tiles_n) * BN;
+    q /= tiles_n;
+    r.tap = (int)(q % taps);
+    r.seg = (int)(q / taps);
+    return r;
+  }
+
+  __device__ void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* sa, uint8_t* sb,
+                       uint64_t* bar, const Tile& t, int kb) const {
+    // blocks past the last image read out of range: TMA fills zeros
+    const long long g = (long long)t.seg * kper + kb;
+    const int img = (int)(g / bpi), rem = (int)(g % bpi);
+    const int oh = rem / bpr, ow0 = (rem % bpr) * 32;
+    ptx::tma_load_3d(sa, ta, bar, oh * wo + ow0, t.oc0, img);
+    const int kh_i = t.tap / kw, kw_i = t.tap % kw;
+#pragma unroll
+    for (int j = 0; j < BN / 32; ++j)
+      ptx::tma_load_4d(sb + j * BK * 128, tb, bar, t.ic0 + 32 * j, ow0 + kw_i * dw - pw,
+                       oh + kh_i * dh - ph, img);
+  }
+
+  __device__ bool col_live(const Tile& t, int col0) const { return t.ic0 + col0 < cin; }
+
+  __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float*, int,
+                        bool accumulate, bool) const {
+    const int oc = t.oc0 + row;
+    if (oc >= cout) return;
+    float* dst = ws + (((long long)t.seg * cout + oc) * taps + t.tap) * cin + t.ic0 + col0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (t.ic0 + col0 + j < cin) {
+        if (accumulate) dst[j] += __uint_as_float(v[j]);
+        else dst[j] = __uint_as_float(v[j]);
+      }
+    }
+  }
+};
+
+// dW[oc][ic][kh][kw] = sum over seg of ws[seg][oc][tap][ic], in seg order.
+__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restrict__ gw, int segs,
+                                    int cout, int cin, int taps) {
+  const long long total = (long long)cout * cin * taps;
+  const long long plane = total;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int tap = (int)(i % taps);
+    const long long r = i / taps;
+    const int ic = (int)(r % cin);
+    const int oc = (int)(r / cin);
+    const long long src = ((long long)oc * taps + tap) * cin + ic;
+    float sum = 0.f;
+    for (int sg = 0; sg < segs; ++sg) sum += __ldg(ws + sg * plane + src);
+    gw[i] = sum;
+  }
+}
+
 // NCHW [N, C, HW] -> NHWC [N, HW, Cs] (channels >= C zero-filled).
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int C,
                                     int HW, int Cs) {
@@ -473,6 +558,91 @@ agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float*
   return run_conv_tc<64, X3, false>(dev, p, x, w, bias, y, s);
 }
 
+template <int BN, bool X3>
+agpu_status run_wgrad_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* gy,
+                         float* gw, cudaStream_t s) {
+  using P = WgradPolicy<BN>;
+  using Cfg = umma::Cfg<BN, X3>;
+  P pol;
+  pol.cout = p.cout; pol.cin = p.cin; pol.kw = p.kw;
+  pol.ph = p.ph; pol.pw = p.pw; pol.dh = p.dh; pol.dw = p.dw; pol.wo = p.wo;
+  pol.bpr = p.wo / 32;
+  pol.bpi = p.ho * pol.bpr;
+  pol.n_img = p.n;
+  pol.tiles_m = (int)ceil_div(p.cout, BM);
+  pol.tiles_n = (int)ceil_div(p.cin, BN);
+  pol.taps = p.kh * p.kw;
+  // K split: the fewest ranges (each at least 32 K-blocks) whose tiles fill
+  // the SMs' waves to 90 %; every range adds a partial weight-sized tensor of
+  // workspace traffic.
+  const long long base = (long long)pol.tiles_m * pol.tiles_n * pol.taps;
+  const long long kblocks = (long long)p.n * pol.bpi;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int sg = 1; sg <= 64; ++sg) {
+    if (sg > 1 && kblocks / sg < 32) break;
+    const long long units = base * sg;
+    const long long waves = (units + dev->sm_count - 1) / dev->sm_count;
+    const double eff = (double)units / (double)(waves * dev->sm_count);
+    if (eff > best_eff + 1e-9) { best_eff = eff; best = sg; }
+    if (eff >= 0.9) break;
+  }
+  pol.segs = best;
+  pol.kper = (int)ceil_div(kblocks, best);
+  pol.tiles = base * best;
+  const int Cs = (p.cin + 3) / 4 * 4;
+  const uint64_t xs_elems = (uint64_t)p.n * p.h * p.w * Cs;
+  const uint64_t ws_elems = (uint64_t)best * p.cout * pol.taps * p.cin;
+  void* scratch = nullptr;
+  AGPU_TRY(pool_alloc(dev, (xs_elems + ws_elems) * sizeof(float) + 256, &scratch, s));
+  float* xs = static_cast<float*>(scratch);
+  pol.ws = xs + (xs_elems + 63) / 64 * 64;
+  {
+    dim3 grid((unsigned)ceil_div((uint64_t)p.h * p.w, 32), (unsigned)ceil_div(Cs, 32), p.n);
+    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xs, p.cin, p.h * p.w, Cs);
+  }
+  agpu_status st = after_launch(dev, "wgrad staging");
+  CUtensorMap ta, tb;
+  if (st == AGPU_OK)
+    st = make_tmap_f32_3d(&ta, gy, (uint64_t)p.ho * p.wo, p.cout, p.n,
+                          (uint64_t)p.cout * p.ho * p.wo, 32, BM, false, !X3);
+  if (st == AGPU_OK) {
+    EncodeTiledFn enc = encode_fn();
+    cuuint64_t dims[4] = {(cuuint64_t)Cs, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
+    cuuint64_t strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)p.w * Cs * 4,
+                             (cuuint64_t)p.h * p.w * Cs * 4};
+    cuuint32_t box[4] = {32, 32, 1, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc ? enc(&tb, X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32,
+                           4, xs, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
+                     : CUDA_ERROR_NOT_FOUND;
+    if (r != CUDA_SUCCESS) st = fail(AGPU_ERR_CUDA, "conv2d_grad_weight: input map (%d)", (int)r);
+  }
+  if (st == AGPU_OK) {
+    auto kern = umma::umma_tf32_kernel<P, X3>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM);
+    if (e != cudaSuccess) {
+      st = cuda_status(e, "wgrad attr");
+    } else {
+      const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
+      kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
+      st = after_launch(dev, "conv2d_grad_weight (umma_tf32_kernel)");
+    }
+  }
+  if (st == AGPU_OK) {
+    const long long total = (long long)p.cout * p.cin * pol.taps;
+    wgrad_reduce_kernel<<<grid_for(dev, total), 256, 0, s>>>(pol.ws, gw, best, p.cout, p.cin,
+                                                             pol.taps);
+    st = after_launch(dev, "wgrad_reduce_kernel");
+  }
+  pool_free(dev, scratch, s);
+  return st;
+}
+
 }  // namespace
 
 bool conv_tc_eligible(const ConvParams& p) {
@@ -531,6 +701,18 @@ agpu_status launch_conv2d_grad_weight(agpu_device* dev, const ConvParams& p, con
                                       const float* gy, float* gw, cudaStream_t s) {
   const long long nw = (long long)p.cout * (p.cin / p.groups) * p.kh * p.kw;
   if (nw == 0) return AGPU_OK;
+  // tensor cores: stride 1, one group, output rows in whole 32-pixel blocks
+  if (dev->precision != AGPU_PREC_FFMA && p.groups == 1 && p.sh == 1 && p.sw == 1 &&
+      p.wo % 32 == 0 && p.n > 0 && p.n <= 65535 &&
+      (long long)p.n * p.cout * p.ho * p.wo * p.cin * p.kh * p.kw >= (1LL << 22)) {
+    if (dev->precision == AGPU_PREC_TF32X3) {
+      if (p.cin > 128) return run_wgrad_tc<256, true>(dev, p, x, gy, gw, s);
+      return run_wgrad_tc<128, true>(dev, p, x, gy, gw, s);
+    }
+    if (p.cin % 160 == 0 && p.cin % 256 != 0) return run_wgrad_tc<160, false>(dev, p, x, gy, gw, s);
+    if (p.cin > 128) return run_wgrad_tc<256, false>(dev, p, x, gy, gw, s);
+    return run_wgrad_tc<128, false>(dev, p, x, gy, gw, s);
+  }
   if (nw > 0x7fffffffLL) return fail(AGPU_ERR_UNSUPPORTED, "conv2d_grad_weight: too many weights");
   conv2d_grad_weight_kernel<<<(unsigned)nw, 256, 0, s>>>(x, gy, gw, p.n, p.cin, p.h, p.w, p.cout,
                                                          p.ho, p.wo, p.kh, p.kw, p.sh, p.sw, p.ph,

@@ -394,6 +394,27 @@ def test_conv_transpose2d_tensor_core(dev, orc, prec, tol, p, d, bias):
     assert orc.rel_fro(got, want) <= tol
 
 
+@pytest.mark.parametrize("prec,tol", [("tf32", 1e-3), ("tf32x3", 1e-5)])
+@pytest.mark.parametrize("cin,cout,p,d", [(96, 64, 1, 1), (320, 160, 2, 2), (40, 48, 1, 1)])
+def test_conv2d_grad_weight_tensor_core(dev, orc, prec, tol, cin, cout, p, d):
+    """Stride-1 weight gradient as per-tap implicit GEMMs on the tensor cores
+    (K split over pixel ranges, ranges summed in order), against the oracle's
+    restatement of the reference shader."""
+    n, h, w, k = 2, 16, 64, 3
+    ho, wo = h + 2 * p - d * (k - 1), w + 2 * p - d * (k - 1)
+    r = np.random.default_rng(cin + p)
+    x = r.standard_normal(n * cin * h * w).astype(np.float32)
+    gy = r.standard_normal(n * cout * ho * wo).astype(np.float32)
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.conv2d_grad_weight(dev.upload(x), dev.upload(gy), n, cin, h, w, cout,
+                                              ho, wo, k, k, 1, 1, p, p, d, d, 1))
+    finally:
+        dev.set_precision("tf32")
+    want = orc.conv2d_grad_weight(x, gy, n, cin, h, w, cout, ho, wo, k, k, 1, 1, p, p, d, d, 1)
+    assert orc.rel_fro(got, want) <= tol
+
+
 def _attn64(q, k, v, bh, s, d, causal=False, rows=None):
     Q = q.reshape(bh, s, d).astype(np.float64)
     K = k.reshape(bh, s, d).astype(np.float64)
