@@ -388,3 +388,31 @@ class GpuDevice:
                        stream: int = 0) -> None:
         _check(_lib.load().agpu_launch_softmax(self._h, x_ptr, y_ptr, rows, cols,
                                                stream or None))
+
+
+class AdamW:
+    """Mirror of the reference optimizer (src/optim.rs:53-138): lr, beta1 0.9,
+    beta2 0.999, eps 1e-8, weight_decay 0.01; moment buffers created (zero) on
+    the first step; each step updates every parameter buffer in place in one
+    launch (agpu_adamw_step)."""
+
+    def __init__(self, lr: float):
+        self.lr, self.beta1, self.beta2, self.eps, self.weight_decay = lr, 0.9, 0.999, 1e-8, 0.01
+        self.step_count = 0
+        self.states: list[tuple[GpuBuffer, GpuBuffer]] = []
+
+    def step(self, dev: "GpuDevice", params: list, grads: list) -> None:
+        """Reference: `AdamW::step(dev, params, grads)` (src/optim.rs:82)."""
+        if len(params) != len(grads):
+            raise AnyGpuError(1, "params/grads length mismatch")
+        self.step_count += 1
+        while len(self.states) < len(params):
+            n = params[len(self.states)].len
+            self.states.append((dev.alloc(n), dev.alloc(n)))  # zero-filled
+        k = len(params)
+        arr = lambda bufs: (C.c_void_p * max(k, 1))(*[b.handle for b in bufs])
+        _check(_lib.load().agpu_adamw_step(
+            dev._h, arr(params), arr(grads), arr([s[0] for s in self.states[:k]]),
+            arr([s[1] for s in self.states[:k]]), k, C.c_float(self.lr), C.c_float(self.beta1),
+            C.c_float(self.beta2), C.c_float(self.eps), C.c_float(self.weight_decay),
+            self.step_count))

@@ -86,6 +86,10 @@ SIGNATURES: dict[str, tuple] = {
                                           C.c_void_p]),
     "agpu_launch_group_norm_backward": (c_status, [c_dev] + [C.c_void_p] * 6 +
                                         [u32, u32, u32, u32, f32, C.c_void_p]),
+    "agpu_adamw_step": (c_status, [c_dev] + [C.POINTER(C.c_void_p)] * 4 +
+                        [u32, f32, f32, f32, f32, f32, u32]),
+    "agpu_launch_adamw": (c_status, [c_dev, C.c_void_p, u32, f32, f32, f32, f32, f32, u32,
+                                     C.c_void_p]),
     "agpu_launch_sdpa": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32, u32, u32, i32,
                                                                  C.c_void_p]),
     "agpu_launch_gemm_ex": (c_status, [c_dev] + [C.c_void_p] * 3 + [u32] * 4 + [i32, i32]

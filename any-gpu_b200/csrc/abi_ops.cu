@@ -4,6 +4,8 @@
 // `impl GpuDevice`: the same argument order and meaning, the same size
 // checks (returned as AGPU_ERR_SHAPE where the reference's `ensure!` returns
 // Err), a freshly allocated output buffer owned by the caller.
+#include <vector>
+
 #include "agpu_internal.cuh"
 
 using namespace agpu;
@@ -346,6 +348,31 @@ extern "C" agpu_status agpu_group_norm_backward(agpu_device* dev, const agpu_buf
   return AGPU_OK;
 }
 
+// ----------------------------------------------------------------- AdamW --
+extern "C" agpu_status agpu_adamw_step(agpu_device* dev, agpu_buffer* const* params,
+                                       const agpu_buffer* const* grads, agpu_buffer* const* m,
+                                       agpu_buffer* const* v, uint32_t count, float lr,
+                                       float beta1, float beta2, float eps, float weight_decay,
+                                       uint32_t step) {
+  CHECK_DEV(dev, "adamw_step");
+  if (count && (!params || !grads || !m || !v))
+    return fail(AGPU_ERR_INVALID, "adamw_step: NULL array");
+  std::vector<agpu_adamw_tensor> t(count);
+  for (uint32_t i = 0; i < count; ++i) {
+    if (!params[i] || !grads[i] || !m[i] || !v[i])
+      return fail(AGPU_ERR_INVALID, "adamw_step: NULL buffer at index %u", i);
+    // src/optim.rs:95
+    if (params[i]->len != grads[i]->len || m[i]->len != params[i]->len ||
+        v[i]->len != params[i]->len)
+      return fail(AGPU_ERR_SHAPE, "adamw_step: param/grad size mismatch at index %u", i);
+    t[i] = agpu_adamw_tensor{params[i]->dptr, grads[i]->dptr, m[i]->dptr, v[i]->dptr,
+                             params[i]->len};
+  }
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  return launch_adamw(dev, t.data(), count, lr, beta1, beta2, eps, weight_decay, step,
+                      dev->stream);
+}
+
 // --------------------------------------------------------- gemm epilogue --
 extern "C" agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
                                     const agpu_buffer* bias, const agpu_buffer* resid,
@@ -572,6 +599,15 @@ agpu_status agpu_launch_group_norm_backward(agpu_device* dev, const float* grad_
     return fail(AGPU_ERR_SHAPE, "launch_group_norm_backward: channels must be divisible by groups");
   return launch_group_norm_backward(dev, grad_out, input, gamma, d_input, d_gamma, d_beta, batch,
                                     channels, spatial, groups, eps, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_adamw(agpu_device* dev, const agpu_adamw_tensor* tensors,
+                              uint32_t count, float lr, float beta1, float beta2, float eps,
+                              float weight_decay, uint32_t step, void* stream) {
+  CHECK_DEV(dev, "launch_adamw");
+  if (count && !tensors) return fail(AGPU_ERR_INVALID, "launch_adamw: NULL tensor array");
+  return launch_adamw(dev, tensors, count, lr, beta1, beta2, eps, weight_decay, step,
+                      pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k, const float* v,

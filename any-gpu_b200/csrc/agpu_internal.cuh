@@ -105,6 +105,9 @@ agpu_status launch_group_norm_backward(agpu_device* dev, const float* dy, const 
                                        float* dbeta, uint32_t batch, uint32_t channels,
                                        uint32_t spatial, uint32_t groups, float eps,
                                        cudaStream_t s);
+agpu_status launch_adamw(agpu_device* dev, const agpu_adamw_tensor* tensors, uint32_t count,
+                         float lr, float beta1, float beta2, float eps, float weight_decay,
+                         uint32_t step, cudaStream_t s);
 
 agpu_status launch_rmsnorm(agpu_device* dev, const float* x, const float* w, float* y,
                            uint64_t rows, uint32_t cols, float eps, cudaStream_t s);

@@ -218,10 +218,20 @@ agpu_status agpu_upload(agpu_device* dev, const float* host, uint64_t n, agpu_bu
   return AGPU_OK;
 }
 
+// Zero-filled, as the reference's wgpu buffers are (src/device.rs:97-112).
 agpu_status agpu_alloc(agpu_device* dev, uint64_t n, agpu_buffer** out) {
   if (!dev || !out) return fail(AGPU_ERR_INVALID, "agpu_alloc: bad argument");
   AGPU_CUDA(cudaSetDevice(dev->ordinal));
-  return new_buffer(dev, n, out);
+  AGPU_TRY(new_buffer(dev, n, out));
+  if (n) {
+    const cudaError_t e = cudaMemsetAsync((*out)->dptr, 0, n * sizeof(float), dev->stream);
+    if (e != cudaSuccess) {
+      agpu_buffer_free(*out);
+      *out = nullptr;
+      return cuda_status(e, "agpu_alloc: zero fill");
+    }
+  }
+  return AGPU_OK;
 }
 
 agpu_status agpu_write(agpu_device* dev, agpu_buffer* buf, const float* host, uint64_t n) {

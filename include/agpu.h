@@ -87,7 +87,8 @@ AGPU_API uint64_t agpu_device_launch_count(const agpu_device* dev);
 /* Replaces GpuDevice::upload (src/device.rs:80-94): H2D copy of n f32. */
 AGPU_API agpu_status agpu_upload(agpu_device* dev, const float* host, uint64_t n,
                                  agpu_buffer** out);
-/* Replaces GpuDevice::alloc (src/device.rs:97-112). Contents undefined. */
+/* Replaces GpuDevice::alloc (src/device.rs:97-112).  Zero-filled, as the
+ * reference's wgpu buffers are (the fill is ordered on the device stream). */
 AGPU_API agpu_status agpu_alloc(agpu_device* dev, uint64_t n, agpu_buffer** out);
 /* Replaces GpuDevice::read (src/device.rs:115-145): blocking D2H of the
  * whole buffer; `n` must equal the buffer length. */
@@ -275,6 +276,32 @@ AGPU_API agpu_status agpu_transpose(agpu_device* dev, const agpu_buffer* a, uint
 AGPU_API agpu_status agpu_add_per_col(agpu_device* dev, const agpu_buffer* a,
                                       const agpu_buffer* b, uint32_t rows, uint32_t cols,
                                       agpu_buffer** out);
+
+/* ---------------------------------------------------------------- AdamW -- */
+/* One AdamW step (the reference's AdamW::step, src/optim.rs:82-138, and its
+ * shader :22-51) for `count` parameter tensors in one launch:
+ *   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2
+ *   p = p (1 - lr wd) - lr (m / (1 - b1^t)) / (sqrt(v / (1 - b2^t)) + eps)
+ * with t = `step` (>= 1; the reference increments its counter before the
+ * update).  params, m, v are updated in place; m and v start at zero.  A
+ * param/grad/m/v length mismatch -> AGPU_ERR_SHAPE (src/optim.rs:95). */
+AGPU_API agpu_status agpu_adamw_step(agpu_device* dev, agpu_buffer* const* params,
+                                     const agpu_buffer* const* grads, agpu_buffer* const* m,
+                                     agpu_buffer* const* v, uint32_t count, float lr,
+                                     float beta1, float beta2, float eps, float weight_decay,
+                                     uint32_t step);
+/* The same on caller-owned device memory: a host array of tensors. */
+typedef struct agpu_adamw_tensor {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  uint64_t n;
+} agpu_adamw_tensor;
+AGPU_API agpu_status agpu_launch_adamw(agpu_device* dev, const agpu_adamw_tensor* tensors,
+                                       uint32_t count, float lr, float beta1, float beta2,
+                                       float eps, float weight_decay, uint32_t step,
+                                       void* stream);
 
 /* ------------------------------------------------ launch layer (raw ptrs) -- */
 /* Same kernels on caller-owned device memory; `stream` is a cudaStream_t

@@ -578,3 +578,31 @@ void oracle_rope(const float* x, float* out, int64_t batch, int64_t seq, int64_t
         }
       }
 }
+
+/* f32 powi as Rust lowers it (square-and-multiply in f32). */
+static float powi_f32(float a, int64_t b) {
+  float r = 1.0f;
+  for (;;) {
+    if (b & 1) r *= a;
+    b >>= 1;
+    if (b == 0) break;
+    a *= a;
+  }
+  return r;
+}
+
+/* oracle_adamw: one AdamW step on one tensor, SHADER_ADAMW
+ * (src/optim.rs:22-51) element by element, with beta^t as AdamW::step
+ * computes it (src/optim.rs:84-86: f32 powi). */
+void oracle_adamw(float* param, const float* grad, float* m, float* v, int64_t n, float lr,
+                  float beta1, float beta2, float eps, float weight_decay, int64_t step) {
+  const float b1t = powi_f32(beta1, step), b2t = powi_f32(beta2, step);
+  for (int64_t i = 0; i < n; ++i) {
+    const float g = grad[i];
+    m[i] = beta1 * m[i] + (1.0f - beta1) * g;
+    v[i] = beta2 * v[i] + (1.0f - beta2) * g * g;
+    const float m_hat = m[i] / (1.0f - b1t);
+    const float v_hat = v[i] / (1.0f - b2t);
+    param[i] = param[i] * (1.0f - lr * weight_decay) - lr * m_hat / (sqrtf(v_hat) + eps);
+  }
+}

@@ -46,6 +46,7 @@ _SIG = {
     "oracle_add_per_col": (None, [_p, _p, _p, _i64, _i64]),
     "oracle_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f32]),
     "oracle_rope": (None, [_p, _p, _i64, _i64, _i64, _i64, _f32]),
+    "oracle_adamw": (None, [_p, _p, _p, _p, _i64, _f32, _f32, _f32, _f32, _f32, _i64]),
 }
 
 ELEMENTWISE = {"add": 0, "sub": 1, "mul": 2, "relu": 3, "sigmoid": 4, "swish": 5, "tanh": 6,
@@ -239,3 +240,11 @@ def rel_fro(got, want) -> float:
     w = np.asarray(want, np.float64).reshape(-1)
     den = np.linalg.norm(w)
     return float(np.linalg.norm(g - w) / (den if den > 0 else 1.0))
+
+
+def adamw(param, grad, m, v, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=1):
+    """One AdamW step (updates copies; returns (param, m, v))."""
+    p, g, mm, vv = (np.array(_a(t), copy=True) for t in (param, grad, m, v))
+    lib().oracle_adamw(_ptr(p), _ptr(g), _ptr(mm), _ptr(vv), p.size, lr, beta1, beta2, eps,
+                       weight_decay, step)
+    return p, mm, vv

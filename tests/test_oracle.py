@@ -168,3 +168,37 @@ def test_oracle_group_norm_backward_vs_autograd(orc, n, c, s, g):
     want = gn_backward_f64(dy, x, gamma, n, c, s, g, 1e-5)
     for a, b in zip(got, want):
         assert orc.rel_fro(a, b) <= 1e-4
+
+
+def test_oracle_adamw_vs_float64(orc):
+    """The oracle's restatement of SHADER_ADAMW (src/optim.rs:22-51) against the
+    same update in float64 (the reference has no test of its own for AdamW)."""
+    r = np.random.default_rng(11)
+    n = 1000
+    p, g = r.standard_normal(n).astype(np.float32), r.standard_normal(n).astype(np.float32)
+    m, v = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    P, M, V = p.astype(np.float64), np.zeros(n), np.zeros(n)
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.999, 1e-8, 0.01
+    for t in (1, 2, 3):
+        p, m, v = orc.adamw(p, g, m, v, lr, b1, b2, eps, wd, t)
+        M = b1 * M + (1 - b1) * g
+        V = b2 * V + (1 - b2) * g.astype(np.float64) ** 2
+        P = P * (1 - lr * wd) - lr * (M / (1 - b1 ** t)) / (np.sqrt(V / (1 - b2 ** t)) + eps)
+    # v differs by ~1e-5: the shader's 1 - beta2 is 0.0009999871 in f32
+    assert orc.rel_fro(p, P) <= 1e-6 and orc.rel_fro(m, M) <= 1e-6 and orc.rel_fro(v, V) <= 1e-4
+
+
+def test_oracle_adamw_reference_tests(orc):
+    """The reference's own AdamW tests (src/optim.rs:149-240), on the oracle."""
+    one = lambda *x: np.array(x, np.float32)
+    z = lambda n: np.zeros(n, np.float32)
+    p, _, _ = orc.adamw(one(1, 2, 3), one(0.1, 0.2, 0.3), z(3), z(3), 0.01, weight_decay=0.0)
+    assert (p < one(1, 2, 3)).all()                                  # test_adamw_basic
+    p, m, v = one(10), z(1), z(1)
+    for t in range(1, 11):                                           # test_adamw_multiple_steps
+        p, m, v = orc.adamw(p, one(1), m, v, 0.1, weight_decay=0.0, step=t)
+    assert p[0] < 10.0
+    p, _, _ = orc.adamw(one(10), one(0), z(1), z(1), 0.01, weight_decay=0.1)
+    assert abs(p[0] - 9.99) <= 1e-3                                  # test_adamw_weight_decay
+    p, _, _ = orc.adamw(one(5), one(-1), z(1), z(1), 0.01, weight_decay=0.0)
+    assert p[0] > 5.0                                                # test_adamw_negative_gradient

@@ -415,6 +415,77 @@ def test_conv2d_grad_weight_tensor_core(dev, orc, prec, tol, cin, cout, p, d):
     assert orc.rel_fro(got, want) <= tol
 
 
+def test_adamw_multi_tensor(dev, orc):
+    """AdamW (src/optim.rs:53-138) over three steps on tensors of ragged sizes
+    (one launch per step), against the oracle's restatement of the shader."""
+    from any_gpu import AdamW
+    r = np.random.default_rng(21)
+    sizes = [1, 7, 1000, (1 << 20) + 3, 4096]
+    ps = [r.standard_normal(n).astype(np.float32) for n in sizes]
+    bufs = [dev.upload(p) for p in ps]
+    opt = AdamW(lr=1e-3)
+    ms = [np.zeros(n, np.float32) for n in sizes]
+    vs = [np.zeros(n, np.float32) for n in sizes]
+    for t in (1, 2, 3):
+        gs = [r.standard_normal(n).astype(np.float32) for n in sizes]
+        opt.step(dev, bufs, [dev.upload(g) for g in gs])
+        for i in range(len(sizes)):
+            ps[i], ms[i], vs[i] = orc.adamw(ps[i], gs[i], ms[i], vs[i], 1e-3, 0.9, 0.999, 1e-8,
+                                            0.01, t)
+    # per element: the GPU contracts a*b + c into one FMA where the oracle
+    # rounds twice, and m = 0.9 m + 0.1 g can nearly cancel for a single value
+    for i, b in enumerate(bufs):
+        np.testing.assert_allclose(dev.read(b), ps[i], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(dev.read(opt.states[i][0]), ms[i], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(dev.read(opt.states[i][1]), vs[i], rtol=1e-5, atol=1e-6)
+
+
+def test_adamw_reference_tests(dev):
+    """The reference's AdamW tests (src/optim.rs:149-240) through AdamW.step."""
+    from any_gpu import AdamW
+    up = lambda *x: dev.upload(np.array(x, np.float32))
+    opt = AdamW(lr=0.01)
+    opt.weight_decay = 0.0
+    p = up(1, 2, 3)
+    opt.step(dev, [p], [up(0.1, 0.2, 0.3)])
+    assert (dev.read(p) < np.array([1, 2, 3], np.float32)).all()
+    opt, p, g = AdamW(lr=0.1), up(10), up(1)
+    opt.weight_decay = 0.0
+    for _ in range(10):
+        opt.step(dev, [p], [g])
+    assert dev.read(p)[0] < 10.0
+    opt, p = AdamW(lr=0.01), up(10)
+    opt.weight_decay = 0.1
+    opt.step(dev, [p], [up(0)])
+    assert abs(dev.read(p)[0] - 9.99) <= 1e-3
+    opt, p = AdamW(lr=0.01), up(5)
+    opt.weight_decay = 0.0
+    opt.step(dev, [p], [up(-1)])
+    assert dev.read(p)[0] > 5.0
+    opt, p = AdamW(lr=0.0), up(10)                     # test_adamw_lr_zero
+    opt.weight_decay = 0.0
+    opt.step(dev, [p], [up(100)])
+    assert abs(dev.read(p)[0] - 10.0) <= 1e-5
+    opt = AdamW(lr=0.001)                              # test_adamw_defaults
+    assert (opt.lr, opt.beta1, opt.beta2, opt.eps, opt.weight_decay) == (0.001, 0.9, 0.999, 1e-8,
+                                                                          0.01)
+
+
+def test_adamw_errors(dev):
+    from any_gpu import AdamW, AnyGpuError
+    opt = AdamW(lr=1e-3)
+    with pytest.raises(AnyGpuError) as e:  # src/optim.rs:95
+        opt.step(dev, [dev.upload(np.ones(4, np.float32))], [dev.upload(np.ones(5, np.float32))])
+    assert e.value.status == 1
+    with pytest.raises(AnyGpuError):  # src/optim.rs:83: two params, one grad
+        AdamW(lr=0.01).step(dev, [dev.upload(np.ones(1, np.float32))] * 2,
+                            [dev.upload(np.ones(1, np.float32))])
+
+
+def test_alloc_is_zero_filled(dev):
+    assert not dev.read(dev.alloc(12345)).any()
+
+
 def _attn64(q, k, v, bh, s, d, causal=False, rows=None):
     Q = q.reshape(bh, s, d).astype(np.float64)
     K = k.reshape(bh, s, d).astype(np.float64)
