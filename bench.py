@@ -52,9 +52,16 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "TFLOPS (matmul, SDPA) and GB/s (softmax/norm) at 1/2/4/8 B200, % of roofline"
 
-# DRAM bytes per launch of the dominant kernel from an ncu capture (see
-# profiles/), or None when not captured for the current kernel and workload.
-TRAFFIC_BYTES = {"bmm_softmax": 3.5e9}
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of that kernel (dram__bytes_read.sum + dram__bytes_write.sum), for
+# the default workload sizes; where the capture ran a smaller case, scaled by
+# the units processed.
+TRAFFIC_BYTES = {
+    "bmm_softmax": 3.5e9,  # pair GEMM, batch-8 capture x 8
+    "sdpa": 0.99e9,        # attention_pair_kernel, 64-head capture x 4
+    "unet": 1.21e8,        # conv kernel, full workload
+    "llama": 2.39e10,      # gate/up GEMM, batch-2 capture x 16
+}
 
 
 def load_peaks() -> dict:
@@ -686,7 +693,9 @@ def run_agpu(args, world, rank, local):
         achieved = wl.dom_flops / (dom_ms * 1e-3) / 1e12
         h2d, d2h = wl.e2e_bytes()
         traffic = TRAFFIC_BYTES.get(wl.name)
-        if wl.name == "bmm_softmax" and args.batch != 64:
+        default_size = {"bmm_softmax": args.batch == 64, "sdpa": args.bh == 256 and args.seq == 2048,
+                        "unet": args.images == 16, "llama": args.llama_batch == 32}
+        if not default_size.get(wl.name, False):
             traffic = None
         line = base_line(args, world, wl)
         line.update({
