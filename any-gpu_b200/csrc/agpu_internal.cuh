@@ -72,6 +72,18 @@ inline cudaStream_t pick_stream(agpu_device* dev, void* s) {
 
 // After a launch: record it and turn launch errors into a status.
 agpu_status after_launch(agpu_device* dev, const char* kernel, int n_launches = 1);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and device
+// (a driver call on every launch otherwise; the value never changes).
+template <auto Kernel>
+cudaError_t set_smem_once(const agpu_device* dev, int bytes) {
+  static std::atomic<uint64_t> done{0};
+  const uint64_t bit = 1ull << (dev->ordinal & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Read back and clear the device status word (non-zero = a bounded wait expired).
 agpu_status check_device_status(agpu_device* dev);

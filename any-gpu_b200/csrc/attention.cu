@@ -1042,7 +1042,7 @@ agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, c
   AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0)};
   AttnQ qin{q, sd.q[0], sd.q[1], sd.q[2]};
   auto kern = attention_tf32_kernel<D, CAUSAL>;
-  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+  AGPU_CUDA((set_smem_once<attention_tf32_kernel<D, CAUSAL>>(dev, C::SMEM)));
   AttnTiles tiles;
   tiles.nqt = (int)ceil_div(s, QT);
   tiles.H = H;
@@ -1067,7 +1067,7 @@ agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k,
   AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0)};
   AttnQ qin{q, sd.q[0], sd.q[1], sd.q[2]};
   auto kern = attention_pair_kernel<D, CAUSAL>;
-  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+  AGPU_CUDA((set_smem_once<attention_pair_kernel<D, CAUSAL>>(dev, C::SMEM)));
   AttnTiles tiles;
   tiles.nqt = (int)ceil_div(s, 2 * QT);
   tiles.H = H;

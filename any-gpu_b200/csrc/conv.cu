@@ -518,8 +518,7 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   } else {
     using Cfg = umma::Cfg<BN, X3>;
     auto kern = umma::umma_tf32_kernel<P, X3>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::SMEM);
+    cudaError_t e = set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM);
     if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
     const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
     kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
@@ -623,8 +622,7 @@ agpu_status run_wgrad_tc(agpu_device* dev, const ConvParams& p, const float* x, 
   }
   if (st == AGPU_OK) {
     auto kern = umma::umma_tf32_kernel<P, X3>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::SMEM);
+    cudaError_t e = set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM);
     if (e != cudaSuccess) {
       st = cuda_status(e, "wgrad attr");
     } else {

@@ -347,7 +347,7 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   pol.resid = ep.resid;
   pol.act = ep.act;
   auto kern = umma::umma_tf32_kernel<P, X3>;
-  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+  AGPU_CUDA((set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM)));
   const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
   kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
   return after_launch(dev, "gemm_tf32 (umma_tf32_kernel)");

@@ -15,7 +15,7 @@ agpu_status launch_pair(agpu_device* dev, const CUtensorMap& ta, const CUtensorM
                         const P& pol, long long tiles, cudaStream_t s, const char* what) {
   using Cfg = umma::PairCfg<P::BN>;
   auto kern = umma::umma_tf32_pair_kernel<P>;
-  AGPU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+  AGPU_CUDA(set_smem_once<umma::umma_tf32_pair_kernel<P>>(dev, Cfg::SMEM));
   const long long clusters = std::min<long long>(tiles, std::max(1, dev->sm_count / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
