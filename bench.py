@@ -139,6 +139,11 @@ def _normal(r, n, scale=1.0):
     return x
 
 
+def _cores(orc, threads):
+    """Host threads a CPU sample uses: all of the oracle's pool, or one."""
+    return max(1, orc.num_threads()) if threads else 1
+
+
 # ----------------------------------------------------------- workloads ---
 class Workload:
     """One benchmark configuration.  Subclasses define the data, the device
@@ -181,7 +186,7 @@ class Workload:
         h2d = sum(v.numel() * 4 for v in self.host.values())
         return h2d, self.out_elems() * 4
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         raise NotImplementedError
 
     def extra(self, ms_step, ms_dom, peaks) -> dict:
@@ -236,17 +241,17 @@ class BmmSoftmax(Workload):
         for b in (ga, gb, gc, gs):
             b.free()
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         r = np.random.default_rng(1235)
         a = _normal(r, self.M * self.K, 0.05)
         b = _normal(r, self.K * self.N, 0.05)
-        chunk, done, t, start = max(16, 2 * orc.num_threads()), 0, 0.0, 0
+        chunk, done, t, start = max(16, 2 * _cores(orc, threads)), 0, 0.0, 0
         while t < target_s:
             rows = min(chunk, self.M - start)
             t0 = time.perf_counter()
             c = orc.matmul(a[start * self.K:(start + rows) * self.K], b, rows, self.N, self.K,
-                           threads=True)
-            orc.softmax(c, rows, self.N, threads=True)
+                           threads=threads)
+            orc.softmax(c, rows, self.N, threads=threads)
             t += time.perf_counter() - t0
             done += rows
             start = (start + rows) % self.M
@@ -308,14 +313,14 @@ class Matmul(Workload):
         for b in (ga, gb, gc):
             b.free()
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         a, b = self.host_inputs().values()
         n = self.n
-        chunk, done, t, start = max(8, orc.num_threads()), 0, 0.0, 0
+        chunk, done, t, start = max(8, _cores(orc, threads)), 0, 0.0, 0
         while t < target_s:
             rows = min(chunk, n - start)
             t0 = time.perf_counter()
-            orc.matmul(a[start * n:(start + rows) * n], b, rows, n, n, threads=True)
+            orc.matmul(a[start * n:(start + rows) * n], b, rows, n, n, threads=threads)
             t += time.perf_counter() - t0
             done += rows
             start = (start + rows) % n
@@ -369,15 +374,15 @@ class Sdpa(Workload):
         for b in g + [go]:
             b.free()
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         r = np.random.default_rng(1236)
         hsz = self.s * self.d
-        heads = max(1, orc.num_threads())
+        heads = _cores(orc, threads)
         q, k, v = (_normal(r, heads * hsz) for _ in range(3))
         done, t = 0, 0.0
         while t < target_s:
             t0 = time.perf_counter()
-            orc.attention(q, k, v, heads, self.s, self.d, threads=True)
+            orc.attention(q, k, v, heads, self.s, self.d, threads=threads)
             t += time.perf_counter() - t0
             done += heads
         return (4.0 * done * self.s * self.s * self.d / t / 1e12,
@@ -440,16 +445,16 @@ class Unet(Workload):
         for b in list(g.values()) + [y1, y]:
             b.free()
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         x, w, gamma, beta = self.host_inputs().values()
         img = self.c * self.h * self.w
         done, t = 0, 0.0
         while t < target_s:
             t0 = time.perf_counter()
             y = orc.conv2d(x[:img], w, None, 1, self.c, self.h, self.w, self.c, 3, 3, (1, 1),
-                           (1, 1), (1, 1), 1, threads=True)
+                           (1, 1), (1, 1), 1, threads=threads)
             y = orc.group_norm(y, gamma, beta, 1, self.c, self.h * self.w, self.g, 1e-5,
-                               threads=True)
+                               threads=threads)
             orc.elementwise("swish", y)
             t += time.perf_counter() - t0
             done += 1
@@ -534,17 +539,17 @@ class Llama(Workload):
         for b in list(g.values()) + list(ws.values()) + [y]:
             b.free()
 
-    def cpu_sample(self, orc, target_s):
+    def cpu_sample(self, orc, target_s, threads=True):
         dm = self.dims
         d = dm.d_model
         r = np.random.default_rng(1239)
         x = _normal(r, 64 * d)
         wqkv = _normal(r, d * 3 * d, 0.02)
         done, t = 0, 0.0
-        rows = max(8, orc.num_threads())
+        rows = max(8, _cores(orc, threads))
         while t < target_s:
             t0 = time.perf_counter()
-            orc.matmul(x[: rows * d], wqkv, rows, 3 * d, d, threads=True)
+            orc.matmul(x[: rows * d], wqkv, rows, 3 * d, d, threads=threads)
             t += time.perf_counter() - t0
             done += rows
         return (2.0 * done * d * 3 * d / t / 1e12,
@@ -719,6 +724,10 @@ def run_agpu(args, world, rank, local):
             v, sample = wl.cpu_sample(orc, args.cpu_seconds)
             line["cpu_baseline"] = {"value": v, "unit": "TFLOPS", "cores": orc.num_threads(),
                                     "kind": "port", "sample": sample}
+            if args.cpu_seconds_single > 0:
+                v1, sample1 = wl.cpu_sample(orc, args.cpu_seconds_single, threads=False)
+                line["cpu_baseline"]["single_thread"] = {"value": v1, "unit": "TFLOPS",
+                                                         "cores": 1, "sample": sample1}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -737,6 +746,8 @@ def main():
                     help="NCCL all-gather of the outputs inside each step")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds-single", type=float, default=5.0,
+                    help="bounded single-thread CPU sample beside the all-cores one (0: skip)")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64,
