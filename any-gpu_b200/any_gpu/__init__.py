@@ -358,6 +358,46 @@ class GpuDevice:
         """Reference: `add_per_col(a, b, rows, cols)` (src/ops/tensor_ops.rs:336)."""
         return self._new(_lib.load().agpu_add_per_col, a.handle, b.handle, rows, cols)
 
+    def add_broadcast(self, a, b, outer: int, inner: int):
+        """Reference: `add_broadcast(a, b, outer, inner)` (src/ops/tensor_ops.rs:298)."""
+        return self._new(_lib.load().agpu_add_broadcast, a.handle, b.handle, outer, inner)
+
+    def sum_inner(self, src, outer: int, inner: int):
+        """Reference: `sum_inner(src, outer, inner)` (src/ops/tensor_ops.rs:318)."""
+        return self._new(_lib.load().agpu_sum_inner, src.handle, outer, inner)
+
+    def sum_rows(self, src, rows: int, cols: int):
+        """Reference: `sum_rows(src, rows, cols)` (src/ops/tensor_ops.rs:356)."""
+        return self._new(_lib.load().agpu_sum_rows, src.handle, rows, cols)
+
+    def concat(self, a, b, outer_size: int, a_inner: int, b_inner: int):
+        """Reference: `concat(a, b, outer_size, a_inner, b_inner)` (src/ops/tensor_ops.rs:229)."""
+        return self._new(_lib.load().agpu_concat, a.handle, b.handle, outer_size, a_inner,
+                         b_inner)
+
+    def slice_per_block(self, src, outer: int, slice_size: int, slice_offset: int,
+                        combined: int):
+        """Reference: `slice_per_block(src, outer, slice_size, slice_offset, combined)`
+        (src/ops/tensor_ops.rs:274)."""
+        return self._new(_lib.load().agpu_slice_per_block, src.handle, outer, slice_size,
+                         slice_offset, combined)
+
+    def upsample_nearest2d(self, input, batch: int, channels: int, in_h: int, in_w: int,
+                           scale_h: int, scale_w: int):
+        """Reference: `upsample_nearest2d(...)` (src/ops/upsample.rs:94)."""
+        return self._new(_lib.load().agpu_upsample_nearest2d, input.handle, batch, channels,
+                         in_h, in_w, scale_h, scale_w)
+
+    def upsample_nearest2d_backward(self, grad_out, batch: int, channels: int, in_h: int,
+                                    in_w: int, scale_h: int, scale_w: int):
+        """Reference: `upsample_nearest2d_backward(...)` (src/ops/upsample.rs:116)."""
+        return self._new(_lib.load().agpu_upsample_nearest2d_backward, grad_out.handle, batch,
+                         channels, in_h, in_w, scale_h, scale_w)
+
+    def mse_loss(self, pred, target):
+        """Reference: `mse_loss(pred, target)` (src/ops/attention.rs:172): 1 element."""
+        return self._new(_lib.load().agpu_mse_loss, pred.handle, target.handle)
+
     # ------------------------------------------- launch layer (raw pointers) --
     def launch_batch_matmul(self, a_ptr: int, b_ptr: int, c_ptr: int, batch: int, m: int,
                             n: int, k: int, stream: int = 0) -> None:

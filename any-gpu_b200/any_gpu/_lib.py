@@ -76,6 +76,15 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_tanh_backward": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_transpose": (c_status, [c_dev, c_buf, u32, u32, u32, u32, P_buf]),
     "agpu_add_per_col": (c_status, [c_dev, c_buf, c_buf, u32, u32, P_buf]),
+    "agpu_add_broadcast": (c_status, [c_dev, c_buf, c_buf, u32, u32, P_buf]),
+    "agpu_sum_inner": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
+    "agpu_sum_rows": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
+    "agpu_concat": (c_status, [c_dev, c_buf, c_buf, u32, u32, u32, P_buf]),
+    "agpu_slice_per_block": (c_status, [c_dev, c_buf, u32, u32, u32, u32, P_buf]),
+    "agpu_upsample_nearest2d": (c_status, [c_dev, c_buf, u32, u32, u32, u32, u32, u32, P_buf]),
+    "agpu_upsample_nearest2d_backward": (c_status, [c_dev, c_buf, u32, u32, u32, u32, u32, u32,
+                                                    P_buf]),
+    "agpu_mse_loss": (c_status, [c_dev, c_buf, c_buf, P_buf]),
     "agpu_launch_batch_matmul": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
                                             u32, u32, u32, u32, C.c_void_p]),
     "agpu_launch_gemm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p, u32, u32, u32,

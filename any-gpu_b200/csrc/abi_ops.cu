@@ -546,6 +546,118 @@ agpu_status agpu_add_per_col(agpu_device* dev, const agpu_buffer* a, const agpu_
   });
 }
 
+agpu_status agpu_add_broadcast(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                               uint32_t outer, uint32_t inner, agpu_buffer** out) {
+  CHECK_DEV(dev, "add_broadcast");
+  CHECK_BUF(a, "add_broadcast", "A");
+  CHECK_BUF(b, "add_broadcast", "B");
+  CHECK_OUT(out, "add_broadcast");
+  // src/ops/tensor_ops.rs:303-304
+  CHECK_LEN(a, (uint64_t)outer * inner, "add_broadcast", "A");
+  CHECK_LEN(b, outer, "add_broadcast", "B");
+  return with_output(dev, (uint64_t)outer * inner, out, [&](float* o) {
+    return launch_add_broadcast(dev, a->dptr, b->dptr, o, outer, inner, dev->stream);
+  });
+}
+
+agpu_status agpu_sum_inner(agpu_device* dev, const agpu_buffer* src, uint32_t outer,
+                           uint32_t inner, agpu_buffer** out) {
+  CHECK_DEV(dev, "sum_inner");
+  CHECK_BUF(src, "sum_inner", "src");
+  CHECK_OUT(out, "sum_inner");
+  CHECK_LEN(src, (uint64_t)outer * inner, "sum_inner", "src");  // src/ops/tensor_ops.rs:323
+  return with_output(dev, outer, out, [&](float* o) {
+    return launch_sum_inner(dev, src->dptr, o, outer, inner, dev->stream);
+  });
+}
+
+agpu_status agpu_sum_rows(agpu_device* dev, const agpu_buffer* src, uint32_t rows, uint32_t cols,
+                          agpu_buffer** out) {
+  CHECK_DEV(dev, "sum_rows");
+  CHECK_BUF(src, "sum_rows", "src");
+  CHECK_OUT(out, "sum_rows");
+  CHECK_LEN(src, (uint64_t)rows * cols, "sum_rows", "src");  // src/ops/tensor_ops.rs:361
+  return with_output(dev, cols, out, [&](float* o) {
+    return launch_sum_rows(dev, src->dptr, o, rows, cols, dev->stream);
+  });
+}
+
+agpu_status agpu_concat(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                        uint32_t outer, uint32_t a_inner, uint32_t b_inner, agpu_buffer** out) {
+  CHECK_DEV(dev, "concat");
+  CHECK_BUF(a, "concat", "A");
+  CHECK_BUF(b, "concat", "B");
+  CHECK_OUT(out, "concat");
+  // src/ops/tensor_ops.rs:234-235
+  CHECK_LEN(a, (uint64_t)outer * a_inner, "concat", "A");
+  CHECK_LEN(b, (uint64_t)outer * b_inner, "concat", "B");
+  const uint64_t total = (uint64_t)outer * ((uint64_t)a_inner + b_inner);
+  return with_output(dev, total, out, [&](float* o) {
+    return launch_concat(dev, a->dptr, b->dptr, o, outer, a_inner, b_inner, dev->stream);
+  });
+}
+
+agpu_status agpu_slice_per_block(agpu_device* dev, const agpu_buffer* src, uint32_t outer,
+                                 uint32_t slice_size, uint32_t slice_offset, uint32_t combined,
+                                 agpu_buffer** out) {
+  CHECK_DEV(dev, "slice_per_block");
+  CHECK_BUF(src, "slice_per_block", "src");
+  CHECK_OUT(out, "slice_per_block");
+  // src/ops/tensor_ops.rs:280-281
+  CHECK_LEN(src, (uint64_t)outer * combined, "slice_per_block", "src");
+  if ((uint64_t)slice_offset + slice_size > combined)
+    return fail(AGPU_ERR_SHAPE, "slice_per_block: offset %u + size %u > combined %u",
+                slice_offset, slice_size, combined);
+  return with_output(dev, (uint64_t)outer * slice_size, out, [&](float* o) {
+    return launch_slice_per_block(dev, src->dptr, o, outer, slice_size, slice_offset, combined,
+                                  dev->stream);
+  });
+}
+
+agpu_status agpu_upsample_nearest2d(agpu_device* dev, const agpu_buffer* input, uint32_t batch,
+                                    uint32_t channels, uint32_t in_h, uint32_t in_w,
+                                    uint32_t scale_h, uint32_t scale_w, agpu_buffer** out) {
+  CHECK_DEV(dev, "upsample_nearest2d");
+  CHECK_BUF(input, "upsample_nearest2d", "input");
+  CHECK_OUT(out, "upsample_nearest2d");
+  const uint64_t planes = (uint64_t)batch * channels;
+  CHECK_LEN(input, planes * in_h * in_w, "upsample_nearest2d", "input");  // upsample.rs:101
+  const uint64_t total = planes * in_h * scale_h * in_w * scale_w;
+  return with_output(dev, total, out, [&](float* o) {
+    return launch_upsample_nearest2d(dev, input->dptr, o, planes, in_h, in_w, scale_h, scale_w,
+                                     dev->stream);
+  });
+}
+
+agpu_status agpu_upsample_nearest2d_backward(agpu_device* dev, const agpu_buffer* grad_out,
+                                             uint32_t batch, uint32_t channels, uint32_t in_h,
+                                             uint32_t in_w, uint32_t scale_h, uint32_t scale_w,
+                                             agpu_buffer** out) {
+  CHECK_DEV(dev, "upsample_nearest2d_backward");
+  CHECK_BUF(grad_out, "upsample_nearest2d_backward", "grad_out");
+  CHECK_OUT(out, "upsample_nearest2d_backward");
+  const uint64_t planes = (uint64_t)batch * channels;
+  // src/ops/upsample.rs:124
+  CHECK_LEN(grad_out, planes * in_h * scale_h * in_w * scale_w, "upsample_nearest2d_backward",
+            "grad_out");
+  return with_output(dev, planes * in_h * in_w, out, [&](float* o) {
+    return launch_upsample_nearest2d_backward(dev, grad_out->dptr, o, planes, in_h, in_w,
+                                              scale_h, scale_w, dev->stream);
+  });
+}
+
+agpu_status agpu_mse_loss(agpu_device* dev, const agpu_buffer* pred, const agpu_buffer* target,
+                          agpu_buffer** out) {
+  CHECK_DEV(dev, "mse_loss");
+  CHECK_BUF(pred, "mse_loss", "pred");
+  CHECK_BUF(target, "mse_loss", "target");
+  CHECK_OUT(out, "mse_loss");
+  CHECK_LEN(target, pred->len, "mse_loss", "target");  // src/ops/attention.rs:173
+  return with_output(dev, 1, out, [&](float* o) {
+    return launch_mse_loss(dev, pred->dptr, target->dptr, o, pred->len, dev->stream);
+  });
+}
+
 // ----------------------------------------------------------- launch layer --
 agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, const float* b, float* c,
                                      uint32_t batch, uint32_t m, uint32_t n, uint32_t k,

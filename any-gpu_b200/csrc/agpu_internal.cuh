@@ -163,5 +163,24 @@ agpu_status launch_transpose(agpu_device* dev, const float* a, float* out, uint6
                              uint64_t d0, uint64_t d1, uint64_t inner, cudaStream_t st);
 agpu_status launch_add_per_col(agpu_device* dev, const float* a, const float* b, float* out,
                                uint64_t rows, uint64_t cols, cudaStream_t st);
+agpu_status launch_add_broadcast(agpu_device* dev, const float* a, const float* b, float* out,
+                                 uint64_t outer, uint64_t inner, cudaStream_t s);
+agpu_status launch_sum_inner(agpu_device* dev, const float* src, float* out, uint64_t outer,
+                             uint64_t inner, cudaStream_t s);
+agpu_status launch_sum_rows(agpu_device* dev, const float* src, float* out, uint64_t rows,
+                            uint64_t cols, cudaStream_t s);
+agpu_status launch_concat(agpu_device* dev, const float* a, const float* b, float* out,
+                          uint64_t outer, uint64_t ai, uint64_t bi, cudaStream_t s);
+agpu_status launch_slice_per_block(agpu_device* dev, const float* src, float* dst, uint64_t outer,
+                                   uint64_t size, uint64_t offset, uint64_t combined,
+                                   cudaStream_t s);
+agpu_status launch_upsample_nearest2d(agpu_device* dev, const float* in, float* out,
+                                      uint64_t planes, uint32_t in_h, uint32_t in_w, uint32_t sh,
+                                      uint32_t sw, cudaStream_t s);
+agpu_status launch_upsample_nearest2d_backward(agpu_device* dev, const float* go, float* gi,
+                                               uint64_t planes, uint32_t in_h, uint32_t in_w,
+                                               uint32_t sh, uint32_t sw, cudaStream_t s);
+agpu_status launch_mse_loss(agpu_device* dev, const float* pred, const float* target, float* out,
+                            uint64_t n, cudaStream_t s);
 
 }  // namespace agpu

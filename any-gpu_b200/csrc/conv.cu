@@ -243,57 +243,75 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restr
   }
 }
 
-// NCHW [N, C, HW] -> NHWC [N, HW, Cs] (channels >= C zero-filled).
-__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int C,
-                                    int HW, int Cs) {
-  __shared__ float tile[32][33];
-  const int n = blockIdx.z;
-  const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  const float* xn = x + (long long)n * C * HW;
-  float* yn = y + (long long)n * HW * Cs;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int c = c0 + i, p = p0 + threadIdx.x;
-    tile[i][threadIdx.x] = (c < C && p < HW) ? xn[(long long)c * HW + p] : 0.0f;
+// Staging for the implicit-GEMM convolutions, in one launch:
+//   blocks [0, wblocks): W [Cout, Cin, taps] -> W2 [Cout, taps, Cw]
+//     (channels >= Cin zero), a grid-stride loop over W2 (coalesced writes);
+//   the rest: NCHW [N, C, HW] -> NHWC [N, HW, Cs] (channels >= C zero), one
+//     32-channel x 128-pixel tile per CTA: 16 loads in flight per thread
+//     (each warp instruction reads 128 contiguous bytes of one channel), a
+//     shared-memory transpose with row pitch 129 (conflict-free both ways),
+//     float4 stores (8 lanes write one pixel's 32 channels, 128 B).
+// The weight blocks come first in the grid, so they overlap the transpose.
+constexpr int kStageP = 128, kStageC = 32;
+
+__global__ void __launch_bounds__(256) conv_stage_kernel(
+    const float* __restrict__ x, float* __restrict__ xs, int C, int HW, int Cs, int ptiles,
+    int ctiles, const float* __restrict__ w, float* __restrict__ w2, int cin, int taps, int Cw,
+    long long w2_elems, int wblocks) {
+  __shared__ float tile[kStageC][kStageP + 1];
+  if ((int)blockIdx.x < wblocks) {
+    for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < w2_elems;
+         i += (long long)wblocks * 256) {
+      const int c = (int)(i % Cw);
+      const long long r = i / Cw;
+      const int t = (int)(r % taps);
+      const long long oc = r / taps;
+      w2[i] = c < cin ? __ldg(w + (oc * cin + c) * taps + t) : 0.0f;
+    }
+    return;
+  }
+  long long b = (long long)blockIdx.x - wblocks;
+  const int pt = (int)(b % ptiles);
+  b /= ptiles;
+  const int ct = (int)(b % ctiles);
+  const long long n = b / ctiles;
+  const int p0 = pt * kStageP, c0 = ct * kStageC;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const float* xn = x + n * C * HW;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int cl = warp + 8 * k, c = c0 + cl;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int p = p0 + lane + 32 * i;
+      tile[cl][lane + 32 * i] = (c < C && p < HW) ? __ldcs(xn + (long long)c * HW + p) : 0.0f;
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int p = p0 + i, c = c0 + threadIdx.x;
-    if (p < HW && c < Cs) yn[(long long)p * Cs + c] = tile[threadIdx.x][i];
+  float* yn = xs + n * HW * Cs;
+  const int c4 = lane % 8;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int pl = warp * 16 + k * 4 + lane / 8;
+    const int p = p0 + pl, c = c0 + 4 * c4;
+    if (p < HW && c < Cs)
+      *reinterpret_cast<float4*>(yn + (long long)p * Cs + c) =
+          make_float4(tile[4 * c4][pl], tile[4 * c4 + 1][pl], tile[4 * c4 + 2][pl],
+                      tile[4 * c4 + 3][pl]);
   }
 }
 
-// W [Cout, Cin, KH, KW] -> W2 [Cout, KH, KW, Cw] (channels >= Cin zero).
-__global__ void weight_khwc_kernel(const float* __restrict__ w, float* __restrict__ w2, int Cout,
-                                   int Cin, int KH, int KW, int Cw) {
-  const long long total = (long long)Cout * KH * KW * Cw;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % Cw);
-    long long r = i / Cw;
-    const int kw = (int)(r % KW);
-    r /= KW;
-    const int kh = (int)(r % KH);
-    const int oc = (int)(r / KH);
-    w2[i] = c < Cin ? w[(((long long)oc * Cin + c) * KH + kh) * KW + kw] : 0.0f;
-  }
-}
-
-// Same relayout, one CTA per output channel: the channel's Cin*KH*KW weights
-// are read contiguously into shared memory and written tap-major, so both the
-// reads and the writes are coalesced.
-__global__ void __launch_bounds__(256) weight_khwc_smem_kernel(const float* __restrict__ w,
-                                                              float* __restrict__ w2, int Cin,
-                                                              int taps, int Cw) {
-  extern __shared__ float row[];  // [Cin][taps]
-  const int oc = blockIdx.x;
-  const float* src = w + (long long)oc * Cin * taps;
-  for (int i = threadIdx.x; i < Cin * taps; i += blockDim.x) row[i] = __ldg(src + i);
-  __syncthreads();
-  float* dst = w2 + (long long)oc * taps * Cw;
-  for (int i = threadIdx.x; i < taps * Cw; i += blockDim.x) {
-    const int t = i / Cw, c = i % Cw;
-    dst[i] = c < Cin ? row[c * taps + t] : 0.0f;
-  }
+// Enqueue conv_stage_kernel: x (NCHW, C channels) -> xs (NHWC, Cs channels);
+// with w != nullptr also W -> W2 as above.
+void launch_conv_stage(const agpu_device* dev, const float* x, float* xs, int n, int C, int HW,
+                       int Cs, const float* w, float* w2, int cout, int cin, int taps, int Cw,
+                       cudaStream_t s) {
+  const int ptiles = (int)ceil_div(HW, kStageP), ctiles = (int)ceil_div(Cs, kStageC);
+  const long long w2_elems = w ? (long long)cout * taps * Cw : 0;
+  const int wblocks = (int)std::min<long long>(ceil_div(w2_elems, 256 * 8), 4LL * dev->sm_count);
+  const long long blocks = wblocks + (long long)n * ctiles * ptiles;
+  conv_stage_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, xs, C, HW, Cs, ptiles, ctiles, w, w2, cin,
+                                                     taps, Cw, w2_elems, wblocks);
 }
 
 // conv_transpose2d weight W [Cin, Cout, KH, KW] -> the equivalent conv2d
@@ -458,17 +476,9 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   AGPU_TRY(pool_alloc(dev, (xs_elems + w2_elems) * sizeof(float) + 256, &scratch, s));
   float* xs = static_cast<float*>(scratch);
   float* w2 = xs + (xs_elems + 63) / 64 * 64;
-  {
-    dim3 grid((unsigned)ceil_div((uint64_t)p.h * p.w, 32), (unsigned)ceil_div(Cs, 32), p.n);
-    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xs, p.cin, p.h * p.w, Cs);
-    const int taps = p.kh * p.kw;
-    if ((long long)p.cin * taps * 4 <= 48 * 1024)
-      weight_khwc_smem_kernel<<<p.cout, 256, p.cin * taps * 4, s>>>(w, w2, p.cin, taps, Cw);
-    else
-      weight_khwc_kernel<<<grid_for(dev, (long long)w2_elems), 256, 0, s>>>(w, w2, p.cout,
-                                                                            p.cin, p.kh, p.kw, Cw);
-  }
-  agpu_status st = after_launch(dev, "conv staging kernels", 2);
+  launch_conv_stage(dev, x, xs, p.n, p.cin, p.h * p.w, Cs, w, w2, p.cout, p.cin, p.kh * p.kw, Cw,
+                    s);
+  agpu_status st = after_launch(dev, "conv_stage_kernel");
   if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
 
   P pol;
@@ -596,11 +606,8 @@ agpu_status run_wgrad_tc(agpu_device* dev, const ConvParams& p, const float* x, 
   AGPU_TRY(pool_alloc(dev, (xs_elems + ws_elems) * sizeof(float) + 256, &scratch, s));
   float* xs = static_cast<float*>(scratch);
   pol.ws = xs + (xs_elems + 63) / 64 * 64;
-  {
-    dim3 grid((unsigned)ceil_div((uint64_t)p.h * p.w, 32), (unsigned)ceil_div(Cs, 32), p.n);
-    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xs, p.cin, p.h * p.w, Cs);
-  }
-  agpu_status st = after_launch(dev, "wgrad staging");
+  launch_conv_stage(dev, x, xs, p.n, p.cin, p.h * p.w, Cs, nullptr, nullptr, 0, 0, 0, 0, s);
+  agpu_status st = after_launch(dev, "conv_stage_kernel");
   CUtensorMap ta, tb;
   if (st == AGPU_OK)
     st = make_tmap_f32_3d(&ta, gy, (uint64_t)p.ho * p.wo, p.cout, p.n,

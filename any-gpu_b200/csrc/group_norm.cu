@@ -15,7 +15,13 @@
 //    holding each group in registers (one 1024-thread CTA per group) and a
 //    persistent cluster kernel streaming slices through shared memory, both
 //    latency-bound, this is the fastest (UNet block: 49.8 vs 58.7 vs 91 us).
-//    Float4 loads when x, y are 16-byte aligned and spatial % 4 == 0, a
+//    Also measured and dropped: one cooperative launch rolling the chunk
+//    list through the resident CTAs (stats of round r, normalise round r-1,
+//    so x crosses HBM once: 59.7 us, the CTAs move in lockstep and HBM
+//    idles during their reductions), and splitting the groups into 24-40 MB
+//    slabs run back to back so the re-read hits L2 (61-85 us).  Kernel 1
+//    loads with an L2 evict-last policy, which keeps more of x in L2 for
+//    kernel 2 (52 -> 50 us).  Float4 loads when x, y are 16-byte aligned and spatial % 4 == 0, a
 //    scalar pair of kernels otherwise.
 //  * `swish` fuses the UNet block's activation, y = z / (1 + exp(-z))
 //    (src/ops/elementwise.rs:77-89), into the store.
@@ -132,6 +138,16 @@ __global__ void __launch_bounds__(kThreads) gn_apply_kernel(
 // (126 MB) is mostly served from there the second time.
 constexpr int kChunkVec = 8;  // float4 per thread: 8192-element chunks
 
+// Load with an L2 evict-last policy: the chunk stays in L2 for the apply
+// kernel's second read (measured: UNet block group norm 52 -> 50 us).
+__device__ __forceinline__ float4 ld_keep(const float4* p, uint64_t pol) {
+  float4 v;
+  asm("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
 __global__ void __launch_bounds__(kThreads) gn_partial_vec_kernel(const float* __restrict__ x,
                                                                   float2* __restrict__ partials,
                                                                   long long gsize, int chunk) {
@@ -141,13 +157,15 @@ __global__ void __launch_bounds__(kThreads) gn_partial_vec_kernel(const float* _
   const int n = (int)(std::min<long long>(c0 + chunk, gsize) - c0);
   const int nvec = n / 4;
   const float4* src = reinterpret_cast<const float4*>(x + grp * gsize + c0);
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   float4 v[kChunkVec];
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < kChunkVec; ++j) {
     const int i = threadIdx.x + j * kThreads;
     if (i < nvec) {
-      v[j] = src[i];  // default caching: the apply kernel re-reads this chunk
+      v[j] = ld_keep(src + i, pol);  // the apply kernel re-reads this chunk
       s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
     }
   }
@@ -449,11 +467,12 @@ agpu_status launch_group_norm(agpu_device* dev, const float* x, const float* gam
   if (groups_total > 65535 || nchunks > 0x7fffffff)
     return fail(AGPU_ERR_UNSUPPORTED, "group_norm: %lld groups x %lld chunks too large",
                 groups_total, nchunks);
+  const bool vec = aligned && spatial % 4 == 0;
   void* buf = nullptr;
   AGPU_TRY(pool_alloc(dev, need, &buf, s));  // stream-ordered, freed after kernel 2
   dim3 grid((unsigned)nchunks, (unsigned)groups_total);
   launch_chunked(x, static_cast<float2*>(buf), gamma, beta, y, gsize, chunk, (int)nchunks,
-                 (int)spatial, (int)cpg, (int)groups, eps, swish, aligned && spatial % 4 == 0,
+                 (int)spatial, (int)cpg, (int)groups, eps, swish, vec,
                  grid, s);
   agpu_status st = after_launch(dev, "gn_partial/apply_kernel", 2);
   pool_free(dev, buf, s);

@@ -276,6 +276,48 @@ AGPU_API agpu_status agpu_transpose(agpu_device* dev, const agpu_buffer* a, uint
 AGPU_API agpu_status agpu_add_per_col(agpu_device* dev, const agpu_buffer* a,
                                       const agpu_buffer* b, uint32_t rows, uint32_t cols,
                                       agpu_buffer** out);
+/* GpuDevice::add_broadcast (src/ops/tensor_ops.rs:298-315): out[o,i] = a[o,i] + b[o]. */
+AGPU_API agpu_status agpu_add_broadcast(agpu_device* dev, const agpu_buffer* a,
+                                        const agpu_buffer* b, uint32_t outer, uint32_t inner,
+                                        agpu_buffer** out);
+/* GpuDevice::sum_inner (src/ops/tensor_ops.rs:318-333, the AddBroadcast backward):
+ * out[o] = sum_i src[o,i]. */
+AGPU_API agpu_status agpu_sum_inner(agpu_device* dev, const agpu_buffer* src, uint32_t outer,
+                                    uint32_t inner, agpu_buffer** out);
+/* GpuDevice::sum_rows (src/ops/tensor_ops.rs:356-372, the AddPerCol backward):
+ * out[c] = sum_r src[r,c]. */
+AGPU_API agpu_status agpu_sum_rows(agpu_device* dev, const agpu_buffer* src, uint32_t rows,
+                                   uint32_t cols, agpu_buffer** out);
+/* GpuDevice::concat (src/ops/tensor_ops.rs:229-245): [outer,a_inner] ++ [outer,b_inner]
+ * -> [outer, a_inner+b_inner]. */
+AGPU_API agpu_status agpu_concat(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
+                                 uint32_t outer, uint32_t a_inner, uint32_t b_inner,
+                                 agpu_buffer** out);
+/* GpuDevice::slice_per_block (src/ops/tensor_ops.rs:274-294, the Concat backward):
+ * [outer, combined] -> [outer, slice_size] from column slice_offset;
+ * slice_offset + slice_size > combined -> AGPU_ERR_SHAPE. */
+AGPU_API agpu_status agpu_slice_per_block(agpu_device* dev, const agpu_buffer* src,
+                                          uint32_t outer, uint32_t slice_size,
+                                          uint32_t slice_offset, uint32_t combined,
+                                          agpu_buffer** out);
+/* GpuDevice::upsample_nearest2d (src/ops/upsample.rs:94-113): NCHW [N,C,H,W] ->
+ * [N,C,H*scale_h,W*scale_w]. */
+AGPU_API agpu_status agpu_upsample_nearest2d(agpu_device* dev, const agpu_buffer* input,
+                                             uint32_t batch, uint32_t channels, uint32_t in_h,
+                                             uint32_t in_w, uint32_t scale_h, uint32_t scale_w,
+                                             agpu_buffer** out);
+/* GpuDevice::upsample_nearest2d_backward (src/ops/upsample.rs:116-137): each input pixel
+ * sums its scale_h x scale_w output block. */
+AGPU_API agpu_status agpu_upsample_nearest2d_backward(agpu_device* dev,
+                                                      const agpu_buffer* grad_out,
+                                                      uint32_t batch, uint32_t channels,
+                                                      uint32_t in_h, uint32_t in_w,
+                                                      uint32_t scale_h, uint32_t scale_w,
+                                                      agpu_buffer** out);
+/* GpuDevice::mse_loss (src/ops/attention.rs:171-182): 1-element mean((pred-target)^2);
+ * pred.len != target.len -> AGPU_ERR_SHAPE. */
+AGPU_API agpu_status agpu_mse_loss(agpu_device* dev, const agpu_buffer* pred,
+                                   const agpu_buffer* target, agpu_buffer** out);
 
 /* ---------------------------------------------------------------- AdamW -- */
 /* One AdamW step (the reference's AdamW::step, src/optim.rs:82-138, and its

@@ -545,6 +545,84 @@ void oracle_add_per_col(const float* a, const float* b, float* out, int64_t rows
   for (int64_t i = 0; i < rows * cols; ++i) out[i] = a[i] + b[i % cols];
 }
 
+/* SHADER_BROADCAST_ADD: src/ops/tensor_ops.rs:87-100. */
+void oracle_add_broadcast(const float* a, const float* b, float* out, int64_t outer,
+                          int64_t inner) {
+  for (int64_t i = 0; i < outer * inner; ++i) out[i] = a[i] + b[i / inner];
+}
+
+/* SHADER_SUM_INNER: src/ops/tensor_ops.rs:113-129 (serial fp32 sum per row). */
+void oracle_sum_inner(const float* src, float* out, int64_t outer, int64_t inner) {
+  for (int64_t o = 0; o < outer; ++o) {
+    float s = 0.0f;
+    for (int64_t i = 0; i < inner; ++i) s += src[o * inner + i];
+    out[o] = s;
+  }
+}
+
+/* SHADER_SUM_ROWS: src/ops/tensor_ops.rs:160-176 (serial fp32 sum per column). */
+void oracle_sum_rows(const float* src, float* out, int64_t rows, int64_t cols) {
+  for (int64_t c = 0; c < cols; ++c) {
+    float s = 0.0f;
+    for (int64_t r = 0; r < rows; ++r) s += src[r * cols + c];
+    out[c] = s;
+  }
+}
+
+/* SHADER_CONCAT: src/ops/tensor_ops.rs:20-41. */
+void oracle_concat(const float* a, const float* b, float* out, int64_t outer, int64_t a_inner,
+                   int64_t b_inner) {
+  const int64_t w = a_inner + b_inner;
+  for (int64_t i = 0; i < outer * w; ++i) {
+    const int64_t o = i / w, j = i % w;
+    out[i] = j < a_inner ? a[o * a_inner + j] : b[o * b_inner + (j - a_inner)];
+  }
+}
+
+/* SHADER_SLICE: src/ops/tensor_ops.rs:59-72. */
+void oracle_slice_per_block(const float* src, float* dst, int64_t outer, int64_t size,
+                            int64_t offset, int64_t combined) {
+  for (int64_t i = 0; i < outer * size; ++i)
+    dst[i] = src[(i / size) * combined + offset + i % size];
+}
+
+/* SHADER_UPSAMPLE_NEAREST: src/ops/upsample.rs:21-45 (ih = oh * in_h / out_h). */
+void oracle_upsample_nearest2d(const float* in, float* out, int64_t batch, int64_t channels,
+                               int64_t in_h, int64_t in_w, int64_t sh, int64_t sw) {
+  const int64_t out_h = in_h * sh, out_w = in_w * sw;
+  const int64_t total = batch * channels * out_h * out_w;
+  for (int64_t i = 0; i < total; ++i) {
+    const int64_t ow = i % out_w, oh = (i / out_w) % out_h, pl = i / (out_w * out_h);
+    out[i] = in[(pl * in_h + oh * in_h / out_h) * in_w + ow * in_w / out_w];
+  }
+}
+
+/* SHADER_UPSAMPLE_NEAREST_BACKWARD: src/ops/upsample.rs:49-78 (dy outer, dx inner). */
+void oracle_upsample_nearest2d_backward(const float* go, float* gi, int64_t batch,
+                                        int64_t channels, int64_t in_h, int64_t in_w, int64_t sh,
+                                        int64_t sw) {
+  const int64_t out_h = in_h * sh, out_w = in_w * sw;
+  const int64_t total = batch * channels * in_h * in_w;
+  for (int64_t i = 0; i < total; ++i) {
+    const int64_t iw = i % in_w, ih = (i / in_w) % in_h, pl = i / (in_w * in_h);
+    float s = 0.0f;
+    for (int64_t dy = 0; dy < sh; ++dy)
+      for (int64_t dx = 0; dx < sw; ++dx)
+        s += go[pl * out_h * out_w + (ih * sh + dy) * out_w + iw * sw + dx];
+    gi[i] = s;
+  }
+}
+
+/* SHADER_MSE_SUM: src/ops/attention.rs:72-87 (serial fp32 sum, then / f32(n)). */
+float oracle_mse_loss(const float* pred, const float* target, int64_t n) {
+  float s = 0.0f;
+  for (int64_t i = 0; i < n; ++i) {
+    const float d = pred[i] - target[i];
+    s += d * d;
+  }
+  return s / (float)n;
+}
+
 /* RMSNorm (not in the reference; standard formula, parity unpinned):
  * y = x / sqrt(mean(x^2) + eps) * w, per row of `cols`. */
 void oracle_rmsnorm(const float* x, const float* w, float* out, int64_t rows, int64_t cols,

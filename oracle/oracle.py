@@ -44,6 +44,14 @@ _SIG = {
     "oracle_elementwise": (None, [C.c_int, _p, _p, _f32, _p, _i64]),
     "oracle_transpose": (None, [_p, _p, _i64, _i64, _i64, _i64]),
     "oracle_add_per_col": (None, [_p, _p, _p, _i64, _i64]),
+    "oracle_add_broadcast": (None, [_p, _p, _p, _i64, _i64]),
+    "oracle_sum_inner": (None, [_p, _p, _i64, _i64]),
+    "oracle_sum_rows": (None, [_p, _p, _i64, _i64]),
+    "oracle_concat": (None, [_p, _p, _p, _i64, _i64, _i64]),
+    "oracle_slice_per_block": (None, [_p, _p, _i64, _i64, _i64, _i64]),
+    "oracle_upsample_nearest2d": (None, [_p, _p] + [_i64] * 6),
+    "oracle_upsample_nearest2d_backward": (None, [_p, _p] + [_i64] * 6),
+    "oracle_mse_loss": (_f32, [_p, _p, _i64]),
     "oracle_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f32]),
     "oracle_rope": (None, [_p, _p, _i64, _i64, _i64, _i64, _f32]),
     "oracle_adamw": (None, [_p, _p, _p, _p, _i64, _f32, _f32, _f32, _f32, _f32, _i64]),
@@ -211,6 +219,61 @@ def transpose(a, outer, d0, d1, inner) -> np.ndarray:
     out = np.empty(a.size, np.float32)
     lib().oracle_transpose(_ptr(a), _ptr(out), outer, d0, d1, inner)
     return out
+
+
+def add_broadcast(a, b, outer, inner) -> np.ndarray:
+    a, b = _a(a), _a(b)
+    out = np.empty(a.size, np.float32)
+    lib().oracle_add_broadcast(_ptr(a), _ptr(b), _ptr(out), outer, inner)
+    return out
+
+
+def sum_inner(src, outer, inner) -> np.ndarray:
+    src = _a(src)
+    out = np.empty(outer, np.float32)
+    lib().oracle_sum_inner(_ptr(src), _ptr(out), outer, inner)
+    return out
+
+
+def sum_rows(src, rows, cols) -> np.ndarray:
+    src = _a(src)
+    out = np.empty(cols, np.float32)
+    lib().oracle_sum_rows(_ptr(src), _ptr(out), rows, cols)
+    return out
+
+
+def concat(a, b, outer, a_inner, b_inner) -> np.ndarray:
+    a, b = _a(a), _a(b)
+    out = np.empty(outer * (a_inner + b_inner), np.float32)
+    lib().oracle_concat(_ptr(a), _ptr(b), _ptr(out), outer, a_inner, b_inner)
+    return out
+
+
+def slice_per_block(src, outer, size, offset, combined) -> np.ndarray:
+    src = _a(src)
+    out = np.empty(outer * size, np.float32)
+    lib().oracle_slice_per_block(_ptr(src), _ptr(out), outer, size, offset, combined)
+    return out
+
+
+def upsample_nearest2d(x, batch, channels, in_h, in_w, sh, sw) -> np.ndarray:
+    x = _a(x)
+    out = np.empty(batch * channels * in_h * sh * in_w * sw, np.float32)
+    lib().oracle_upsample_nearest2d(_ptr(x), _ptr(out), batch, channels, in_h, in_w, sh, sw)
+    return out
+
+
+def upsample_nearest2d_backward(go, batch, channels, in_h, in_w, sh, sw) -> np.ndarray:
+    go = _a(go)
+    out = np.empty(batch * channels * in_h * in_w, np.float32)
+    lib().oracle_upsample_nearest2d_backward(_ptr(go), _ptr(out), batch, channels, in_h, in_w,
+                                             sh, sw)
+    return out
+
+
+def mse_loss(pred, target) -> np.ndarray:
+    p, t = _a(pred), _a(target)
+    return np.array([lib().oracle_mse_loss(_ptr(p), _ptr(t), p.size)], np.float32)
 
 
 def add_per_col(a, b, rows, cols) -> np.ndarray:

@@ -238,6 +238,30 @@ def cases():
     add("transpose_1x_n", "src/ops/tensor_ops.rs:435-441", "transpose",
         {"a": [1, 2, 3, 4, 5]}, dict(outer=1, d0=1, d1=5, inner=1), expect=[1, 2, 3, 4, 5],
         exact=True)
+    add("concat_flat", "src/ops/tensor_ops.rs:379-382", "concat",
+        {"a": [1, 2, 3], "b": [4, 5, 6]}, dict(outer=1, a_inner=3, b_inner=3),
+        expect=[1, 2, 3, 4, 5, 6], exact=True)
+    add("concat_asymmetric", "src/ops/tensor_ops.rs:385-391", "concat",
+        {"a": [1, 2], "b": [3, 4, 5]}, dict(outer=1, a_inner=2, b_inner=3),
+        expect=[1, 2, 3, 4, 5], exact=True)
+    add("concat_batched_channel_axis", "src/ops/tensor_ops.rs:394-404", "concat",
+        {"a": [10, 20, 30, 40], "b": [1, 2, 3, 4, 5, 6, 7, 8]},
+        dict(outer=2, a_inner=2, b_inner=4),
+        expect=[10, 20, 1, 2, 3, 4, 30, 40, 5, 6, 7, 8], exact=True)
+
+    # ------------------------------------------------ src/ops/upsample.rs --
+    add("upsample_2x", "src/ops/upsample.rs:161-170", "upsample_nearest2d",
+        {"x": [1, 2, 3, 4]}, dict(batch=1, channels=1, in_h=2, in_w=2, scale_h=2, scale_w=2),
+        expect=[1, 1, 2, 2, 1, 1, 2, 2, 3, 3, 4, 4, 3, 3, 4, 4], exact=True)
+    add("upsample_3x_vs_cpu", "src/ops/upsample.rs:173-179", "upsample_nearest2d",
+        {"x": rng(1, 7, lambda x: x)},
+        dict(batch=1, channels=1, in_h=2, in_w=3, scale_h=3, scale_w=3), exact=True)
+    add("upsample_batched_multichannel_vs_cpu", "src/ops/upsample.rs:182-188",
+        "upsample_nearest2d", {"x": rng(0, 24, lambda i: i)},
+        dict(batch=2, channels=3, in_h=2, in_w=2, scale_h=2, scale_w=2), exact=True)
+    add("upsample_1x1", "src/ops/upsample.rs:191-195", "upsample_nearest2d", {"x": [7]},
+        dict(batch=1, channels=1, in_h=1, in_w=1, scale_h=3, scale_w=3), expect=[7] * 9,
+        exact=True)
     return c
 
 

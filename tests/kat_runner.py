@@ -7,7 +7,7 @@ import numpy as np
 GPU_OPS = {"matmul", "batch_matmul", "softmax", "add", "sub", "mul", "relu", "sigmoid", "swish",
            "tanh", "scale", "relu_backward", "sigmoid_backward", "swish_backward",
            "tanh_backward", "transpose", "group_norm", "conv2d", "conv_transpose2d",
-           "conv2d_grad_bias", "sdpa"}
+           "conv2d_grad_bias", "sdpa", "concat", "upsample_nearest2d"}
 
 
 def run_oracle(orc, case) -> np.ndarray:
@@ -36,6 +36,11 @@ def run_oracle(orc, case) -> np.ndarray:
                               a["spatial"], a["groups"], a["eps"])
     if op == "transpose":
         return orc.transpose(x["a"], a["outer"], a["d0"], a["d1"], a["inner"])
+    if op == "concat":
+        return orc.concat(x["a"], x["b"], a["outer"], a["a_inner"], a["b_inner"])
+    if op == "upsample_nearest2d":
+        return orc.upsample_nearest2d(x["x"], a["batch"], a["channels"], a["in_h"], a["in_w"],
+                                      a["scale_h"], a["scale_w"])
     if op == "scale":
         return orc.elementwise("scale", x["a"], None, a["s"])
     if op in ("add", "sub", "mul", "relu_backward", "sigmoid_backward", "swish_backward",
@@ -80,6 +85,12 @@ def run_gpu(dev, case) -> np.ndarray:
                                        a["channels"], a["spatial"], a["groups"], a["eps"]))
     if op == "transpose":
         return dev.read(dev.transpose(up(x["a"]), a["outer"], a["d0"], a["d1"], a["inner"]))
+    if op == "concat":
+        return dev.read(dev.concat(up(x["a"]), up(x["b"]), a["outer"], a["a_inner"],
+                                   a["b_inner"]))
+    if op == "upsample_nearest2d":
+        return dev.read(dev.upsample_nearest2d(up(x["x"]), a["batch"], a["channels"], a["in_h"],
+                                               a["in_w"], a["scale_h"], a["scale_w"]))
     if op == "scale":
         return dev.read(dev.scale(up(x["a"]), a["s"]))
     if op in ("add", "sub", "mul", "relu_backward", "sigmoid_backward", "swish_backward",
@@ -108,7 +119,10 @@ def check(case, got, want_oracle=None):
             assert_approx(got, want, case["tol"])
     else:
         assert want_oracle is not None
-        assert_approx(got, want_oracle, case["tol"])
+        if case["exact"]:
+            assert np.array_equal(got, np.asarray(want_oracle, np.float32)), case["name"]
+        else:
+            assert_approx(got, want_oracle, case["tol"])
     if case.get("row_sums"):
         cols = case["args"]["cols"]
         sums = got.reshape(-1, cols).astype(np.float64).sum(axis=1)

@@ -1,0 +1,267 @@
+"""The reference's autograd tests (src/autograd.rs:488-810) through `any_gpu.autograd.Tape`.
+
+Each test body restates one `#[test]` of the reference with its literal
+expected values and tolerances.  They run twice: on the B200 through the
+C ABI (`-m gpu`), and on the CPU with the oracle standing in for the device,
+which checks the tape's host-side logic (recording, reverse walk, gradient
+accumulation, the backward rules) without a GPU."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import assert_approx
+
+
+def _cpu_tape(orc):
+    from any_gpu.autograd import Tape
+    from oracle_device import OracleDevice
+    dev = OracleDevice(orc)
+    return lambda: Tape(dev)
+
+
+@pytest.fixture(params=["oracle", pytest.param("gpu", marks=pytest.mark.gpu)])
+def new_tape(request, orc):
+    if request.param == "oracle":
+        return _cpu_tape(orc)
+    from any_gpu.autograd import Tape
+    dev = request.getfixturevalue("dev")
+    return lambda: Tape(dev)
+
+
+def _mse0(tape, t, n):
+    return tape.mse_loss(t, tape.leaf(np.zeros(n, np.float32)))
+
+
+def test_backward_add(new_tape):  # src/autograd.rs:489-513
+    tape = new_tape()
+    a, b = tape.leaf([1.0, 2.0, 3.0]), tape.leaf([4.0, 5.0, 6.0])
+    loss = _mse0(tape, tape.add(a, b), 3)
+    tape.backward(loss)
+    assert_approx(tape.read(loss), [155.0 / 3.0], 1e-3)
+    assert_approx(tape.read_grad(a), [10 / 3, 14 / 3, 18 / 3], 1e-3)
+    assert_approx(tape.read_grad(b), [10 / 3, 14 / 3, 18 / 3], 1e-3)
+
+
+def test_backward_mul(new_tape):  # :516-537
+    tape = new_tape()
+    a, b = tape.leaf([2.0, 3.0]), tape.leaf([4.0, 5.0])
+    loss = _mse0(tape, tape.mul(a, b), 2)
+    tape.backward(loss)
+    assert_approx(tape.read(loss), [144.5], 1e-3)
+    assert_approx(tape.read_grad(a), [32.0, 75.0], 1e-3)
+    assert_approx(tape.read_grad(b), [16.0, 45.0], 1e-3)
+
+
+def test_backward_matmul(new_tape):  # :540-561
+    tape = new_tape()
+    a, b = tape.leaf([1.0, 2.0]), tape.leaf([3.0, 4.0])
+    loss = _mse0(tape, tape.matmul(a, b, 1, 1, 2), 1)
+    tape.backward(loss)
+    assert_approx(tape.read(loss), [121.0], 1e-3)
+    assert_approx(tape.read_grad(a), [66.0, 88.0], 1e-3)
+    assert_approx(tape.read_grad(b), [22.0, 44.0], 1e-3)
+
+
+def test_backward_relu(new_tape):  # :564-581
+    tape = new_tape()
+    a = tape.leaf([-1.0, 2.0, -3.0, 4.0])
+    loss = _mse0(tape, tape.relu(a), 4)
+    tape.backward(loss)
+    assert_approx(tape.read(loss), [5.0], 1e-3)
+    assert_approx(tape.read_grad(a), [0.0, 1.0, 0.0, 2.0], 1e-3)
+
+
+def test_backward_scale(new_tape):  # :584-593
+    tape = new_tape()
+    a = tape.leaf([1.0, 2.0, 3.0])
+    tape.backward(_mse0(tape, tape.scale(a, 3.0), 3))
+    assert_approx(tape.read_grad(a), [6.0, 12.0, 18.0], 1e-3)
+
+
+def test_backward_sub(new_tape):  # :596-610
+    tape = new_tape()
+    a, b = tape.leaf([5.0, 10.0]), tape.leaf([1.0, 2.0])
+    tape.backward(_mse0(tape, tape.sub(a, b), 2))
+    assert_approx(tape.read_grad(a), [4.0, 8.0], 1e-3)
+    assert_approx(tape.read_grad(b), [-4.0, -8.0], 1e-3)
+
+
+def test_backward_sigmoid(new_tape):  # :613-629
+    tape = new_tape()
+    a = tape.leaf([0.0, 1.0, -1.0])
+    tape.backward(_mse0(tape, tape.sigmoid(a), 3))
+    s = [0.5, 0.7311, 0.2689]
+    assert_approx(tape.read_grad(a), [2 * v / 3 * v * (1 - v) for v in s], 1e-3)
+
+
+def test_backward_tanh(new_tape):  # :632-647
+    tape = new_tape()
+    a = tape.leaf([0.0, 1.0, -1.0])
+    tape.backward(_mse0(tape, tape.tanh_act(a), 3))
+    t = [0.0, 0.7616, -0.7616]
+    assert_approx(tape.read_grad(a), [2 * v / 3 * (1 - v * v) for v in t], 1e-2)
+
+
+def test_backward_swish(new_tape):  # :650-668
+    tape = new_tape()
+    x = [0.0, 1.0, -1.0]
+    a = tape.leaf(x)
+    tape.backward(_mse0(tape, tape.swish(a), 3))
+    want = []
+    for v in x:
+        s = 1 / (1 + math.exp(-v))
+        want.append(2 * (v * s) / 3 * (s + v * s * (1 - s)))
+    assert_approx(tape.read_grad(a), want, 1e-2)
+
+
+def test_read_grad_before_backward(new_tape):  # :671-675
+    tape = new_tape()
+    assert tape.read_grad(tape.leaf([1.0, 2.0])) is None
+
+
+def test_backward_non_scalar_loss(new_tape):  # :678-683
+    from any_gpu import AnyGpuError
+    tape = new_tape()
+    with pytest.raises(AnyGpuError):
+        tape.backward(tape.leaf([1.0, 2.0]))
+
+
+def test_backward_diamond_graph(new_tape):  # :686-705
+    tape = new_tape()
+    a = tape.leaf([1.0])
+    d = tape.add(tape.scale(a, 2.0), tape.scale(a, 3.0))
+    tape.backward(_mse0(tape, d, 1))
+    assert_approx(tape.read_grad(a), [50.0], 1e-3)
+
+
+def test_tape_leaf_data_roundtrip(new_tape):  # :708-713
+    tape = new_tape()
+    data = [1.5, -2.7, 0.0, 99.9]
+    np.testing.assert_array_equal(tape.read(tape.leaf(data)), np.float32(data))
+
+
+def test_tape_conv2d_forward(new_tape):  # :716-726
+    tape = new_tape()
+    x = [float(v) for v in range(1, 10)]
+    out = tape.conv2d(tape.leaf(x), tape.leaf([1.0]), tape.leaf([0.0]), 1, 1, 3, 3, 1, 1, 1)
+    assert_approx(tape.read(out), x, 1e-5)
+
+
+def _conv_loss(new_tape, x, w):
+    tape = new_tape()
+    out = tape.conv2d(tape.leaf(x), tape.leaf(w), None, 1, 1, 3, 3, 1, 1, 1)
+    return float(tape.read(_mse0(tape, out, 9))[0])
+
+
+def test_tape_conv2d_backward_weight_grad(new_tape):  # :729-756
+    eps = 1e-3
+    x = [v * 0.1 for v in range(1, 10)]
+    tape = new_tape()
+    w = tape.leaf([0.5])
+    out = tape.conv2d(tape.leaf(x), w, None, 1, 1, 3, 3, 1, 1, 1)
+    tape.backward(_mse0(tape, out, 9))
+    gw = tape.read_grad(w)
+    numeric = (_conv_loss(new_tape, x, [0.5 + eps]) - _conv_loss(new_tape, x, [0.5 - eps])) / (
+        2 * eps)
+    assert abs(gw[0] - numeric) < 1e-2, (gw[0], numeric)
+
+
+def test_tape_conv2d_backward_input_grad(new_tape):  # :759-790
+    eps = 1e-3
+    x = [v * 0.1 for v in range(1, 10)]
+    tape = new_tape()
+    inp = tape.leaf(x)
+    out = tape.conv2d(inp, tape.leaf([0.5]), None, 1, 1, 3, 3, 1, 1, 1)
+    tape.backward(_mse0(tape, out, 9))
+    gi = tape.read_grad(inp)
+    for i in range(9):
+        hi, lo = list(x), list(x)
+        hi[i] += eps
+        lo[i] -= eps
+        numeric = (_conv_loss(new_tape, hi, [0.5]) - _conv_loss(new_tape, lo, [0.5])) / (2 * eps)
+        assert abs(gi[i] - numeric) < 1e-2, (i, gi[i], numeric)
+
+
+def test_tape_conv2d_backward_bias_grad(new_tape):  # :793-810
+    tape = new_tape()
+    b = tape.leaf([0.0])
+    out = tape.conv2d(tape.leaf([1.0, 2.0, 3.0, 4.0]), tape.leaf([1.0]), b, 1, 1, 2, 2, 1, 1, 1)
+    tape.backward(_mse0(tape, out, 4))
+    assert_approx(tape.read_grad(b), [5.0], 1e-3)
+
+
+# ---------------------------------------------------------------------------
+# Beyond the reference's tests: a UNet-style graph over every recorded op,
+# gradients against torch autograd in float64.
+
+def _unet_graph(tape, p):
+    """conv -> +bias(broadcast) -> group_norm -> swish -> upsample -> concat(skip)
+    -> conv(stride 2) -> relu -> matmul -> +bias(per col) -> sigmoid * tanh -> mse."""
+    x = tape.leaf(p["x"])
+    h = tape.conv2d(x, tape.leaf(p["w1"]), None, 2, 3, 8, 8, 4, 3, 3, (1, 1), (1, 1))
+    h = tape.add_broadcast(h, tape.leaf(p["cb"]), 2 * 4, 64)
+    h = tape.group_norm(h, tape.leaf(p["g"]), tape.leaf(p["be"]), 2, 4, 64, 2, 1e-5)
+    h = tape.swish(h)
+    u = tape.upsample_nearest2d(h, 2, 4, 8, 8, 2, 2)                      # [2,4,16,16]
+    s = tape.upsample_nearest2d(x, 2, 3, 8, 8, 2, 2)                      # [2,3,16,16]
+    c = tape.concat(u, s, 2, 4 * 256, 3 * 256)                            # [2,7,16,16]
+    h = tape.conv2d(c, tape.leaf(p["w2"]), tape.leaf(p["b2"]), 2, 7, 16, 16, 5, 3, 3,
+                    (2, 2), (1, 1))                                       # [2,5,8,8]
+    h = tape.relu(h)
+    h = tape.matmul(h, tape.leaf(p["wl"]), 2 * 5 * 8, 6, 8)               # rows (n,c,y), x
+    h = tape.add_per_col(h, tape.leaf(p["bl"]), 80, 6)
+    h = tape.mul(tape.sigmoid(h), tape.tanh_act(h))
+    h = tape.sub(h, tape.scale(h, 0.25))
+    return tape.mse_loss(h, tape.leaf(p["t"]))
+
+
+def _params(seed=5):
+    r = np.random.default_rng(seed)
+    f = lambda *s: r.standard_normal(s).astype(np.float32).ravel()
+    return {"x": f(2, 3, 8, 8), "w1": 0.3 * f(4, 3, 3, 3), "cb": 0.1 * f(8),
+            "g": 1 + 0.1 * f(4), "be": 0.1 * f(4), "w2": 0.2 * f(5, 7, 3, 3), "b2": 0.1 * f(5),
+            "wl": 0.3 * f(8, 6), "bl": 0.1 * f(6), "t": f(80 * 6)}
+
+
+def _torch_grads(p):
+    import torch
+    import torch.nn.functional as F
+    t = {k: torch.tensor(v, dtype=torch.float64, requires_grad=True) for k, v in p.items()}
+    x = t["x"].view(2, 3, 8, 8)
+    h = F.conv2d(x, t["w1"].view(4, 3, 3, 3), padding=1)
+    h = h + t["cb"].view(2, 4, 1, 1)
+    h = F.group_norm(h, 2, t["g"], t["be"], eps=1e-5)
+    h = h * torch.sigmoid(h)
+    u = F.interpolate(h, scale_factor=2, mode="nearest")
+    s = F.interpolate(x, scale_factor=2, mode="nearest")
+    c = torch.cat([u, s], 1)
+    h = F.relu(F.conv2d(c, t["w2"].view(5, 7, 3, 3), t["b2"], stride=2, padding=1))
+    h = h.reshape(80, 8) @ t["wl"].view(8, 6) + t["bl"]
+    h = torch.sigmoid(h) * torch.tanh(h)
+    h = h - 0.25 * h
+    loss = ((h.reshape(-1) - t["t"]) ** 2).mean()
+    loss.backward()
+    return {k: v.grad.numpy() for k, v in t.items()}
+
+
+def test_unet_graph_gradients(new_tape):
+    p = _params()
+    tape = new_tape()
+    loss = _unet_graph(tape, p)
+    tape.backward(loss)
+    want = _torch_grads(p)
+    # leaf ids in creation order (the graph creates them in this order)
+    order = ["x", "w1", "cb", "g", "be", "w2", "b2", "wl", "bl", "t"]
+    ids = [e.output for e in tape._entries if e.op == "leaf"]
+    assert len(ids) == len(order)
+    for name, tid in zip(order, ids):
+        if name == "t":
+            assert tape.read_grad(tid) is None  # the target gets no gradient
+            continue
+        got = tape.read_grad(tid)
+        w = want[name]
+        err = np.linalg.norm(got.astype(np.float64) - w) / max(np.linalg.norm(w), 1e-30)
+        assert err < 5e-3, (name, err)

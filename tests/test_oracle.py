@@ -202,3 +202,29 @@ def test_oracle_adamw_reference_tests(orc):
     assert abs(p[0] - 9.99) <= 1e-3                                  # test_adamw_weight_decay
     p, _, _ = orc.adamw(one(5), one(-1), z(1), z(1), 0.01, weight_decay=0.0)
     assert p[0] > 5.0                                                # test_adamw_negative_gradient
+
+
+def test_oracle_tape_ops_vs_numpy(orc):
+    """The restated tape shaders (src/ops/tensor_ops.rs, upsample.rs,
+    attention.rs:72-87) against numpy on random shapes."""
+    r = np.random.default_rng(11)
+    a = r.standard_normal((5, 7)).astype(np.float32)
+    b = r.standard_normal((5, 3)).astype(np.float32)
+    np.testing.assert_array_equal(orc.concat(a, b, 5, 7, 3), np.concatenate([a, b], 1).ravel())
+    ab = np.concatenate([a, b], 1)
+    np.testing.assert_array_equal(orc.slice_per_block(ab, 5, 3, 7, 10), b.ravel())
+    v = r.standard_normal(5).astype(np.float32)
+    np.testing.assert_array_equal(orc.add_broadcast(a, v, 5, 7), (a + v[:, None]).ravel())
+    np.testing.assert_allclose(orc.sum_inner(a, 5, 7), a.astype(np.float64).sum(1), rtol=1e-5)
+    np.testing.assert_allclose(orc.sum_rows(a, 5, 7), a.astype(np.float64).sum(0), rtol=1e-5,
+                               atol=1e-6)
+    x = r.standard_normal((2, 3, 4, 5)).astype(np.float32)
+    up = x.repeat(2, axis=2).repeat(3, axis=3)
+    np.testing.assert_array_equal(orc.upsample_nearest2d(x, 2, 3, 4, 5, 2, 3), up.ravel())
+    go = r.standard_normal(up.shape).astype(np.float32)
+    want = go.reshape(2, 3, 4, 2, 5, 3).astype(np.float64).sum((3, 5))
+    np.testing.assert_allclose(orc.upsample_nearest2d_backward(go, 2, 3, 4, 5, 2, 3),
+                               want.ravel(), rtol=1e-5, atol=1e-6)
+    t = r.standard_normal(a.size).astype(np.float32)
+    d = a.ravel().astype(np.float64) - t
+    np.testing.assert_allclose(orc.mse_loss(a, t)[0], (d * d).mean(), rtol=1e-5)

@@ -202,6 +202,8 @@ def _gn64(x, gamma, beta, n, c, s, g, eps):
                                      (2, 64, 1024, 32),      # 2 channels x 1024 per group
                                      (3, 12, 37, 4),         # spatial % 4 != 0: chunked path
                                      (1, 4, 300000, 2),      # 600k-element groups: chunked
+                                     (1, 2, 2621440, 1),     # 640 chunks in one group: more
+                                                             # than the resident CTAs roll
                                      (2, 6, 8, 6)])          # per-channel groups
 def test_group_norm_parity(dev, orc, n, c, s, g, swish):
     """Config 4's group_norm (eps 1e-5, gamma 1, beta 0 there) and ragged shapes
@@ -278,6 +280,20 @@ def test_batch_matmul_softmax(dev, orc, batch, m, n, k):
     sep = dev.read(dev.softmax(dev.batch_matmul(dev.upload(a), dev.upload(b), batch, m, n, k),
                                batch * m, n))
     np.testing.assert_array_equal(got, sep)
+
+
+@pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32), (3, 12, 37, 4)])
+def test_group_norm_in_place(dev, orc, n, c, s, g):
+    """y may alias x: every chunk is read (twice) before it is overwritten."""
+    r = np.random.default_rng(n + c + s)
+    x = r.standard_normal(n * c * s).astype(np.float32)
+    gamma = (1 + 0.1 * r.standard_normal(c)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(c)).astype(np.float32)
+    X, G, B = dev.upload(x), dev.upload(gamma), dev.upload(beta)
+    want = dev.read(dev.group_norm_swish(X, G, B, n, c, s, g, 1e-5))
+    dev.launch_group_norm(X.device_ptr, G.device_ptr, B.device_ptr, X.device_ptr, n, c, s, g,
+                          1e-5, swish=True)
+    np.testing.assert_array_equal(dev.read(X), want)
 
 
 def test_group_norm_errors(dev):
@@ -553,3 +569,97 @@ def test_sdpa_errors(dev):
     with pytest.raises(AnyGpuError) as e:
         dev.scaled_dot_product_attention(a, a, b, 1, 3, 4)
     assert e.value.status == 1
+
+
+# ----------------------------------------------------------------- tape ops --
+@pytest.mark.parametrize("outer,ai,bi", [(2, 2, 4), (16, 320 * 64, 320 * 64), (7, 5, 3),
+                                         (3, 1, 1), (1000, 12, 8)])
+def test_concat_slice_parity(dev, orc, outer, ai, bi):
+    """concat (src/ops/tensor_ops.rs:229) and its backward slice_per_block
+    (:274): copies, bit-exact, float4 and scalar paths."""
+    r = np.random.default_rng(outer + ai)
+    a = r.standard_normal(outer * ai).astype(np.float32)
+    b = r.standard_normal(outer * bi).astype(np.float32)
+    got = dev.concat(dev.upload(a), dev.upload(b), outer, ai, bi)
+    np.testing.assert_array_equal(dev.read(got), orc.concat(a, b, outer, ai, bi))
+    np.testing.assert_array_equal(dev.read(dev.slice_per_block(got, outer, ai, 0, ai + bi)), a)
+    np.testing.assert_array_equal(dev.read(dev.slice_per_block(got, outer, bi, ai, ai + bi)), b)
+
+
+@pytest.mark.parametrize("n,c,h,w,sh,sw", [(1, 1, 2, 2, 2, 2), (2, 3, 5, 7, 3, 2),
+                                           (16, 320, 32, 32, 2, 2), (1, 1, 1, 1, 3, 3)])
+def test_upsample_parity(dev, orc, n, c, h, w, sh, sw):
+    """upsample_nearest2d and its backward (src/ops/upsample.rs:94-137):
+    the forward is a gather, the backward sums each window in the shader's
+    order, so both are bit-exact."""
+    r = np.random.default_rng(n * c + h)
+    x = r.standard_normal(n * c * h * w).astype(np.float32)
+    got = dev.read(dev.upsample_nearest2d(dev.upload(x), n, c, h, w, sh, sw))
+    np.testing.assert_array_equal(got, orc.upsample_nearest2d(x, n, c, h, w, sh, sw))
+    go = r.standard_normal(got.size).astype(np.float32)
+    gi = dev.read(dev.upsample_nearest2d_backward(dev.upload(go), n, c, h, w, sh, sw))
+    np.testing.assert_array_equal(gi, orc.upsample_nearest2d_backward(go, n, c, h, w, sh, sw))
+
+
+@pytest.mark.parametrize("outer,inner", [(1, 1), (3, 5), (320, 65536), (65536, 64),
+                                         (2, 1000003), (7, 2049)])
+def test_broadcast_add_and_sum_inner_parity(dev, orc, outer, inner):
+    """add_broadcast (bit-exact) and sum_inner, its bias gradient, against the
+    oracle's serial sums: within 1e-5 of float64 or as close as the oracle."""
+    r = np.random.default_rng(outer + inner)
+    a = r.standard_normal(outer * inner).astype(np.float32)
+    b = r.standard_normal(outer).astype(np.float32)
+    A = dev.upload(a)
+    np.testing.assert_array_equal(dev.read(dev.add_broadcast(A, dev.upload(b), outer, inner)),
+                                  orc.add_broadcast(a, b, outer, inner))
+    got = dev.read(dev.sum_inner(A, outer, inner))
+    want = orc.sum_inner(a, outer, inner)
+    ref = a.reshape(outer, inner).astype(np.float64).sum(1)
+    assert orc.rel_fro(got, ref) <= max(1e-5, orc.rel_fro(want, ref))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (5, 3), (65536, 64), (300, 11008), (100003, 5),
+                                       (2, 70000)])
+def test_sum_rows_parity(dev, orc, rows, cols):
+    """sum_rows (src/ops/tensor_ops.rs:356), the add_per_col bias gradient."""
+    r = np.random.default_rng(rows + cols)
+    a = r.standard_normal(rows * cols).astype(np.float32)
+    got = dev.read(dev.sum_rows(dev.upload(a), rows, cols))
+    want = orc.sum_rows(a, rows, cols)
+    ref = a.reshape(rows, cols).astype(np.float64).sum(0)
+    assert orc.rel_fro(got, ref) <= max(1e-5, orc.rel_fro(want, ref))
+
+
+@pytest.mark.parametrize("n", [1, 3, 4097, 1 << 22, 10000019])
+def test_mse_loss_parity(dev, orc, n):
+    """mse_loss (src/ops/attention.rs:172): a deterministic tree sum against
+    the shader's serial fp32 sum."""
+    r = np.random.default_rng(n)
+    p = r.standard_normal(n).astype(np.float32)
+    t = r.standard_normal(n).astype(np.float32)
+    P, T = dev.upload(p), dev.upload(t)
+    got = dev.read(dev.mse_loss(P, T))
+    d = p.astype(np.float64) - t
+    ref = (d * d).mean()
+    want = orc.mse_loss(p, t)[0]
+    assert abs(got[0] - ref) / ref <= max(1e-6, abs(want - ref) / ref)
+    assert got[0] == dev.read(dev.mse_loss(P, T))[0]  # deterministic
+
+
+def test_tape_ops_errors(dev):
+    from any_gpu import AnyGpuError
+    up = lambda k: dev.upload(np.ones(k, np.float32))
+    calls = [lambda: dev.concat(up(5), up(4), 1, 4, 4),            # a size
+             lambda: dev.concat(up(4), up(5), 1, 4, 4),            # b size
+             lambda: dev.slice_per_block(up(8), 2, 3, 2, 4),       # offset + size > combined
+             lambda: dev.slice_per_block(up(9), 2, 2, 0, 4),       # src size
+             lambda: dev.add_broadcast(up(6), up(2), 3, 2),        # b size
+             lambda: dev.sum_inner(up(5), 2, 2),
+             lambda: dev.sum_rows(up(5), 2, 2),
+             lambda: dev.upsample_nearest2d(up(5), 1, 1, 2, 2, 2, 2),
+             lambda: dev.upsample_nearest2d_backward(up(5), 1, 1, 1, 1, 2, 2),
+             lambda: dev.mse_loss(up(3), up(4))]
+    for c in calls:
+        with pytest.raises(AnyGpuError) as e:
+            c()
+        assert e.value.status == 1
