@@ -32,6 +32,7 @@
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
 #include "umma2_kernel.cuh"
+#include "umma2_splitk_kernel.cuh"
 #include "pair_launch.cuh"
 
 namespace agpu {
@@ -381,6 +382,68 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
                      "gemm_tf32 (umma_tf32_pair_kernel)");
 }
 
+// Split-K over a cluster of S CTA pairs per 256 x 256 tile (S = 2 or 4).
+template <bool A_MN, bool B_MN, int S>
+static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const float* b, float* c,
+                                      uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                      const GemmEpilogue& ep, cudaStream_t s) {
+  using P = GemmPairPolicy<256, A_MN, B_MN>;
+  using Cfg = umma::PairCfg<256>;
+  CUtensorMap ta, tb;
+  if (!A_MN)
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, true));
+  else
+    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, true));
+  if (B_MN)
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, true));
+  else
+    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, P::HALF, false, true));
+  P pol;
+  pol.M = m; pol.N = n; pol.K = k;
+  pol.tiles_m = (int)ceil_div(m, P::PM);
+  pol.tiles_n = (int)ceil_div(n, 256);
+  pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
+  pol.C = c;
+  pol.c_batch = (long long)m * n;
+  pol.bias = ep.bias;
+  pol.resid = ep.resid;
+  pol.act = ep.act;
+  auto kern = umma::umma_tf32_pair_splitk_kernel<P, S>;
+  AGPU_CUDA((set_smem_once<umma::umma_tf32_pair_splitk_kernel<P, S>>(dev, Cfg::SMEM)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * S * pol.tiles), 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2 * S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AGPU_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, pol, dev->d_status));
+  return after_launch(dev, "gemm_tf32 (umma_tf32_pair_splitk_kernel)");
+}
+
+// K slices for a pair GEMM whose 256 x 256 tiles leave most SM pairs idle:
+// the largest S in {4, 2} with tiles * S <= pairs and >= 2 K-blocks per
+// slice, else 1 (AGPU_GEMM_SPLITK=0 disables).
+static int splitk_slices(const agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n,
+                         uint32_t k) {
+  static const bool enabled = [] {
+    const char* e = getenv("AGPU_GEMM_SPLITK");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled) return 1;
+  const long long pairs = std::max(1, dev->sm_count / 2);
+  const long long tiles = (long long)ceil_div(m, 256) * ceil_div(n, 256) * batch;
+  const long long nk = ceil_div(k, BK);
+  for (int sl : {4, 2})
+    if (tiles * sl <= pairs && nk >= 2LL * sl) return sl;
+  return 1;
+}
+
 // The CTA-pair kernel serves TF32 GEMMs with at least one full 256 x 256 tile;
 // AGPU_GEMM_PAIR=0 in the environment selects the single-CTA kernel instead.
 static bool use_pair(uint32_t m, uint32_t n) {
@@ -424,6 +487,19 @@ static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b,
                                bool bt, const GemmEpilogue& ep, cudaStream_t s) {
   const bool wide = n > 128;
   if (!X3 && use_pair(m, n)) {
+    const int sl = splitk_slices(dev, batch, m, n, k);
+    if (sl == 4) {
+      if (!at && !bt) return run_tc_pair_splitk<false, true, 4>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (!at && bt) return run_tc_pair_splitk<false, false, 4>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (at && !bt) return run_tc_pair_splitk<true, true, 4>(dev, a, b, c, batch, m, n, k, ep, s);
+      return run_tc_pair_splitk<true, false, 4>(dev, a, b, c, batch, m, n, k, ep, s);
+    }
+    if (sl == 2) {
+      if (!at && !bt) return run_tc_pair_splitk<false, true, 2>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (!at && bt) return run_tc_pair_splitk<false, false, 2>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (at && !bt) return run_tc_pair_splitk<true, true, 2>(dev, a, b, c, batch, m, n, k, ep, s);
+      return run_tc_pair_splitk<true, false, 2>(dev, a, b, c, batch, m, n, k, ep, s);
+    }
     if (use_wide(dev, batch, m, n, k)) {
       if (!at && !bt) return run_tc_pair<512, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
       if (!at && bt) return run_tc_pair<512, false, false>(dev, a, b, c, batch, m, n, k, ep, s);

@@ -31,6 +31,8 @@ data-path collective); `--gather` adds an NCCL all-gather of the outputs.
            pinned memory), max over ranks.
   roofline the dominant kernel's FLOP/s (CUDA events around each launch) against
            the TF32 dense peak = half the measured bf16 peak.
+  matmul steps are microseconds of device work, less than a host enqueue takes:
+  their K steps are timed as one CUDA graph (`--no-graph`: host launches).
 """
 from __future__ import annotations
 
@@ -154,6 +156,7 @@ class Workload:
     flops = 0.0       # FLOPs of one step
     dom_flops = 0.0   # FLOPs of one launch of the dominant kernel
     dom_kernel = ""
+    graph_default = False  # time the steps as one CUDA graph (latency-bound steps)
 
     def __init__(self, args, rank):
         self.args, self.rank = args, rank
@@ -269,6 +272,7 @@ class BmmSoftmax(Workload):
 
 class Matmul(Workload):
     name = "matmul"
+    graph_default = True
 
     def __init__(self, args, rank):
         super().__init__(args, rank)
@@ -281,7 +285,9 @@ class Matmul(Workload):
 
     def config(self):
         return {"workload": "matmul", "m": self.n, "n": self.n, "k": self.n,
-                "inputs": "U[-1,1) seeded"}
+                "inputs": "U[-1,1) seeded",
+                "timing": "K steps captured in one CUDA graph" if self.args.graph is not False
+                else "K steps launched from the host"}
 
     def host_inputs(self):
         r = np.random.default_rng(1234 + 1000 * self.rank)
@@ -660,23 +666,49 @@ def run_agpu(args, world, rank, local):
     barrier()
     torch.cuda.synchronize()
 
+    # Latency-bound steps (a small matmul is a few microseconds of device work,
+    # less than the host needs to enqueue it) are timed as one CUDA graph of
+    # the K steps: the device runs them back to back, as a graph-captured
+    # inner loop would in an application.  Per-step events cannot be recorded
+    # inside a graph, so the dominant kernel's time is the step time there
+    # (one launch per matmul step).
+    use_graph = wl.graph_default if args.graph is None else args.graph
+    use_graph = use_graph and world == 1 and not args.gather
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graph = None
+    if use_graph:
+        launches0 = dev.launch_count
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                wl.step(dev, sptr, None)
+        launches = dev.launch_count - launches0
+        graph.replay()  # untimed: uploads the graph
+        torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     launches0 = dev.launch_count
     t_start.record()
-    for i in range(args.steps):
-        step(evs[i])
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.steps):
+            step(evs[i])
     t_end.record()
     torch.cuda.synchronize()
-    launches = dev.launch_count - launches0
+    if graph is None:
+        launches = dev.launch_count - launches0
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()
     total_ms = t_start.elapsed_time(t_end)
-    dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    if graph is not None:
+        dom_ms = total_ms / args.steps
+        del graph
+    else:
+        dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
 
     # e2e through the public API with host buffers (pinned), every copy timed
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
@@ -750,6 +782,9 @@ def main():
                     help="bounded single-thread CPU sample beside the all-cores one (0: skip)")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", dest="graph", action="store_true", default=None,
+                    help="time the K steps as one CUDA graph (default: matmul workload only)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false")
     ap.add_argument("--batch", type=int, default=64,
                     help="bmm_softmax batch count (64 = the headline workload; smaller only "
                          "for profiler captures)")

@@ -95,6 +95,46 @@ def test_gemm_transposed_operands(dev, orc, ta, tb, batch, m, n, k, prec):
     assert orc.rel_fro(got, want) <= TOL[prec]
 
 
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("batch,m,n,k", [(1, 256, 256, 256),     # 1 tile, 4 K slices
+                                         (1, 1024, 1024, 1024),  # 16 tiles, 4 slices
+                                         (2, 512, 512, 2048),    # 8 tiles, 4 slices
+                                         (1, 1280, 1536, 512),   # 30 tiles, 2 slices
+                                         (1, 300, 520, 132)])    # ragged M, N and K
+def test_gemm_split_k_cluster(dev, orc, ta, tb, batch, m, n, k):
+    """GEMMs with too few 256 x 256 tiles for the SM pairs run K-split over a
+    cluster of pairs, the partials summed through distributed shared memory."""
+    r = np.random.default_rng(m + n + k)
+    a = r.uniform(-1, 1, batch * m * k).astype(np.float32)
+    b = r.uniform(-1, 1, batch * k * n).astype(np.float32)
+    A = a.reshape(batch, k, m).transpose(0, 2, 1) if ta else a.reshape(batch, m, k)
+    B = b.reshape(batch, n, k).transpose(0, 2, 1) if tb else b.reshape(batch, k, n)
+    before = dev.launch_count
+    got = dev.read(dev.gemm(dev.upload(a), dev.upload(b), batch, m, n, k, ta, tb))
+    assert dev.launch_count - before == 1
+    want = orc.batch_matmul(np.ascontiguousarray(A), np.ascontiguousarray(B), batch, m, n, k,
+                            threads=True)
+    assert orc.rel_fro(got, want) <= 1e-3
+    again = dev.read(dev.gemm(dev.upload(a), dev.upload(b), batch, m, n, k, ta, tb))
+    np.testing.assert_array_equal(got, again)  # fixed summation order
+
+
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_gemm_split_k_epilogue(dev, orc, act):
+    """bias + residual + activation applied once, after the K-slice sum."""
+    m, n, k = 512, 768, 1024
+    r = np.random.default_rng(act)
+    a = (r.standard_normal(m * k) * 0.05).astype(np.float32)
+    b = (r.standard_normal(k * n) * 0.05).astype(np.float32)
+    bias = r.standard_normal(n).astype(np.float32)
+    res = r.standard_normal(m * n).astype(np.float32)
+    got = dev.read(dev.gemm_ex(dev.upload(a), dev.upload(b), 1, m, n, k, bias=dev.upload(bias),
+                               resid=dev.upload(res), act=act))
+    z = orc.matmul(a, b, m, n, k, threads=True).reshape(m, n) + bias + res.reshape(m, n)
+    want = {0: z, 1: z / (1 + np.exp(-z)), 2: np.maximum(z, 0)}[act].ravel()
+    assert orc.rel_fro(got, want) <= 1e-3
+
+
 @pytest.mark.parametrize("rows,cols", [(1000, 2048), (513, 1000), (64, 4), (77, 37),
                                        (9, 5000), (3, 1), (4096, 128), (2, 100000)])
 def test_softmax_parity(dev, orc, rows, cols):
