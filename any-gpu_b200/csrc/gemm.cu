@@ -26,6 +26,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include "agpu_internal.cuh"
@@ -426,11 +427,43 @@ static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const fl
   return after_launch(dev, "gemm_tf32 (umma_tf32_pair_splitk_kernel)");
 }
 
+// Clusters of 2*S CTAs of the split-K kernel that fit on the device at once
+// (a cluster occupies 2*S SMs of one GPC: 15 of 8 CTAs on a B200).
+template <int S>
+static int splitk_max_clusters(agpu_device* dev) {
+  static std::atomic<int> cached{-1};
+  int v = cached.load(std::memory_order_acquire);
+  if (v >= 0) return v;
+  using P = GemmPairPolicy<256, false, true>;
+  using Cfg = umma::PairCfg<256>;
+  int n = 0;
+  if (set_smem_once<umma::umma_tf32_pair_splitk_kernel<P, S>>(dev, Cfg::SMEM) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * S, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2 * S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, umma::umma_tf32_pair_splitk_kernel<P, S>, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  cached.store(n, std::memory_order_release);
+  return n;
+}
+
 // K slices for a pair GEMM whose 256 x 256 tiles leave most SM pairs idle:
-// the largest S in {4, 2} with tiles * S <= pairs and >= 2 K-blocks per
-// slice, else 1 (AGPU_GEMM_SPLITK=0 disables).
-static int splitk_slices(const agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n,
-                         uint32_t k) {
+// the largest S in {4, 2} whose clusters (one per tile) all fit at once, with
+// >= 2 K-blocks per slice and fewer tiles than half the SM pairs; else 1
+// (AGPU_GEMM_SPLITK=0 disables).
+static int splitk_slices(agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n, uint32_t k) {
   static const bool enabled = [] {
     const char* e = getenv("AGPU_GEMM_SPLITK");
     return !(e && e[0] == '0');
@@ -439,8 +472,9 @@ static int splitk_slices(const agpu_device* dev, uint32_t batch, uint32_t m, uin
   const long long pairs = std::max(1, dev->sm_count / 2);
   const long long tiles = (long long)ceil_div(m, 256) * ceil_div(n, 256) * batch;
   const long long nk = ceil_div(k, BK);
-  for (int sl : {4, 2})
-    if (tiles * sl <= pairs && nk >= 2LL * sl) return sl;
+  if (2 * tiles > pairs) return 1;
+  if (nk >= 8 && tiles <= splitk_max_clusters<4>(dev)) return 4;
+  if (nk >= 4 && tiles <= splitk_max_clusters<2>(dev)) return 2;
   return 1;
 }
 

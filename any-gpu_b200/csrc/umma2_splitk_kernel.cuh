@@ -29,13 +29,23 @@
 namespace agpu {
 namespace umma {
 
+// Plain load from distributed shared memory (ordered after the cluster
+// barrier by that barrier's own memory clobber; no clobber here, so the
+// compiler can keep several in flight).
 __device__ __forceinline__ float4 ld_dsmem_v4(uint32_t cluster_addr) {
   float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(cluster_addr));
   return v;
+}
+
+// Exit barrier: a relaxed arrive does not wait for this CTA's outstanding
+// global stores (a release arrive would); it only has to keep every CTA's
+// shared memory alive until the others' reads of it have returned.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;"
+               ::: "memory");
 }
 
 __device__ __forceinline__ float splitk_act(float x, int act) {
@@ -187,14 +197,20 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     constexpr int V4 = BN / 4;
     const uint32_t base = ptx::smem_u32(part);
     float* Cb = pol.C + (long long)tile.b * pol.c_batch;
+    uint32_t src[S];  // the S partials of half h: cluster ranks h, 2 + h, ...
+#pragma unroll
+    for (int pp = 0; pp < S; ++pp) src[pp] = ptx::mapa(base, (uint32_t)(2 * pp + h));
+#pragma unroll 2
     for (int f = threadIdx.x; f < ROWS * V4; f += C::THREADS) {
       const int r = p * ROWS + f / V4, c4 = f % V4;
       const uint32_t off = (uint32_t)(r * PITCH + c4 * 4) * 4u;
-      float4 acc = ld_dsmem_v4(ptx::mapa(base + off, (uint32_t)h));
+      float4 t[S];
+#pragma unroll
+      for (int pp = 0; pp < S; ++pp) t[pp] = ld_dsmem_v4(src[pp] + off);
+      float4 acc = t[0];
 #pragma unroll
       for (int pp = 1; pp < S; ++pp) {
-        const float4 t = ld_dsmem_v4(ptx::mapa(base + off, (uint32_t)(2 * pp + h)));
-        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+        acc.x += t[pp].x; acc.y += t[pp].y; acc.z += t[pp].z; acc.w += t[pp].w;
       }
       const int grow = tile.m0 + h * BM + r, col = tile.n0 + c4 * 4;
       if (grow < pol.M && col < pol.N) {
@@ -216,7 +232,7 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
       }
     }
   }
-  ptx::cluster_sync();  // no CTA leaves while another reads its shared memory
+  cluster_sync_relaxed();  // no CTA leaves while another reads its shared memory
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc_pair(tmem_base, BN);
