@@ -200,35 +200,48 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     uint32_t src[S];  // the S partials of half h: cluster ranks h, 2 + h, ...
 #pragma unroll
     for (int pp = 0; pp < S; ++pp) src[pp] = ptx::mapa(base, (uint32_t)(2 * pp + h));
-#pragma unroll 2
-    for (int f = threadIdx.x; f < ROWS * V4; f += C::THREADS) {
-      const int r = p * ROWS + f / V4, c4 = f % V4;
-      const uint32_t off = (uint32_t)(r * PITCH + c4 * 4) * 4u;
-      float4 t[S];
+    // U rows-chunks per thread per batch, all S*U loads issued before any use
+    constexpr int U = 4, TOTAL = ROWS * V4;
+    for (int f0 = threadIdx.x; f0 < TOTAL; f0 += U * C::THREADS) {
+      float4 t[U][S];
 #pragma unroll
-      for (int pp = 0; pp < S; ++pp) t[pp] = ld_dsmem_v4(src[pp] + off);
-      float4 acc = t[0];
+      for (int u = 0; u < U; ++u) {
+        const int f = f0 + u * C::THREADS;
+        if (f < TOTAL) {
+          const int r = p * ROWS + f / V4, c4 = f % V4;
+          const uint32_t off = (uint32_t)(r * PITCH + c4 * 4) * 4u;
 #pragma unroll
-      for (int pp = 1; pp < S; ++pp) {
-        acc.x += t[pp].x; acc.y += t[pp].y; acc.z += t[pp].z; acc.w += t[pp].w;
+          for (int pp = 0; pp < S; ++pp) t[u][pp] = ld_dsmem_v4(src[pp] + off);
+        }
       }
-      const int grow = tile.m0 + h * BM + r, col = tile.n0 + c4 * 4;
-      if (grow < pol.M && col < pol.N) {
-        const long long o = (long long)grow * pol.N + col;
-        if (pol.bias) {
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(pol.bias + col));
-          acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int f = f0 + u * C::THREADS;
+        if (f >= TOTAL) break;
+        const int r = p * ROWS + f / V4, c4 = f % V4;
+        float4 acc = t[u][0];
+#pragma unroll
+        for (int pp = 1; pp < S; ++pp) {
+          acc.x += t[u][pp].x; acc.y += t[u][pp].y; acc.z += t[u][pp].z; acc.w += t[u][pp].w;
         }
-        if (pol.resid) {
-          const float4 rr = __ldg(
-              reinterpret_cast<const float4*>(pol.resid + (long long)tile.b * pol.c_batch + o));
-          acc.x += rr.x; acc.y += rr.y; acc.z += rr.z; acc.w += rr.w;
+        const int grow = tile.m0 + h * BM + r, col = tile.n0 + c4 * 4;
+        if (grow < pol.M && col < pol.N) {
+          const long long o = (long long)grow * pol.N + col;
+          if (pol.bias) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(pol.bias + col));
+            acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
+          }
+          if (pol.resid) {
+            const float4 rr = __ldg(reinterpret_cast<const float4*>(
+                pol.resid + (long long)tile.b * pol.c_batch + o));
+            acc.x += rr.x; acc.y += rr.y; acc.z += rr.z; acc.w += rr.w;
+          }
+          if (pol.act) {
+            acc.x = splitk_act(acc.x, pol.act); acc.y = splitk_act(acc.y, pol.act);
+            acc.z = splitk_act(acc.z, pol.act); acc.w = splitk_act(acc.w, pol.act);
+          }
+          *reinterpret_cast<float4*>(Cb + o) = acc;
         }
-        if (pol.act) {
-          acc.x = splitk_act(acc.x, pol.act); acc.y = splitk_act(acc.y, pol.act);
-          acc.z = splitk_act(acc.z, pol.act); acc.w = splitk_act(acc.w, pol.act);
-        }
-        *reinterpret_cast<float4*>(Cb + o) = acc;
       }
     }
   }
