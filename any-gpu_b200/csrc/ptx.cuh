@@ -25,6 +25,19 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
+// Programmatic dependent launch.  griddep_wait blocks until the grid this
+// one was launched after (with the programmatic-serialization attribute) has
+// completed and its memory is visible; a no-op otherwise.  A kernel calls it
+// after its prologue and before its first access to global memory that the
+// previous kernel may read or write.  griddep_launch_dependents lets the next
+// such launch start its prologue on free SMs.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

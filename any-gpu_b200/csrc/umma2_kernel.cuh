@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
   __syncthreads();
   ptx::cluster_sync();  // peer barriers initialised, tensor memory allocated
   ptx::tc_fence_after();
+  ptx::griddep_wait();  // the previous kernel's outputs are visible from here on
+  ptx::griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const int num_k = pol.num_k();
   const long long num_tiles = pol.num_tiles();

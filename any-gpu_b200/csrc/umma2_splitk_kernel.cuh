@@ -112,6 +112,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
   __syncthreads();
   ptx::cluster_sync();  // barriers initialised, tensor memory allocated, cluster-wide
   ptx::tc_fence_after();
+  ptx::griddep_wait();  // the previous kernel's outputs are visible from here on
+  ptx::griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const long long tile_id = blockIdx.x / (2 * S);
   const auto tile = pol.tile(tile_id);

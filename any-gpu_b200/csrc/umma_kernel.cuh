@@ -147,6 +147,8 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  ptx::griddep_wait();  // the previous kernel's outputs are visible from here on
+  ptx::griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   const int num_k = pol.num_k();
   const long long num_tiles = pol.num_tiles();

@@ -470,9 +470,17 @@ class Unet(Workload):
     def extra(self, ms_step, ms_dom, peaks):
         gn_ms = ms_step - ms_dom
         nbytes = 2.0 * self.out_elems() * 4
-        return {"group_norm_swish": {"ms": gn_ms, "gbs": nbytes / (gn_ms * 1e-3) / 1e9,
-                                     "frac_hbm": nbytes / (gn_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                                     "note": "step time minus conv time"}}
+        # the group norm runs as two passes (stats, then normalise + swish):
+        # counted per pass it moves x twice and y once
+        pbytes = 3.0 * self.out_elems() * 4
+        gbs, pgbs = nbytes / (gn_ms * 1e-3) / 1e9, pbytes / (gn_ms * 1e-3) / 1e9
+        return {"group_norm_swish": {"ms": gn_ms, "gbs": gbs, "frac_hbm": gbs / peaks["hbm_gbs"],
+                                     "gbs_per_pass": pgbs,
+                                     "frac_hbm_per_pass": pgbs / peaks["hbm_gbs"],
+                                     "note": "step time minus conv time; gbs counts 8 B per "
+                                             "element (x read once, y written once), "
+                                             "gbs_per_pass the 12 B per element the two "
+                                             "passes move"}}
 
 
 class Llama(Workload):
