@@ -63,6 +63,7 @@ TRAFFIC_BYTES = {
     "sdpa": 0.99e9,        # attention_pair_kernel, 64-head capture x 4
     "unet": 1.21e8,        # conv kernel, full workload
     "llama": 2.39e10,      # gate/up GEMM, batch-2 capture x 16
+    "matmul": 2.13e6,      # split-K GEMM at 512^3, full capture (C stays in L2)
 }
 
 
@@ -739,7 +740,8 @@ def run_agpu(args, world, rank, local):
         h2d, d2h = wl.e2e_bytes()
         traffic = TRAFFIC_BYTES.get(wl.name)
         default_size = {"bmm_softmax": args.batch == 64, "sdpa": args.bh == 256 and args.seq == 2048,
-                        "unet": args.images == 16, "llama": args.llama_batch == 32}
+                        "unet": args.images == 16, "llama": args.llama_batch == 32,
+                        "matmul": args.size == 512}
         if not default_size.get(wl.name, False):
             traffic = None
         line = base_line(args, world, wl)
