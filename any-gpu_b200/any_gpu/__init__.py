@@ -175,6 +175,20 @@ class GpuDevice:
         _check(_lib.load().agpu_write(self._h, buf.handle, arr.ctypes.data_as(C.c_void_p),
                                       arr.size))
 
+    def write_async(self, buf: GpuBuffer, host_ptr: int, n: int, offset: int = 0,
+                    stream: int = 0) -> None:
+        """Copy n floats from host address `host_ptr` into buf[offset:offset+n] on
+        `stream` without waiting (the host memory must outlive the copy)."""
+        _check(_lib.load().agpu_write_async(self._h, buf.handle, int(offset), host_ptr, int(n),
+                                            stream or None))
+
+    def read_async(self, buf: GpuBuffer, host_ptr: int, n: int, offset: int = 0,
+                   stream: int = 0) -> None:
+        """Copy buf[offset:offset+n] to host address `host_ptr` on `stream` without
+        waiting."""
+        _check(_lib.load().agpu_read_async(self._h, buf.handle, int(offset), host_ptr, int(n),
+                                           stream or None))
+
     # -------------------------------------------------------- contractions --
     def matmul(self, a: GpuBuffer, b: GpuBuffer, m: int, n: int, k: int) -> GpuBuffer:
         """C[m,n] = A[m,k] B[k,n]; reference `matmul(a,b,m,n,k)` (src/ops/conv.rs:416)."""

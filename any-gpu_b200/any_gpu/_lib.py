@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_alloc": (c_status, [c_dev, u64, P_buf]),
     "agpu_read": (c_status, [c_dev, c_buf, C.c_void_p, u64]),
     "agpu_write": (c_status, [c_dev, c_buf, C.c_void_p, u64]),
+    "agpu_write_async": (c_status, [c_dev, c_buf, u64, C.c_void_p, u64, C.c_void_p]),
+    "agpu_read_async": (c_status, [c_dev, c_buf, u64, C.c_void_p, u64, C.c_void_p]),
     "agpu_buffer_free": (c_status, [c_buf]),
     "agpu_buffer_len": (u64, [c_buf]),
     "agpu_buffer_device_ptr": (C.c_void_p, [c_buf]),

@@ -257,6 +257,35 @@ agpu_status agpu_read(agpu_device* dev, const agpu_buffer* buf, float* host, uin
   return check_device_status(dev);
 }
 
+static agpu_status copy_async(agpu_device* dev, const agpu_buffer* buf, uint64_t offset,
+                              uint64_t n, const void* host, bool to_device, void* stream,
+                              const char* fn) {
+  if (!dev || !buf || (!host && n)) return fail(AGPU_ERR_INVALID, "%s: bad argument", fn);
+  if (offset > buf->len || n > buf->len - offset)
+    return fail(AGPU_ERR_SHAPE, "%s: elements [%llu, %llu) outside a buffer of %llu", fn,
+                (unsigned long long)offset, (unsigned long long)(offset + n),
+                (unsigned long long)buf->len);
+  if (n == 0) return AGPU_OK;
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  float* d = buf->dptr + offset;
+  const cudaError_t e =
+      to_device ? cudaMemcpyAsync(d, host, n * sizeof(float), cudaMemcpyHostToDevice,
+                                  pick_stream(dev, stream))
+                : cudaMemcpyAsync(const_cast<void*>(host), d, n * sizeof(float),
+                                  cudaMemcpyDeviceToHost, pick_stream(dev, stream));
+  return e == cudaSuccess ? AGPU_OK : cuda_status(e, fn);
+}
+
+agpu_status agpu_write_async(agpu_device* dev, agpu_buffer* buf, uint64_t offset,
+                             const float* host, uint64_t n, void* stream) {
+  return copy_async(dev, buf, offset, n, host, true, stream, "agpu_write_async");
+}
+
+agpu_status agpu_read_async(agpu_device* dev, const agpu_buffer* buf, uint64_t offset,
+                            float* host, uint64_t n, void* stream) {
+  return copy_async(dev, buf, offset, n, host, false, stream, "agpu_read_async");
+}
+
 agpu_status agpu_buffer_free(agpu_buffer* buf) {
   if (!buf) return AGPU_OK;
   agpu_device* dev = buf->dev;

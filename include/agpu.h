@@ -97,6 +97,18 @@ AGPU_API agpu_status agpu_read(agpu_device* dev, const agpu_buffer* buf, float* 
 /* Stream-ordered H2D into an existing buffer (no new allocation). */
 AGPU_API agpu_status agpu_write(agpu_device* dev, agpu_buffer* buf, const float* host,
                                 uint64_t n);
+/* Stream-ordered partial copies, for hosts that overlap PCIe transfers in
+ * both directions with compute on other streams (the reference's upload and
+ * read are synchronous).  Copies `n` floats between `host` and elements
+ * [offset, offset + n) of `buf` on `stream` (NULL = the device stream) and
+ * returns without waiting; `host` must stay valid and unchanged until the
+ * stream reaches the copy (page-locked memory makes the copy asynchronous).
+ * offset + n > buffer length -> AGPU_ERR_SHAPE.  Expired device waits are
+ * reported by the next agpu_read / agpu_synchronize. */
+AGPU_API agpu_status agpu_write_async(agpu_device* dev, agpu_buffer* buf, uint64_t offset,
+                                      const float* host, uint64_t n, void* stream);
+AGPU_API agpu_status agpu_read_async(agpu_device* dev, const agpu_buffer* buf, uint64_t offset,
+                                     float* host, uint64_t n, void* stream);
 /* Replaces Drop for GpuBuffer: returns memory to the device pool. */
 AGPU_API agpu_status agpu_buffer_free(agpu_buffer* buf);
 /* GpuBuffer::len (src/device.rs:25). */

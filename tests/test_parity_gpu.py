@@ -703,3 +703,29 @@ def test_tape_ops_errors(dev):
         with pytest.raises(AnyGpuError) as e:
             c()
         assert e.value.status == 1
+
+
+def test_async_partial_copies(dev):
+    """agpu_write_async / agpu_read_async: element ranges of a buffer on a
+    caller's stream, bounds checked like the synchronous calls."""
+    import torch
+    from any_gpu import AnyGpuError
+    n = 1 << 20
+    host = torch.arange(n, dtype=torch.float32).pin_memory()
+    out = torch.zeros(n, dtype=torch.float32).pin_memory()
+    buf = dev.alloc(n)
+    dev.synchronize()
+    s = torch.cuda.Stream()
+    half = n // 2
+    dev.write_async(buf, host.data_ptr() + 4 * half, half, half, s.cuda_stream)  # upper half
+    dev.write_async(buf, host.data_ptr(), half, 0, s.cuda_stream)                # lower half
+    dev.read_async(buf, out.data_ptr() + 4 * 7, n - 7, 7, s.cuda_stream)
+    s.synchronize()
+    np.testing.assert_array_equal(out.numpy()[7:], host.numpy()[7:])
+    assert not out.numpy()[:7].any()
+    np.testing.assert_array_equal(dev.read(buf), host.numpy())
+    for call in (lambda: dev.write_async(buf, host.data_ptr(), 2, n - 1, s.cuda_stream),
+                 lambda: dev.read_async(buf, out.data_ptr(), 1, n, s.cuda_stream)):
+        with pytest.raises(AnyGpuError) as e:
+            call()
+        assert e.value.status == 1
