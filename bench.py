@@ -245,10 +245,6 @@ class BmmSoftmax(Workload):
         for b in (ga, gb, gc, gs):
             b.free()
 
-    e2e_how = ("batch split in 8 chunks; per chunk agpu_write_async of A and B on an upload "
-               "stream, batch_matmul + softmax (launch layer) on a compute stream, "
-               "agpu_read_async of S on a download stream: PCIe both ways overlapped")
-
     def e2e_pipelined(self, dev):
         import torch
         if not hasattr(self, "_pipe"):
@@ -257,7 +253,11 @@ class BmmSoftmax(Workload):
             dev.synchronize()  # the zero fills finish before other streams write
             self._pipe = (bufs, [torch.cuda.Stream() for _ in range(3)])
         (ga, gb, gc, gs), (up, comp, down) = self._pipe
-        chunks = 8 if self.B % 8 == 0 else 1
+        chunks = next(c for c in (16, 8, 4, 2, 1) if self.B % c == 0)
+        self.e2e_how = (f"batch split in {chunks} chunks; per chunk agpu_write_async of A and "
+                        "B on an upload stream, batch_matmul + softmax (launch layer) on a "
+                        "compute stream, agpu_read_async of S on a download stream: PCIe "
+                        "both ways overlapped")
         per = self.B // chunks
         na, nb, nc = per * self.M * self.K, per * self.K * self.N, per * self.M * self.N
         ha, hb = self.host["a"].data_ptr(), self.host["b"].data_ptr()

@@ -729,3 +729,15 @@ def test_async_partial_copies(dev):
         with pytest.raises(AnyGpuError) as e:
             call()
         assert e.value.status == 1
+
+
+def test_tape_ops_empty_and_degenerate(dev):
+    """Zero-size inputs: empty outputs, zero sums, and the shader's 0/0 = NaN
+    for the mean of an empty mse."""
+    up = lambda k: dev.upload(np.ones(k, np.float32))
+    assert dev.concat(up(0), up(0), 0, 3, 4).len == 0
+    assert dev.slice_per_block(up(0), 0, 2, 1, 4).len == 0
+    np.testing.assert_array_equal(dev.read(dev.sum_rows(up(0), 0, 5)), np.zeros(5, np.float32))
+    np.testing.assert_array_equal(dev.read(dev.sum_inner(up(0), 4, 0)), np.zeros(4, np.float32))
+    assert dev.upsample_nearest2d(up(0), 0, 3, 4, 4, 2, 2).len == 0
+    assert np.isnan(dev.read(dev.mse_loss(up(0), up(0)))[0])
