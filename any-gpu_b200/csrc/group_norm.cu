@@ -19,10 +19,14 @@
 //    list through the resident CTAs (stats of round r, normalise round r-1,
 //    so x crosses HBM once: 59.7 us, the CTAs move in lockstep and HBM
 //    idles during their reductions), and splitting the groups into 24-40 MB
-//    slabs run back to back so the re-read hits L2 (61-85 us).  Kernel 1
-//    loads with an L2 evict-last policy, which keeps more of x in L2 for
-//    kernel 2 (52 -> 50 us).  Float4 loads when x, y are 16-byte aligned and spatial % 4 == 0, a
-//    scalar pair of kernels otherwise.
+//    slabs run back to back so the re-read hits L2 (61-85 us); and one pass
+//    on a cluster of 4 CTAs per group holding the group in registers, the
+//    exact mean and M2 exchanged through distributed shared memory (49.5 us:
+//    x crosses HBM once, but the CTAs wait on each other with the data held,
+//    so it is latency-bound at the same time).  Kernel 1 loads with an L2
+//    evict-last policy, which keeps more of x in L2 for kernel 2 (52 -> 50
+//    us).  Float4 loads when x, y are 16-byte aligned and spatial % 4 == 0,
+//    a scalar pair of kernels otherwise.
 //  * `swish` fuses the UNet block's activation, y = z / (1 + exp(-z))
 //    (src/ops/elementwise.rs:77-89), into the store.
 #include <algorithm>

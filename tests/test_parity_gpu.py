@@ -238,6 +238,7 @@ def _gn64(x, gamma, beta, n, c, s, g, eps):
 @pytest.mark.parametrize("swish", [False, True])
 @pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32),   # UNet block: 5 chunks per group
                                      (2, 40, 4096, 8),       # ragged last chunk (20480)
+                                     (2, 64, 4096, 4),       # 65536 per group: 8-CTA cluster
                                      (1, 64, 4096, 2),       # 16 chunks per group
                                      (2, 64, 1024, 32),      # 2 channels x 1024 per group
                                      (3, 12, 37, 4),         # spatial % 4 != 0: chunked path
