@@ -500,11 +500,12 @@ static bool use_pair(uint32_t m, uint32_t n) {
 // AGPU_GEMM_WIDE=0 disables them.
 static bool use_wide(const agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n,
                      uint32_t k) {
-  static const bool enabled = [] {
+  static const int mode = [] {
     const char* e = getenv("AGPU_GEMM_WIDE");
-    return !(e && e[0] == '0');
+    return e ? (e[0] == '0' ? 0 : e[0] == '2' ? 2 : 1) : 1;
   }();
-  if (!enabled || n < 512) return false;
+  if (mode == 0 || n < 512) return false;
+  if (mode == 2) return true;
   const long long pairs = std::max(1, dev->sm_count / 2);
   const long long tm = ceil_div(m, 256);
   auto score = [&](long long bn, double eff) {
