@@ -247,7 +247,7 @@ def _gn64(x, gamma, beta, n, c, s, g, eps):
                                                              # than the resident CTAs roll
                                      (2, 6, 8, 6)])          # per-channel groups
 def test_group_norm_parity(dev, orc, n, c, s, g, swish):
-    """Config 4's group_norm (eps 1e-5, gamma 1, beta 0 there) and ragged shapes
+    """The UNet block's group_norm (eps 1e-5, gamma 1, beta 0 there) and ragged shapes
     against the oracle; tolerance as for softmax (the reference's E[x^2]-mean^2
     in sequential fp32 drifts on large groups)."""
     r = np.random.default_rng(n * c + s)
@@ -380,7 +380,7 @@ def test_conv2d_parity(dev, orc, case, prec):
 
 
 def test_conv2d_unet_full_size_sampled(dev, orc):
-    """Config 4's conv at full size (N16, 320->320, 64x64, 3x3 pad 1), Kaiming-
+    """The UNet block's conv at full size (N16, 320->320, 64x64, 3x3 pad 1), Kaiming-
     uniform weights, bias 0: sampled output planes against float64."""
     n, c, h, w = 16, 320, 64, 64
     r = np.random.default_rng(1237)
