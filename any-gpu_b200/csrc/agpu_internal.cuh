@@ -14,6 +14,9 @@ struct agpu_device {
   int ordinal = 0;
   int sm_count = 0;
   cudaStream_t stream = nullptr;
+  // second stream for work a launcher forks off and joins back (created on
+  // first use, under `mu`)
+  cudaStream_t aux = nullptr;
   cudaMemPool_t pool = nullptr;
   agpu_precision precision = AGPU_PREC_TF32;
   char name[256] = {0};
@@ -62,6 +65,9 @@ void pool_free(agpu_device* dev, void* p, cudaStream_t s);
 
 // Drop one reference to `dev`; the last one releases the stream.
 void device_release(agpu_device* dev);
+
+// The device's auxiliary stream (created on first use), or nullptr on error.
+cudaStream_t aux_stream(agpu_device* dev);
 
 // Allocate an output buffer of n floats on the device stream.
 agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out);

@@ -463,24 +463,15 @@ unsigned grid_for(const agpu_device* dev, long long work) {
   return (unsigned)std::max<long long>(1, std::min<long long>(want, (long long)dev->sm_count * 16));
 }
 
+// The implicit-GEMM conv of images [0, p.n) of a staged NHWC input `xs` and
+// tap-major weights `w2` (both from conv_stage_kernel), output NCHW `y`.
 template <int BN, bool X3, bool PAIR>
-agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
-                        const float* bias, float* y, cudaStream_t s) {
-  static_assert(!(X3 && PAIR), "the CTA-pair kernel is TF32 only");
+agpu_status conv_tc_staged(agpu_device* dev, const ConvParams& p, const float* xs,
+                           const float* w2, const float* bias, float* y, cudaStream_t s) {
   using P = typename std::conditional<PAIR, ConvPairPolicy<BN>, ConvPolicy<BN>>::type;
   const int Cs = (p.cin + 3) / 4 * 4;
   const int Cw = (p.cin + BK - 1) / BK * BK;
-  const uint64_t xs_elems = (uint64_t)p.n * p.h * p.w * Cs;
-  const uint64_t w2_elems = (uint64_t)p.cout * p.kh * p.kw * Cw;
-  void* scratch = nullptr;
-  AGPU_TRY(pool_alloc(dev, (xs_elems + w2_elems) * sizeof(float) + 256, &scratch, s));
-  float* xs = static_cast<float*>(scratch);
-  float* w2 = xs + (xs_elems + 63) / 64 * 64;
-  launch_conv_stage(dev, x, xs, p.n, p.cin, p.h * p.w, Cs, w, w2, p.cout, p.cin, p.kh * p.kw, Cw,
-                    s);
-  agpu_status st = after_launch(dev, "conv_stage_kernel");
-  if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
-
+  agpu_status st = AGPU_OK;
   P pol;
   pol.n_img = p.n; pol.cout = p.cout; pol.KW = p.kw;
   pol.ph = p.ph; pol.pw = p.pw; pol.dh = p.dh; pol.dw = p.dw;
@@ -500,7 +491,7 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   pol.out = y;
 
   EncodeTiledFn enc = encode_fn();
-  if (!enc) { pool_free(dev, scratch, s); return fail(AGPU_ERR_CUDA, "no cuTensorMapEncodeTiled"); }
+  if (!enc) return fail(AGPU_ERR_CUDA, "no cuTensorMapEncodeTiled");
   CUtensorMap ta, tb;
   {
     cuuint64_t dims[4] = {(cuuint64_t)Cs, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
@@ -510,18 +501,15 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     cuuint32_t es[4] = {1, 1, 1, 1};
     // TF32 mode: the TMA unit rounds to tf32 (nearest-even); 3xTF32 needs raw fp32
     CUresult r = enc(&ta, X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_TFLOAT32,
-                     4, xs, dims, strides, box, es,
+                     4, const_cast<float*>(xs), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      pool_free(dev, scratch, s);
+    if (r != CUDA_SUCCESS)
       return fail(AGPU_ERR_CUDA, "conv2d: input tensor map encode failed (%d)", (int)r);
-    }
   }
-  st = make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
-                        (uint64_t)p.kh * p.kw * Cw * p.cout, BK,
-                        PAIR ? umma::PairCfg<BN>::MMA_N / 2 : BN, false, !X3);
-  if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
+  AGPU_TRY(make_tmap_f32_3d(&tb, w2, (uint64_t)p.kh * p.kw * Cw, p.cout, 1,
+                            (uint64_t)p.kh * p.kw * Cw * p.cout, BK,
+                            PAIR ? umma::PairCfg<BN>::MMA_N / 2 : BN, false, !X3));
   if constexpr (PAIR) {
     st = launch_pair(dev, ta, tb, pol, pol.tiles, s,
                      "conv2d_tf32 (umma_tf32_pair_kernel)");
@@ -529,12 +517,78 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     using Cfg = umma::Cfg<BN, X3>;
     auto kern = umma::umma_tf32_kernel<P, X3>;
     cudaError_t e = set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM);
-    if (e != cudaSuccess) { pool_free(dev, scratch, s); return cuda_status(e, "conv attr"); }
+    if (e != cudaSuccess) return cuda_status(e, "conv attr");
     const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
     kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM, s>>>(ta, tb, pol, dev->d_status);
     st = after_launch(dev, "conv2d_tf32 (umma_tf32_kernel)");
   }
+  return st;
+}
+
+// Stage, then convolve.  With the CTA-pair kernel and >= 4 images the batch
+// runs as two halves: the weights and the first half's input are staged on
+// `s`; the second half's input is staged on the device's auxiliary stream
+// while the first half's conv runs (the staging kernel's CTAs fit beside the
+// conv's on each SM), and its conv fills the SMs the first half's last wave
+// leaves idle; `s` then waits for the auxiliary stream.
+// AGPU_CONV_OVERLAP=0 keeps one stage and one conv launch.
+template <int BN, bool X3, bool PAIR>
+agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
+                        const float* bias, float* y, cudaStream_t s) {
+  static_assert(!(X3 && PAIR), "the CTA-pair kernel is TF32 only");
+  const int Cs = (p.cin + 3) / 4 * 4;
+  const int Cw = (p.cin + BK - 1) / BK * BK;
+  const uint64_t img_elems = (uint64_t)p.h * p.w * Cs;
+  const uint64_t xs_elems = (uint64_t)p.n * img_elems;
+  const uint64_t w2_elems = (uint64_t)p.cout * p.kh * p.kw * Cw;
+  void* scratch = nullptr;
+  AGPU_TRY(pool_alloc(dev, (xs_elems + w2_elems) * sizeof(float) + 256, &scratch, s));
+  float* xs = static_cast<float*>(scratch);
+  float* w2 = xs + (xs_elems + 63) / 64 * 64;
+  static const bool overlap_ok = [] {
+    const char* e = getenv("AGPU_CONV_OVERLAP");
+    return !(e && e[0] == '0');
+  }();
+  cudaStream_t s2 = (PAIR && overlap_ok && p.n >= 4) ? aux_stream(dev) : nullptr;
+  const int na = s2 ? p.n / 2 : p.n;
+  launch_conv_stage(dev, x, xs, na, p.cin, p.h * p.w, Cs, w, w2, p.cout, p.cin, p.kh * p.kw, Cw,
+                    s);
+  agpu_status st = after_launch(dev, "conv_stage_kernel");
+  if (st != AGPU_OK) { pool_free(dev, scratch, s); return st; }
+  if (!s2) {
+    st = conv_tc_staged<BN, X3, PAIR>(dev, p, xs, w2, bias, y, s);
+    pool_free(dev, scratch, s);
+    return st;
+  }
+  ConvParams pa = p, pb = p;
+  pa.n = na;
+  pb.n = p.n - na;
+  const uint64_t x_img = (uint64_t)p.cin * p.h * p.w, y_img = (uint64_t)p.cout * p.ho * p.wo;
+  cudaEvent_t forked = nullptr, joined = nullptr;
+  if (cudaEventCreateWithFlags(&forked, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&joined, cudaEventDisableTiming) != cudaSuccess) {
+    if (forked) cudaEventDestroy(forked);
+    pool_free(dev, scratch, s);
+    return cuda_status(cudaGetLastError(), "conv2d: event create");
+  }
+  cudaError_t e = cudaEventRecord(forked, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s2, forked, 0);
+  if (e == cudaSuccess) {
+    launch_conv_stage(dev, x + na * x_img, xs + na * img_elems, pb.n, p.cin, p.h * p.w, Cs,
+                      nullptr, nullptr, 0, 0, 0, 0, s2);
+    st = after_launch(dev, "conv_stage_kernel");
+    if (st == AGPU_OK) st = conv_tc_staged<BN, X3, PAIR>(dev, pa, xs, w2, bias, y, s);
+    if (st == AGPU_OK)
+      st = conv_tc_staged<BN, X3, PAIR>(dev, pb, xs + na * img_elems, w2, bias, y + na * y_img,
+                                        s2);
+    // join in every case, so that the scratch is freed after both streams
+    e = cudaEventRecord(joined, s2);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, joined, 0);
+  }
+  cudaEventDestroy(forked);
+  cudaEventDestroy(joined);
   pool_free(dev, scratch, s);
+  if (e != cudaSuccess && st == AGPU_OK) st = cuda_status(e, "conv2d: stream fork/join");
   return st;
 }
 

@@ -71,7 +71,20 @@ void device_release(agpu_device* dev) {
   cudaStreamSynchronize(dev->stream);
   cudaFree(dev->d_status);
   cudaStreamDestroy(dev->stream);
+  if (dev->aux) {
+    cudaStreamSynchronize(dev->aux);
+    cudaStreamDestroy(dev->aux);
+  }
   delete dev;
+}
+
+cudaStream_t aux_stream(agpu_device* dev) {
+  std::lock_guard<std::mutex> lock(dev->mu);
+  if (!dev->aux && cudaStreamCreateWithFlags(&dev->aux, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    dev->aux = nullptr;
+  }
+  return dev->aux;
 }
 
 agpu_status after_launch(agpu_device* dev, const char* kernel, int n_launches) {

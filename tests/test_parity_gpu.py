@@ -356,6 +356,8 @@ CONV_CASES = [
     (1, 40, 20, 30, 256, 3, 1, 2, 2, 1),    # dilation 2
     (1, 16, 33, 33, 32, 3, 2, 1, 1, 1),     # stride 2 -> direct kernel
     (2, 8, 12, 12, 8, 3, 1, 1, 1, 2),       # groups 2 -> direct kernel
+    (5, 64, 20, 24, 320, 3, 1, 1, 1, 1),    # 5 images: halves of 2 and 3 on two streams
+    (4, 96, 16, 16, 256, 3, 1, 1, 1, 1),    # 4 images, 256-wide pair tiles, two halves
 ]
 
 
