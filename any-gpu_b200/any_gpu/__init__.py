@@ -232,6 +232,16 @@ class GpuDevice:
                          out_c, kh, kw, stride[0], stride[1], padding[0], padding[1],
                          dilation[0], dilation[1], groups)
 
+    def conv2d_group_norm_swish(self, input, weight, bias, batch, in_c, in_h, in_w, out_c, kh,
+                                kw, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1,
+                                gamma=None, beta=None, gn_groups=32, eps=1e-5) -> GpuBuffer:
+        """swish(group_norm(conv2d(...))) in one call (the UNet block)."""
+        return self._new(_lib.load().agpu_conv2d_group_norm_swish, input.handle, weight.handle,
+                         bias.handle if bias is not None else None, batch, in_c, in_h, in_w,
+                         out_c, kh, kw, stride[0], stride[1], padding[0], padding[1],
+                         dilation[0], dilation[1], groups, gamma.handle, beta.handle, gn_groups,
+                         C.c_float(eps))
+
     def conv_transpose2d(self, input, weight, bias, batch, in_c, in_h, in_w, out_c, kh, kw,
                          stride=(1, 1), padding=(0, 0), output_padding=(0, 0),
                          dilation=(1, 1), groups=1) -> GpuBuffer:
@@ -425,6 +435,15 @@ class GpuDevice:
                                               batch, in_c, in_h, in_w, out_c, kh, kw, stride_h,
                                               stride_w, pad_h, pad_w, dil_h, dil_w, groups,
                                               stream or None))
+
+    def launch_conv2d_group_norm_swish(self, x_ptr, w_ptr, bias_ptr, y_ptr, batch, in_c, in_h,
+                                       in_w, out_c, kh, kw, stride_h, stride_w, pad_h, pad_w,
+                                       dil_h, dil_w, groups, gamma_ptr, beta_ptr, gn_groups, eps,
+                                       stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_conv2d_group_norm_swish(
+            self._h, x_ptr, w_ptr, bias_ptr or None, y_ptr, batch, in_c, in_h, in_w, out_c, kh,
+            kw, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, groups, gamma_ptr, beta_ptr,
+            gn_groups, C.c_float(eps), stream or None))
 
     def launch_group_norm_backward(self, dy_ptr, x_ptr, g_ptr, dx_ptr, dg_ptr, db_ptr, batch,
                                    channels, spatial, groups, eps, stream=0):

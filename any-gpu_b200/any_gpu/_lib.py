@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple] = {
                                 i32, P_buf]),
     "agpu_softmax": (c_status, [c_dev, c_buf, u32, u32, P_buf]),
     "agpu_conv2d": (c_status, [c_dev, c_buf, c_buf, c_buf] + [u32] * 14 + [P_buf]),
+    "agpu_conv2d_group_norm_swish": (c_status, [c_dev, c_buf, c_buf, c_buf] + [u32] * 14
+                                     + [c_buf, c_buf, u32, f32, P_buf]),
     "agpu_conv_transpose2d": (c_status, [c_dev, c_buf, c_buf, c_buf] + [u32] * 16 + [P_buf]),
     "agpu_conv2d_grad_weight": (c_status, [c_dev, c_buf, c_buf] + [u32] * 16 + [P_buf]),
     "agpu_conv2d_grad_bias": (c_status, [c_dev, c_buf, u32, u32, u32, u32, P_buf]),
@@ -92,6 +94,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_gemm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p, u32, u32, u32,
                                     u32, i32, i32, C.c_void_p]),
     "agpu_launch_conv2d": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 14 + [C.c_void_p]),
+    "agpu_launch_conv2d_group_norm_swish": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 14
+                                            + [C.c_void_p, C.c_void_p, u32, f32, C.c_void_p]),
     "agpu_launch_group_norm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,
                                           C.c_void_p, u32, u32, u32, u32, f32, i32,
                                           C.c_void_p]),

@@ -201,6 +201,38 @@ extern "C" agpu_status agpu_conv2d(agpu_device* dev, const agpu_buffer* input,
   });
 }
 
+// conv2d -> group_norm -> swish (the UNet block) in one call; the same
+// checks as agpu_conv2d and agpu_group_norm_swish.
+extern "C" agpu_status agpu_conv2d_group_norm_swish(
+    agpu_device* dev, const agpu_buffer* input, const agpu_buffer* weight,
+    const agpu_buffer* bias, uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+    uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw,
+    uint32_t dh, uint32_t dw, uint32_t groups, const agpu_buffer* gamma, const agpu_buffer* beta,
+    uint32_t gn_groups, float eps, agpu_buffer** out) {
+  CHECK_DEV(dev, "conv2d_group_norm_swish");
+  CHECK_BUF(input, "conv2d_group_norm_swish", "input");
+  CHECK_BUF(weight, "conv2d_group_norm_swish", "weight");
+  CHECK_BUF(gamma, "conv2d_group_norm_swish", "gamma");
+  CHECK_BUF(beta, "conv2d_group_norm_swish", "beta");
+  CHECK_OUT(out, "conv2d_group_norm_swish");
+  ConvParams p;
+  AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
+                         &p, "conv2d_group_norm_swish"));
+  CHECK_LEN(input, (uint64_t)batch * in_c * in_h * in_w, "conv2d_group_norm_swish", "input");
+  CHECK_LEN(weight, (uint64_t)out_c * (in_c / groups) * kh * kw, "conv2d_group_norm_swish",
+            "weight");
+  if (bias) CHECK_LEN(bias, out_c, "conv2d_group_norm_swish", "bias");
+  if (gn_groups == 0 || out_c % gn_groups != 0)  // src/ops/norm.rs:218-221
+    return fail(AGPU_ERR_SHAPE, "conv2d_group_norm_swish: channels must be divisible by groups");
+  CHECK_LEN(gamma, out_c, "conv2d_group_norm_swish", "gamma");
+  CHECK_LEN(beta, out_c, "conv2d_group_norm_swish", "beta");
+  const GnEpilogue gn{gamma->dptr, beta->dptr, gn_groups, eps, true};
+  return with_output(dev, (uint64_t)batch * out_c * p.ho * p.wo, out, [&](float* y) {
+    return launch_conv2d_gn(dev, p, input->dptr, weight->dptr, bias ? bias->dptr : nullptr, y, gn,
+                            dev->stream);
+  });
+}
+
 extern "C" agpu_status agpu_conv_transpose2d(
     agpu_device* dev, const agpu_buffer* input, const agpu_buffer* weight,
     const agpu_buffer* bias, uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
@@ -688,6 +720,23 @@ agpu_status agpu_launch_conv2d(agpu_device* dev, const float* input, const float
   AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
                          &p, "launch_conv2d"));
   return launch_conv2d(dev, p, input, weight, bias, out, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_conv2d_group_norm_swish(
+    agpu_device* dev, const float* input, const float* weight, const float* bias, float* out,
+    uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w, uint32_t out_c, uint32_t kh,
+    uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw, uint32_t dh, uint32_t dw,
+    uint32_t groups, const float* gamma, const float* beta, uint32_t gn_groups, float eps,
+    void* stream) {
+  CHECK_DEV(dev, "launch_conv2d_group_norm_swish");
+  ConvParams p;
+  AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
+                         &p, "launch_conv2d_group_norm_swish"));
+  if (gn_groups == 0 || out_c % gn_groups != 0)
+    return fail(AGPU_ERR_SHAPE,
+                "launch_conv2d_group_norm_swish: channels must be divisible by groups");
+  const GnEpilogue gn{gamma, beta, gn_groups, eps, true};
+  return launch_conv2d_gn(dev, p, input, weight, bias, out, gn, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,

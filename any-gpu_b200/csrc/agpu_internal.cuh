@@ -150,6 +150,17 @@ struct ConvParams {
 };
 agpu_status launch_conv2d(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
                           const float* bias, float* y, cudaStream_t s);
+// conv2d followed by group_norm (+ swish) of its output, in place.
+struct GnEpilogue {
+  const float* gamma;
+  const float* beta;
+  uint32_t groups;
+  float eps;
+  bool swish;
+};
+agpu_status launch_conv2d_gn(agpu_device* dev, const ConvParams& p, const float* x,
+                             const float* w, const float* bias, float* y, const GnEpilogue& gn,
+                             cudaStream_t s);
 agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const float* x,
                                     const float* w, const float* bias, float* y, cudaStream_t s);
 agpu_status launch_conv2d_grad_weight(agpu_device* dev, const ConvParams& p, const float* x,

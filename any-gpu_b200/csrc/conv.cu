@@ -534,8 +534,14 @@ agpu_status conv_tc_staged(agpu_device* dev, const ConvParams& p, const float* x
 // AGPU_CONV_OVERLAP=0 keeps one stage and one conv launch.
 template <int BN, bool X3, bool PAIR>
 agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, const float* w,
-                        const float* bias, float* y, cudaStream_t s) {
+                        const float* bias, float* y, cudaStream_t s, const GnEpilogue* gn) {
   static_assert(!(X3 && PAIR), "the CTA-pair kernel is TF32 only");
+  // the fused group norm (+ swish) of images [0, n) of y, in place, on `st`
+  auto norm = [&](const ConvParams& q, float* yq, cudaStream_t st) {
+    return gn ? launch_group_norm(dev, yq, gn->gamma, gn->beta, yq, q.n, q.cout, q.ho * q.wo,
+                                  gn->groups, gn->eps, gn->swish, st)
+              : AGPU_OK;
+  };
   const int Cs = (p.cin + 3) / 4 * 4;
   const int Cw = (p.cin + BK - 1) / BK * BK;
   const uint64_t img_elems = (uint64_t)p.h * p.w * Cs;
@@ -558,6 +564,7 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
   if (!s2) {
     st = conv_tc_staged<BN, X3, PAIR>(dev, p, xs, w2, bias, y, s);
     pool_free(dev, scratch, s);
+    if (st == AGPU_OK) st = norm(p, y, s);
     return st;
   }
   ConvParams pa = p, pb = p;
@@ -581,6 +588,9 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     if (st == AGPU_OK)
       st = conv_tc_staged<BN, X3, PAIR>(dev, pb, xs + na * img_elems, w2, bias, y + na * y_img,
                                         s2);
+    // a fused group norm of the first half runs beside the second half's conv
+    if (st == AGPU_OK) st = norm(pa, y, s);
+    if (st == AGPU_OK) st = norm(pb, y + na * y_img, s2);
     // join in every case, so that the scratch is freed after both streams
     e = cudaEventRecord(joined, s2);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, joined, 0);
@@ -595,7 +605,8 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
 // BN: output-channel tile minimising padding (N of the MMA, multiple of 32).
 template <bool X3>
 agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float* x,
-                             const float* w, const float* bias, float* y, cudaStream_t s) {
+                             const float* w, const float* bias, float* y, cudaStream_t s,
+                             const GnEpilogue* gn = nullptr) {
   // TF32 convs with at least two 128-pixel tiles per image run on CTA pairs;
   // output-channel counts that are multiples of 320 take 256 x 320 tiles (two
   // MMAs of N 160: fewer TMA bytes per FLOP than 256 x 160).
@@ -607,18 +618,18 @@ agpu_status dispatch_conv_tc(agpu_device* dev, const ConvParams& p, const float*
   }();
   if constexpr (PAIR) {
     if ((long long)p.ho * p.wo >= 256) {
-      if (wide && p.cout % 320 == 0) return run_conv_tc<320, X3, true>(dev, p, x, w, bias, y, s);
+      if (wide && p.cout % 320 == 0) return run_conv_tc<320, X3, true>(dev, p, x, w, bias, y, s, gn);
       if (p.cout % 160 == 0 && p.cout % 256 != 0)
-        return run_conv_tc<160, X3, true>(dev, p, x, w, bias, y, s);
-      if (p.cout >= 256) return run_conv_tc<256, X3, true>(dev, p, x, w, bias, y, s);
-      if (p.cout > 96) return run_conv_tc<128, X3, true>(dev, p, x, w, bias, y, s);
-      return run_conv_tc<64, X3, true>(dev, p, x, w, bias, y, s);
+        return run_conv_tc<160, X3, true>(dev, p, x, w, bias, y, s, gn);
+      if (p.cout >= 256) return run_conv_tc<256, X3, true>(dev, p, x, w, bias, y, s, gn);
+      if (p.cout > 96) return run_conv_tc<128, X3, true>(dev, p, x, w, bias, y, s, gn);
+      return run_conv_tc<64, X3, true>(dev, p, x, w, bias, y, s, gn);
     }
   }
-  if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3, false>(dev, p, x, w, bias, y, s);
-  if (p.cout >= 256) return run_conv_tc<256, X3, false>(dev, p, x, w, bias, y, s);
-  if (p.cout > 96) return run_conv_tc<128, X3, false>(dev, p, x, w, bias, y, s);
-  return run_conv_tc<64, X3, false>(dev, p, x, w, bias, y, s);
+  if (p.cout % 160 == 0 && p.cout % 256 != 0) return run_conv_tc<160, X3, false>(dev, p, x, w, bias, y, s, gn);
+  if (p.cout >= 256) return run_conv_tc<256, X3, false>(dev, p, x, w, bias, y, s, gn);
+  if (p.cout > 96) return run_conv_tc<128, X3, false>(dev, p, x, w, bias, y, s, gn);
+  return run_conv_tc<64, X3, false>(dev, p, x, w, bias, y, s, gn);
 }
 
 template <int BN, bool X3>
@@ -722,6 +733,21 @@ agpu_status launch_conv2d(agpu_device* dev, const ConvParams& p, const float* x,
       x, w, bias, y, p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, p.sh, p.sw, p.ph, p.pw, p.dh, p.dw,
       p.groups, p.ho, p.wo);
   return after_launch(dev, "conv2d_direct_kernel");
+}
+
+agpu_status launch_conv2d_gn(agpu_device* dev, const ConvParams& p, const float* x,
+                             const float* w, const float* bias, float* y, const GnEpilogue& gn,
+                             cudaStream_t s) {
+  const long long total = (long long)p.n * p.cout * p.ho * p.wo;
+  if (total == 0) return AGPU_OK;
+  if (dev->precision != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
+    if (dev->precision == AGPU_PREC_TF32X3)
+      return dispatch_conv_tc<true>(dev, p, x, w, bias, y, s, &gn);
+    return dispatch_conv_tc<false>(dev, p, x, w, bias, y, s, &gn);
+  }
+  AGPU_TRY(launch_conv2d(dev, p, x, w, bias, y, s));
+  return launch_group_norm(dev, y, gn.gamma, gn.beta, y, p.n, p.cout, p.ho * p.wo, gn.groups,
+                           gn.eps, gn.swish, s);
 }
 
 agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const float* x,

@@ -158,6 +158,7 @@ class Workload:
     dom_flops = 0.0   # FLOPs of one launch of the dominant kernel
     dom_kernel = ""
     graph_default = False  # time the steps as one CUDA graph (latency-bound steps)
+    dom_separate = False   # dominant kernel timed in its own loop (dom_step), not per step
 
     def __init__(self, args, rank):
         self.args, self.rank = args, rank
@@ -443,7 +444,8 @@ class Unet(Workload):
         super().__init__(args, rank)
         self.n, self.c, self.h, self.w, self.g = args.images, 320, 64, 64, 32
         self.flops = self.dom_flops = 2.0 * self.n * self.c * self.h * self.w * self.c * 9
-        self.dom_kernel = "umma_tf32_pair_kernel<ConvPairPolicy<160>> (implicit-GEMM conv2d)"
+        self.dom_kernel = ("umma_tf32_pair_kernel<ConvPairPolicy<320>> (implicit-GEMM conv2d, "
+                           "staging included; timed in a separate loop of conv2d calls)")
 
     def config(self):
         return {"workload": "unet_block conv2d3x3->group_norm->swish", "n": self.n,
@@ -466,29 +468,34 @@ class Unet(Workload):
         self.Y1 = torch.empty(self.out_elems(), dtype=torch.float32, device=f"cuda:{local}")
         self.Y = torch.empty_like(self.Y1)
 
+    # The step is the fused entry point (conv2d -> group_norm -> swish in one
+    # call, the group norm of one half of the batch beside the conv of the
+    # other), so the conv's own time comes from a separate loop of conv2d
+    # launches after the timed region.
+    dom_separate = True
+
     def step(self, dev, sptr, ev=None):
         d = self.dev_in
-        if ev is not None:
-            ev[0].record()
+        dev.launch_conv2d_group_norm_swish(
+            d["x"].data_ptr(), d["w"].data_ptr(), 0, self.Y.data_ptr(), self.n, self.c, self.h,
+            self.w, self.c, 3, 3, 1, 1, 1, 1, 1, 1, 1, d["gamma"].data_ptr(),
+            d["beta"].data_ptr(), self.g, 1e-5, sptr)
+
+    def dom_step(self, dev, sptr):
+        d = self.dev_in
         dev.launch_conv2d(d["x"].data_ptr(), d["w"].data_ptr(), 0, self.Y1.data_ptr(), self.n,
                           self.c, self.h, self.w, self.c, 3, 3, 1, 1, 1, 1, 1, 1, 1, sptr)
-        if ev is not None:
-            ev[1].record()
-        dev.launch_group_norm(self.Y1.data_ptr(), d["gamma"].data_ptr(), d["beta"].data_ptr(),
-                              self.Y.data_ptr(), self.n, self.c, self.h * self.w, self.g, 1e-5,
-                              True, sptr)
 
     def output(self):
         return self.Y
 
     def e2e_step(self, dev):
         g = {k: dev.upload(v.numpy()) for k, v in self.host.items()}
-        y1 = dev.conv2d(g["x"], g["w"], None, self.n, self.c, self.h, self.w, self.c, 3, 3,
-                        (1, 1), (1, 1), (1, 1), 1)
-        y = dev.group_norm_swish(y1, g["gamma"], g["beta"], self.n, self.c, self.h * self.w,
-                                 self.g, 1e-5)
+        y = dev.conv2d_group_norm_swish(g["x"], g["w"], None, self.n, self.c, self.h, self.w,
+                                        self.c, 3, 3, (1, 1), (1, 1), (1, 1), 1, gamma=g["gamma"],
+                                        beta=g["beta"], gn_groups=self.g, eps=1e-5)
         dev.read(y, out=self.out_host.numpy())
-        for b in list(g.values()) + [y1, y]:
+        for b in list(g.values()) + [y]:
             b.free()
 
     def cpu_sample(self, orc, target_s, threads=True):
@@ -517,7 +524,9 @@ class Unet(Workload):
         return {"group_norm_swish": {"ms": gn_ms, "gbs": gbs, "frac_hbm": gbs / peaks["hbm_gbs"],
                                      "gbs_per_pass": pgbs,
                                      "frac_hbm_per_pass": pgbs / peaks["hbm_gbs"],
-                                     "note": "step time minus conv time; gbs counts 8 B per "
+                                     "note": "step time minus the conv-only time (the part "
+                                             "of the group norm not hidden behind the "
+                                             "conv); gbs counts 8 B per "
                                              "element (x read once, y written once), "
                                              "gbs_per_pass the 12 B per element the two "
                                              "passes move"}}
@@ -755,6 +764,16 @@ def run_agpu(args, world, rank, local):
     if graph is not None:
         dom_ms = total_ms / args.steps
         del graph
+    elif wl.dom_separate:
+        for _ in range(2):
+            wl.dom_step(dev, sptr)
+        torch.cuda.synchronize()
+        for e0, e1 in evs:
+            e0.record()
+            wl.dom_step(dev, sptr)
+            e1.record()
+        torch.cuda.synchronize()
+        dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
     else:
         dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
 

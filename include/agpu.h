@@ -170,6 +170,18 @@ AGPU_API agpu_status agpu_conv2d(agpu_device* dev, const agpu_buffer* input,
                                  uint32_t stride_w, uint32_t pad_h, uint32_t pad_w,
                                  uint32_t dil_h, uint32_t dil_w, uint32_t groups,
                                  agpu_buffer** out);
+/* conv2d -> group_norm -> swish (the UNet block) in one call:
+ * out = swish(group_norm(conv2d(input, weight, bias, ...), gamma, beta,
+ * gn_groups, eps)).  Arguments and shape checks as agpu_conv2d and
+ * agpu_group_norm_swish (out_c % gn_groups != 0 -> AGPU_ERR_SHAPE).  With
+ * several images the batch runs in two halves on two streams and the group
+ * norm of one half overlaps the conv of the other. */
+AGPU_API agpu_status agpu_conv2d_group_norm_swish(
+    agpu_device* dev, const agpu_buffer* input, const agpu_buffer* weight,
+    const agpu_buffer* bias, uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w,
+    uint32_t out_c, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw,
+    uint32_t dh, uint32_t dw, uint32_t groups, const agpu_buffer* gamma, const agpu_buffer* beta,
+    uint32_t gn_groups, float eps, agpu_buffer** out);
 /* GpuDevice::conv_transpose2d (src/ops/conv.rs:484-530): weight
  * [in_c, out_c/groups, kh, kw]; out = (in-1)*stride - 2*pad + dil*(k-1) + out_pad + 1. */
 AGPU_API agpu_status agpu_conv_transpose2d(agpu_device* dev, const agpu_buffer* input,
@@ -374,6 +386,13 @@ AGPU_API agpu_status agpu_launch_conv2d(agpu_device* dev, const float* input, co
                                         uint32_t stride_h, uint32_t stride_w, uint32_t pad_h,
                                         uint32_t pad_w, uint32_t dil_h, uint32_t dil_w,
                                         uint32_t groups, void* stream);
+/* Launch-layer agpu_conv2d_group_norm_swish (caller memory, caller stream). */
+AGPU_API agpu_status agpu_launch_conv2d_group_norm_swish(
+    agpu_device* dev, const float* input, const float* weight, const float* bias, float* out,
+    uint32_t batch, uint32_t in_c, uint32_t in_h, uint32_t in_w, uint32_t out_c, uint32_t kh,
+    uint32_t kw, uint32_t sh, uint32_t sw, uint32_t ph, uint32_t pw, uint32_t dh, uint32_t dw,
+    uint32_t groups, const float* gamma, const float* beta, uint32_t gn_groups, float eps,
+    void* stream);
 AGPU_API agpu_status agpu_launch_group_norm(agpu_device* dev, const float* x, const float* gamma,
                                             const float* beta, float* y, uint32_t batch,
                                             uint32_t channels, uint32_t spatial, uint32_t groups,

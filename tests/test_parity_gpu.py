@@ -744,3 +744,28 @@ def test_tape_ops_empty_and_degenerate(dev):
     np.testing.assert_array_equal(dev.read(dev.sum_inner(up(0), 4, 0)), np.zeros(4, np.float32))
     assert dev.upsample_nearest2d(up(0), 0, 3, 4, 4, 2, 2).len == 0
     assert np.isnan(dev.read(dev.mse_loss(up(0), up(0)))[0])
+
+
+@pytest.mark.parametrize("n,cin,h,w,cout,g", [(16, 320, 64, 64, 320, 32), (5, 64, 20, 24, 320, 32),
+                                              (1, 32, 16, 16, 64, 8), (2, 3, 17, 19, 64, 4)])
+def test_conv2d_group_norm_swish_fused(dev, n, cin, h, w, cout, g):
+    """The fused UNet block equals conv2d followed by group_norm_swish, bit for
+    bit (the same kernels, the group norm per half of the batch)."""
+    r = np.random.default_rng(n + cin + cout)
+    x = r.standard_normal(n * cin * h * w).astype(np.float32)
+    bound = np.sqrt(6.0 / (cin * 9))
+    wt = r.uniform(-bound, bound, cout * cin * 9).astype(np.float32)
+    bias = (0.1 * r.standard_normal(cout)).astype(np.float32)
+    gamma = (1 + 0.1 * r.standard_normal(cout)).astype(np.float32)
+    beta = (0.1 * r.standard_normal(cout)).astype(np.float32)
+    X, W, B, G, Bt = (dev.upload(v) for v in (x, wt, bias, gamma, beta))
+    got = dev.read(dev.conv2d_group_norm_swish(X, W, B, n, cin, h, w, cout, 3, 3, (1, 1), (1, 1),
+                                               gamma=G, beta=Bt, gn_groups=g, eps=1e-5))
+    y = dev.conv2d(X, W, B, n, cin, h, w, cout, 3, 3, (1, 1), (1, 1))
+    want = dev.read(dev.group_norm_swish(y, G, Bt, n, cout, h * w, g, 1e-5))
+    np.testing.assert_array_equal(got, want)
+    from any_gpu import AnyGpuError
+    with pytest.raises(AnyGpuError) as e:
+        dev.conv2d_group_norm_swish(X, W, B, n, cin, h, w, cout, 3, 3, (1, 1), (1, 1), gamma=G,
+                                    beta=Bt, gn_groups=cout + 1)
+    assert e.value.status == 1
