@@ -436,6 +436,11 @@ class GpuDevice:
                                               stride_w, pad_h, pad_w, dil_h, dil_w, groups,
                                               stream or None))
 
+    def launch_batch_matmul_softmax(self, a_ptr: int, b_ptr: int, out_ptr: int, batch: int,
+                                    m: int, n: int, k: int, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_batch_matmul_softmax(self._h, a_ptr, b_ptr, out_ptr,
+                                                            batch, m, n, k, stream or None))
+
     def launch_conv2d_group_norm_swish(self, x_ptr, w_ptr, bias_ptr, y_ptr, batch, in_c, in_h,
                                        in_w, out_c, kh, kw, stride_h, stride_w, pad_h, pad_w,
                                        dil_h, dil_w, groups, gamma_ptr, beta_ptr, gn_groups, eps,

@@ -94,6 +94,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_gemm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p, u32, u32, u32,
                                     u32, i32, i32, C.c_void_p]),
     "agpu_launch_conv2d": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 14 + [C.c_void_p]),
+    "agpu_launch_batch_matmul_softmax": (c_status, [c_dev] + [C.c_void_p] * 3 + [u32] * 4
+                                         + [C.c_void_p]),
     "agpu_launch_conv2d_group_norm_swish": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 14
                                             + [C.c_void_p, C.c_void_p, u32, f32, C.c_void_p]),
     "agpu_launch_group_norm": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -4,6 +4,7 @@
 // `impl GpuDevice`: the same argument order and meaning, the same size
 // checks (returned as AGPU_ERR_SHAPE where the reference's `ensure!` returns
 // Err), a freshly allocated output buffer owned by the caller.
+#include <cstdlib>
 #include <vector>
 
 #include "agpu_internal.cuh"
@@ -113,6 +114,62 @@ agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a, const agpu
   });
 }
 
+// C = batch_matmul(A, B), then the row softmax of C in place (each row is
+// read completely before any of it is written).  When the batch splits into
+// pieces that each still fill the SMs (up to 8), piece i runs on stream i % 2
+// (the caller's and the device's auxiliary stream): piece i's softmax
+// (HBM-bound) then runs beside piece i+1's GEMM (tensor-bound), and only the
+// last piece's softmax is exposed.
+static agpu_status bmm_softmax(agpu_device* dev, const float* a, const float* b, float* c,
+                               uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                               cudaStream_t s) {
+  const uint64_t tiles_item = ceil_div(m, 256) * ceil_div(n, 256);
+  uint32_t pieces = 1;
+  static const uint32_t max_pieces = [] {
+    const char* e = getenv("AGPU_BMM_SOFTMAX_PIECES");
+    return e ? (uint32_t)atoi(e) : 8u;
+  }();
+  for (uint32_t p : {8u, 4u, 2u})
+    if (p <= max_pieces &&
+        batch >= p && (uint64_t)(batch / p) * tiles_item >= (uint64_t)dev->sm_count) {
+      pieces = p;
+      break;
+    }
+  cudaStream_t s2 = pieces > 1 ? aux_stream(dev) : nullptr;
+  if (!s2) {
+    AGPU_TRY(launch_gemm(dev, a, b, c, batch, m, n, k, false, false, s));
+    return launch_softmax(dev, c, c, (uint64_t)batch * m, n, s);
+  }
+  cudaEvent_t forked = nullptr, joined = nullptr;
+  if (cudaEventCreateWithFlags(&forked, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&joined, cudaEventDisableTiming) != cudaSuccess) {
+    if (forked) cudaEventDestroy(forked);
+    return cuda_status(cudaGetLastError(), "batch_matmul_softmax: event create");
+  }
+  agpu_status st = AGPU_OK;
+  cudaError_t e = cudaEventRecord(forked, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s2, forked, 0);
+  if (e == cudaSuccess) {
+    uint32_t b0 = 0;
+    for (uint32_t i = 0; i < pieces && st == AGPU_OK; ++i) {
+      const uint32_t nb = (uint32_t)((uint64_t)batch * (i + 1) / pieces) - b0;
+      cudaStream_t si = (i % 2) ? s2 : s;
+      const float* ai = a + (uint64_t)b0 * m * k;
+      const float* bi = b + (uint64_t)b0 * k * n;
+      float* ci = c + (uint64_t)b0 * m * n;
+      st = launch_gemm(dev, ai, bi, ci, nb, m, n, k, false, false, si);
+      if (st == AGPU_OK) st = launch_softmax(dev, ci, ci, (uint64_t)nb * m, n, si);
+      b0 += nb;
+    }
+    e = cudaEventRecord(joined, s2);  // join in every case
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, joined, 0);
+  }
+  cudaEventDestroy(forked);
+  cudaEventDestroy(joined);
+  if (e != cudaSuccess && st == AGPU_OK) st = cuda_status(e, "batch_matmul_softmax: fork/join");
+  return st;
+}
+
 agpu_status agpu_batch_matmul_softmax(agpu_device* dev, const agpu_buffer* a,
                                       const agpu_buffer* b, uint32_t batch, uint32_t m,
                                       uint32_t n, uint32_t k, agpu_buffer** out) {
@@ -124,9 +181,7 @@ agpu_status agpu_batch_matmul_softmax(agpu_device* dev, const agpu_buffer* a,
   CHECK_LEN(a, (uint64_t)batch * m * k, "batch_matmul_softmax", "A");
   CHECK_LEN(b, (uint64_t)batch * k * n, "batch_matmul_softmax", "B");
   return with_output(dev, (uint64_t)batch * m * n, out, [&](float* c) {
-    AGPU_TRY(launch_gemm(dev, a->dptr, b->dptr, c, batch, m, n, k, false, false, dev->stream));
-    // each row is read completely before any of it is written: in place is exact
-    return launch_softmax(dev, c, c, (uint64_t)batch * m, n, dev->stream);
+    return bmm_softmax(dev, a->dptr, b->dptr, c, batch, m, n, k, dev->stream);
   });
 }
 
@@ -720,6 +775,16 @@ agpu_status agpu_launch_conv2d(agpu_device* dev, const float* input, const float
   AGPU_TRY(conv_geometry(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, dh, dw, groups,
                          &p, "launch_conv2d"));
   return launch_conv2d(dev, p, input, weight, bias, out, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_batch_matmul_softmax(agpu_device* dev, const float* a, const float* b,
+                                             float* out, uint32_t batch, uint32_t m, uint32_t n,
+                                             uint32_t k, void* stream) {
+  CHECK_DEV(dev, "launch_batch_matmul_softmax");
+  if ((!a || !b || !out) && (uint64_t)batch * m * n)
+    return fail(AGPU_ERR_INVALID, "launch_batch_matmul_softmax: NULL pointer");
+  if ((uint64_t)batch * m * n == 0) return AGPU_OK;
+  return bmm_softmax(dev, a, b, out, batch, m, n, k, pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_conv2d_group_norm_swish(

@@ -376,6 +376,14 @@ AGPU_API agpu_status agpu_launch_adamw(agpu_device* dev, const agpu_adamw_tensor
 AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, const float* b,
                                               float* c, uint32_t batch, uint32_t m, uint32_t n,
                                               uint32_t k, void* stream);
+/* Launch-layer agpu_batch_matmul_softmax: out = softmax(A * B) row-wise, on
+ * `stream`; the GEMM writes `out` and the softmax runs on it in place.  With
+ * a large batch the two halves run on two streams (the first half's softmax
+ * beside the second half's GEMM). */
+AGPU_API agpu_status agpu_launch_batch_matmul_softmax(agpu_device* dev, const float* a,
+                                                     const float* b, float* out, uint32_t batch,
+                                                     uint32_t m, uint32_t n, uint32_t k,
+                                                     void* stream);
 AGPU_API agpu_status agpu_launch_gemm(agpu_device* dev, const float* a, const float* b, float* c,
                                       uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                       int trans_a, int trans_b, void* stream);

@@ -323,6 +323,30 @@ def test_batch_matmul_softmax(dev, orc, batch, m, n, k):
     np.testing.assert_array_equal(got, sep)
 
 
+@pytest.mark.parametrize("batch,k", [(8, 256),    # 2 pieces of 4 x 64 tiles
+                                     (13, 64),    # 4 pieces of 3-4 x 64 tiles
+                                     (24, 32)])   # 8 pieces of 3 x 64 tiles
+def test_batch_matmul_softmax_two_streams(dev, batch, k):
+    """A batch large enough to run in pieces on two streams (each piece's
+    softmax beside the next piece's GEMM) equals the separate calls, through
+    both the buffer and the launch layer."""
+    import torch
+    m = n = 2048
+    r = np.random.default_rng(batch)
+    a = (r.standard_normal(batch * m * k) * 0.05).astype(np.float32)
+    b = (r.standard_normal(batch * k * n) * 0.05).astype(np.float32)
+    A, B = dev.upload(a), dev.upload(b)
+    got = dev.read(dev.batch_matmul_softmax(A, B, batch, m, n, k))
+    sep = dev.read(dev.softmax(dev.batch_matmul(A, B, batch, m, n, k), batch * m, n))
+    np.testing.assert_array_equal(got, sep)
+    out = torch.empty(batch * m * n, device="cuda")
+    s = torch.cuda.Stream()
+    dev.launch_batch_matmul_softmax(A.device_ptr, B.device_ptr, out.data_ptr(), batch, m, n, k,
+                                    s.cuda_stream)
+    s.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), sep)
+
+
 @pytest.mark.parametrize("n,c,s,g", [(16, 320, 4096, 32), (3, 12, 37, 4)])
 def test_group_norm_in_place(dev, orc, n, c, s, g):
     """y may alias x: every chunk is read (twice) before it is overwritten."""
