@@ -116,22 +116,23 @@ agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a, const agpu
 
 // C = batch_matmul(A, B), then the row softmax of C in place (each row is
 // read completely before any of it is written).  When the batch splits into
-// pieces that each still fill the SMs (up to 8), piece i runs on stream i % 2
-// (the caller's and the device's auxiliary stream): piece i's softmax
-// (HBM-bound) then runs beside piece i+1's GEMM (tensor-bound), and only the
-// last piece's softmax is exposed.
+// pieces that each still fill the SMs (up to 8), the GEMMs run back to back on
+// the caller's stream and each piece's softmax on the device's auxiliary
+// stream as soon as its GEMM is done: the softmax (HBM-bound) runs beside
+// the next GEMM (tensor-bound), no GEMM ever waits for a softmax, and only
+// the last piece's softmax is exposed.
 static agpu_status bmm_softmax(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                cudaStream_t s) {
   const uint64_t tiles_item = ceil_div(m, 256) * ceil_div(n, 256);
-  uint32_t pieces = 1;
   static const uint32_t max_pieces = [] {
     const char* e = getenv("AGPU_BMM_SOFTMAX_PIECES");
     return e ? (uint32_t)atoi(e) : 8u;
   }();
+  uint32_t pieces = 1;
   for (uint32_t p : {8u, 4u, 2u})
-    if (p <= max_pieces &&
-        batch >= p && (uint64_t)(batch / p) * tiles_item >= (uint64_t)dev->sm_count) {
+    if (p <= max_pieces && batch >= p &&
+        (uint64_t)(batch / p) * tiles_item >= (uint64_t)dev->sm_count) {
       pieces = p;
       break;
     }
@@ -140,32 +141,29 @@ static agpu_status bmm_softmax(agpu_device* dev, const float* a, const float* b,
     AGPU_TRY(launch_gemm(dev, a, b, c, batch, m, n, k, false, false, s));
     return launch_softmax(dev, c, c, (uint64_t)batch * m, n, s);
   }
-  cudaEvent_t forked = nullptr, joined = nullptr;
-  if (cudaEventCreateWithFlags(&forked, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&joined, cudaEventDisableTiming) != cudaSuccess) {
-    if (forked) cudaEventDestroy(forked);
+  cudaEvent_t ev = nullptr;
+  if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess)
     return cuda_status(cudaGetLastError(), "batch_matmul_softmax: event create");
-  }
   agpu_status st = AGPU_OK;
-  cudaError_t e = cudaEventRecord(forked, s);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(s2, forked, 0);
-  if (e == cudaSuccess) {
-    uint32_t b0 = 0;
-    for (uint32_t i = 0; i < pieces && st == AGPU_OK; ++i) {
-      const uint32_t nb = (uint32_t)((uint64_t)batch * (i + 1) / pieces) - b0;
-      cudaStream_t si = (i % 2) ? s2 : s;
-      const float* ai = a + (uint64_t)b0 * m * k;
-      const float* bi = b + (uint64_t)b0 * k * n;
-      float* ci = c + (uint64_t)b0 * m * n;
-      st = launch_gemm(dev, ai, bi, ci, nb, m, n, k, false, false, si);
-      if (st == AGPU_OK) st = launch_softmax(dev, ci, ci, (uint64_t)nb * m, n, si);
-      b0 += nb;
-    }
-    e = cudaEventRecord(joined, s2);  // join in every case
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, joined, 0);
+  cudaError_t e = cudaSuccess;
+  uint32_t b0 = 0;
+  for (uint32_t i = 0; i < pieces && st == AGPU_OK && e == cudaSuccess; ++i) {
+    const uint32_t nb = (uint32_t)((uint64_t)batch * (i + 1) / pieces) - b0;
+    float* ci = c + (uint64_t)b0 * m * n;
+    st = launch_gemm(dev, a + (uint64_t)b0 * m * k, b + (uint64_t)b0 * k * n, ci, nb, m, n, k,
+                     false, false, s);
+    // each wait takes the event's latest record: this piece's GEMM
+    if (st == AGPU_OK) e = cudaEventRecord(ev, s);
+    if (st == AGPU_OK && e == cudaSuccess) e = cudaStreamWaitEvent(s2, ev, 0);
+    if (st == AGPU_OK && e == cudaSuccess)
+      st = launch_softmax(dev, ci, ci, (uint64_t)nb * m, n, s2);
+    b0 += nb;
   }
-  cudaEventDestroy(forked);
-  cudaEventDestroy(joined);
+  // join in every case, so that nothing on s2 outlives the call's stream order
+  const cudaError_t ej = cudaEventRecord(ev, s2);
+  const cudaError_t ew = ej == cudaSuccess ? cudaStreamWaitEvent(s, ev, 0) : ej;
+  cudaEventDestroy(ev);
+  if (e == cudaSuccess) e = ew;
   if (e != cudaSuccess && st == AGPU_OK) st = cuda_status(e, "batch_matmul_softmax: fork/join");
   return st;
 }

@@ -4,8 +4,9 @@
 Default workload (the headline): fp32 batch_matmul -> row softmax.
   One step = C = batch_matmul(A, B), batch 64, M = K = N = 2048, A, B ~ N(0,1)*0.05
   (seeded), then S = softmax(C) over the last dim (131072 rows x 2048), through
-  the fused entry point agpu_launch_batch_matmul_softmax (the batch in pieces on
-  two streams, each piece's softmax beside the next piece's GEMM).  The GEMM runs
+  the fused entry point agpu_launch_batch_matmul_softmax (the batch in pieces:
+  the GEMMs back to back on one stream, each piece's softmax on a second stream
+  beside the next piece's GEMM).  The GEMM runs
   on tcgen05 tensor cores in TF32 (operands rounded to nearest by TMA) with fp32
   accumulation; softmax is the one-read-one-write warp-per-row kernel.  The GEMM
   alone and the softmax alone are also timed, each in its own loop.
