@@ -128,7 +128,9 @@ AGPU_API agpu_status agpu_batch_matmul(agpu_device* dev, const agpu_buffer* a,
 
 /* batch_matmul followed by a row softmax over the last dim of the result (the
  * batch_matmul + softmax workload), in one call and one output buffer: the
- * softmax runs in place on the product.  Same shape checks as batch_matmul. */
+ * softmax runs in place on the product.  Same shape checks as batch_matmul.
+ * A large batch runs in pieces whose softmaxes overlap the next pieces'
+ * GEMMs (see agpu_launch_batch_matmul_softmax). */
 AGPU_API agpu_status agpu_batch_matmul_softmax(agpu_device* dev, const agpu_buffer* a,
                                                const agpu_buffer* b, uint32_t batch, uint32_t m,
                                                uint32_t n, uint32_t k, agpu_buffer** out);
@@ -378,8 +380,9 @@ AGPU_API agpu_status agpu_launch_batch_matmul(agpu_device* dev, const float* a, 
                                               uint32_t k, void* stream);
 /* Launch-layer agpu_batch_matmul_softmax: out = softmax(A * B) row-wise, on
  * `stream`; the GEMM writes `out` and the softmax runs on it in place.  With
- * a large batch the two halves run on two streams (the first half's softmax
- * beside the second half's GEMM). */
+ * a large batch the pieces' GEMMs run back to back on `stream` and each
+ * piece's softmax on a second stream beside the next GEMM; `stream` waits
+ * for all of it before the call's later work. */
 AGPU_API agpu_status agpu_launch_batch_matmul_softmax(agpu_device* dev, const float* a,
                                                      const float* b, float* out, uint32_t batch,
                                                      uint32_t m, uint32_t n, uint32_t k,
