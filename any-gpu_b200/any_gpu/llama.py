@@ -9,12 +9,15 @@ pointers, one stream); this module only sequences the launches:
     o   = sdpa(q, k, v)          (strided: read straight from qkv, written [B,S,H,Dh])
     x2  = x + o @ Wo             (residual fused in the GEMM epilogue)
     h2  = rmsnorm(x2, w_ffn_norm)
-    gu  = h2 @ Wgu                                      [T, 2F]  gate | up
-    a   = swish(gate) * up                              [T, F]
+    a   = swish(h2 @ Wg) * (h2 @ Wu)                    [T, F]   (SwiGLU)
     y   = x2 + a @ Wd            (residual fused in the GEMM epilogue)
 
-Weights are row-major [in, out] (x @ W).  Attention is non-causal by default
-(the reference's SDPA is non-causal); `causal=True` masks future keys.
+Weights are row-major [in, out] (x @ W).  Wgu [d, 2F] packs Wg and Wu: when
+F % 32 == 0 in 32-column blocks (gate block j = columns [64j, 64j+32), up
+block j = [64j+32, 64j+64)), so that the gate/up GEMM's epilogue writes
+swish(gate) * up directly (gemm_ex act 3); otherwise as [Wg | Wu], with a
+separate swish * up pass.  Attention is non-causal by default (the
+reference's SDPA is non-causal); `causal=True` masks future keys.
 """
 from __future__ import annotations
 
@@ -42,6 +45,11 @@ class LlamaDims:
     def head_dim(self) -> int:
         return self.d_model // self.heads
 
+    @property
+    def fused_swiglu(self) -> bool:
+        """Wgu in interleaved 32-column gate/up blocks, SwiGLU in the GEMM epilogue."""
+        return self.ffn % 32 == 0
+
     def gemm_flops(self) -> float:
         t, d, f = self.tokens, self.d_model, self.ffn
         return 2.0 * t * (4 * d * d + 3 * d * f)
@@ -53,8 +61,8 @@ class LlamaDims:
 
     def workspace_elems(self) -> dict:
         t, d, f = self.tokens, self.d_model, self.ffn
-        return {"h": t * d, "qkv": t * 3 * d, "o": t * d, "x2": t * d, "gu": t * 2 * f,
-                "a": t * f}
+        return {"h": t * d, "qkv": t * 3 * d, "o": t * d, "x2": t * d,
+                "gu": 1 if self.fused_swiglu else t * 2 * f, "a": t * f}
 
 
 def layer_forward(dev, dims: LlamaDims, x, w, ws, y, stream: int = 0) -> None:
@@ -74,7 +82,10 @@ def layer_forward(dev, dims: LlamaDims, x, w, ws, y, stream: int = 0) -> None:
                             dims.causal, stream)
     dev.launch_gemm_ex(ws["o"], w["wo"], ws["x2"], 1, T, d, d, resid_ptr=x, stream=stream)
     dev.launch_rmsnorm(ws["x2"], w["ffn_norm"], ws["h"], T, d, dims.eps, stream)
-    dev.launch_gemm_ex(ws["h"], w["wgu"], ws["gu"], 1, T, 2 * Fd, d, stream=stream)
-    dev.launch_swish_mul(ws["gu"], ws["gu"] + Fd * F32, ws["a"], T, Fd, 2 * Fd, 2 * Fd, Fd,
-                         stream)
+    if dims.fused_swiglu:
+        dev.launch_gemm_ex(ws["h"], w["wgu"], ws["a"], 1, T, 2 * Fd, d, act=3, stream=stream)
+    else:
+        dev.launch_gemm_ex(ws["h"], w["wgu"], ws["gu"], 1, T, 2 * Fd, d, stream=stream)
+        dev.launch_swish_mul(ws["gu"], ws["gu"] + Fd * F32, ws["a"], T, Fd, 2 * Fd, 2 * Fd, Fd,
+                             stream)
     dev.launch_gemm_ex(ws["a"], w["wd"], y, 1, T, d, Fd, resid_ptr=ws["x2"], stream=stream)

@@ -471,12 +471,15 @@ extern "C" agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, cons
   CHECK_LEN(b, (uint64_t)batch * k * n, "gemm_ex", "B");
   if (bias) CHECK_LEN(bias, n, "gemm_ex", "bias");
   if (resid) CHECK_LEN(resid, (uint64_t)batch * m * n, "gemm_ex", "resid");
-  if (act < 0 || act > 2) return fail(AGPU_ERR_INVALID, "gemm_ex: unknown activation %d", act);
+  if (act < 0 || act > 3) return fail(AGPU_ERR_INVALID, "gemm_ex: unknown activation %d", act);
+  if (act == 3 && (n % 64 != 0 || bias || resid))
+    return fail(AGPU_ERR_SHAPE, "gemm_ex: SwiGLU needs n %% 64 == 0 and no bias or residual");
   GemmEpilogue ep;
   ep.bias = bias ? bias->dptr : nullptr;
   ep.resid = resid ? resid->dptr : nullptr;
   ep.act = act;
-  return with_output(dev, (uint64_t)batch * m * n, out, [&](float* c) {
+  const uint64_t cn = act == 3 ? n / 2 : n;
+  return with_output(dev, (uint64_t)batch * m * cn, out, [&](float* c) {
     return launch_gemm_ex(dev, a->dptr, b->dptr, c, batch, m, n, k, trans_a != 0, trans_b != 0,
                           ep, dev->stream);
   });
@@ -848,7 +851,9 @@ agpu_status agpu_launch_gemm_ex(agpu_device* dev, const float* a, const float* b
   CHECK_DEV(dev, "launch_gemm_ex");
   if ((!a || !b || !c) && (uint64_t)batch * m * n)
     return fail(AGPU_ERR_INVALID, "launch_gemm_ex: NULL pointer");
-  if (act < 0 || act > 2) return fail(AGPU_ERR_INVALID, "launch_gemm_ex: unknown activation");
+  if (act < 0 || act > 3) return fail(AGPU_ERR_INVALID, "launch_gemm_ex: unknown activation");
+  if (act == 3 && (n % 64 != 0 || bias || resid))
+    return fail(AGPU_ERR_SHAPE, "launch_gemm_ex: SwiGLU needs n %% 64 == 0 and no bias or residual");
   GemmEpilogue ep;
   ep.bias = bias;
   ep.resid = resid;

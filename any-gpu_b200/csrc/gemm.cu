@@ -106,6 +106,41 @@ struct GemmPolicy {
 
   __device__ bool col_live(const Tile& t, int col0) const { return t.n0 + col0 < N; }
 
+  // SwiGLU epilogue (act 3): B's columns come in 32-column blocks, gate block
+  // j = columns [64j, 64j+32), up block j = [64j+32, 64j+64); C is [M, N/2]
+  // with C[:, 32j + i] = swish(gate) * up.  The pair kernel hands both blocks
+  // of a pair to store_swiglu.
+  __device__ bool paired() const { return act == 3; }
+
+  __device__ void store_swiglu(const Tile& t, int row, int col0, const uint32_t (&g)[32],
+                               const uint32_t (&u)[32], float* stg, int lane) const {
+    float4* srow = reinterpret_cast<float4*>(stg + lane * kEpiStride);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float gv = __uint_as_float(g[4 * j + e]);
+        a[e] = gv / (1.0f + expf(-gv)) * __uint_as_float(u[4 * j + e]);
+      }
+      srow[j] = make_float4(a[0], a[1], a[2], a[3]);
+    }
+    __syncwarp();
+    const int no = N / 2;
+    const int row_base = t.m0 + row - lane;
+    const int col = (t.n0 + col0) / 2 + (lane & 7) * 4;
+    float* Cb = C + (long long)t.b * c_batch;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = i * 4 + (lane >> 3);
+      const int grow = row_base + r;
+      const float4 val = *reinterpret_cast<const float4*>(stg + r * kEpiStride + (lane & 7) * 4);
+      if (grow < M && col < no)
+        *reinterpret_cast<float4*>(Cb + (long long)grow * no + col) = val;
+    }
+    __syncwarp();
+  }
+
   // Thread `lane` holds row (row_base + lane), columns n0+col0 .. +31.  The
   // warp transposes its 32x32 block through shared memory so that each
   // store instruction writes four full 128-byte row segments.
@@ -375,7 +410,7 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   pol.tiles_n = (int)ceil_div(n, BN);
   pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
   pol.C = c;
-  pol.c_batch = (long long)m * n;
+  pol.c_batch = (long long)m * (ep.act == 3 ? n / 2 : n);
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
@@ -591,6 +626,37 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
     return AGPU_OK;
   }
   const agpu_precision p = dev->precision;
+  if (ep.act == 3) {
+    // SwiGLU: fused into the CTA-pair kernel's epilogue when that kernel runs
+    // the GEMM whole; otherwise the plain GEMM into scratch, then swish * up
+    // over the 32-column block pairs (rows of 64: gate 32 | up 32)
+    const bool fused = p == AGPU_PREC_TF32 && !ep.bias && !ep.resid && n % 64 == 0 &&
+                       use_pair(m, n) && gemm_tc_eligible(a, b, c, m, n, k) &&
+                       splitk_slices(dev, batch, m, n, k) == 1;
+    if (fused) {
+      if (use_wide(dev, batch, m, n, k)) {
+        if (!a_trans && !b_trans) return run_tc_pair<512, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+        if (!a_trans && b_trans) return run_tc_pair<512, false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+        if (a_trans && !b_trans) return run_tc_pair<512, true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+        return run_tc_pair<512, true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+      }
+      if (!a_trans && !b_trans) return run_tc_pair<256, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (!a_trans && b_trans) return run_tc_pair<256, false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+      if (a_trans && !b_trans) return run_tc_pair<256, true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+      return run_tc_pair<256, true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    }
+    void* tmp = nullptr;
+    AGPU_TRY(pool_alloc(dev, (size_t)batch * m * n * sizeof(float), &tmp, s));
+    float* t = static_cast<float*>(tmp);
+    GemmEpilogue plain;
+    plain.bias = ep.bias;
+    plain.resid = ep.resid;
+    agpu_status st = launch_gemm_ex(dev, a, b, t, batch, m, n, k, a_trans, b_trans, plain, s);
+    if (st == AGPU_OK)
+      st = launch_swish_mul(dev, t, t + 32, c, (uint64_t)batch * m * n / 64, 32, 64, 64, 32, s);
+    pool_free(dev, tmp, s);
+    return st;
+  }
   const bool tiny = (uint64_t)m * n * k * batch < (1ull << 15);
   const bool vec_ep = (reinterpret_cast<uintptr_t>(ep.bias) |
                        reinterpret_cast<uintptr_t>(ep.resid)) % 16 == 0;

@@ -204,13 +204,26 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
                                                   abort_flag)))
         break;
       ptx::tc_fence_after();
+      const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      if (pol.paired()) {  // SwiGLU: gate and up blocks of 32 columns side by side
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        if (!pol.col_live(tile, c * 32)) break;  // warp-uniform
-        uint32_t v[32];
-        ptx::tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, v);
-        ptx::tmem_wait_ld();
-        pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, false, true);
+        for (int c = 0; c < BN / 32; c += 2) {
+          if (!pol.col_live(tile, c * 32)) break;  // warp-uniform
+          uint32_t g[32], u[32];
+          ptx::tmem_ld32(trow + c * 32, g);
+          ptx::tmem_ld32(trow + (c + 1) * 32, u);
+          ptx::tmem_wait_ld();
+          pol.store_swiglu(tile, q * 32 + lane, c * 32, g, u, stg, lane);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          if (!pol.col_live(tile, c * 32)) break;  // warp-uniform
+          uint32_t v[32];
+          ptx::tmem_ld32(trow + c * 32, v);
+          ptx::tmem_wait_ld();
+          pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, false, true);
+        }
       }
       ptx::tc_fence_before();
       __syncwarp();

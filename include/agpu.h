@@ -149,7 +149,11 @@ AGPU_API agpu_status agpu_gemm(agpu_device* dev, const agpu_buffer* a, const agp
  * 0 = none, 1 = swish, 2 = relu; bias ([n]) and resid ([batch, m, n]) may be
  * NULL.  The bias term is the reference's Linear bias add_per_col
  * (src/ops/tensor_ops.rs:336-352) and swish its activation
- * (src/ops/elementwise.rs:77-89), applied while the tile is in registers. */
+ * (src/ops/elementwise.rs:77-89), applied while the tile is in registers.
+ * act 3 = SwiGLU: B's n columns come in 32-column blocks, gate block j =
+ * columns [64j, 64j+32) and up block j = [64j+32, 64j+64); C is
+ * [batch, m, n/2] with C[.., 32j+i] = swish(gate_i) * up_i; n % 64 == 0 and
+ * no bias or residual, else AGPU_ERR_SHAPE. */
 AGPU_API agpu_status agpu_gemm_ex(agpu_device* dev, const agpu_buffer* a, const agpu_buffer* b,
                                   const agpu_buffer* bias, const agpu_buffer* resid,
                                   uint32_t batch, uint32_t m, uint32_t n, uint32_t k,

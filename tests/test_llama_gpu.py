@@ -71,6 +71,47 @@ def test_gemm_fused_epilogue(dev, orc, prec, tol, act):
     assert orc.rel_fro(got, want) <= tol
 
 
+def _swiglu_blocks(c, m, n):
+    """swish(gate) * up over 32-column block pairs: gate j = [64j, 64j+32),
+    up j = [64j+32, 64j+64) -> [m, n/2]."""
+    blk = np.asarray(c, np.float64).reshape(m, n // 64, 2, 32)
+    g, u = blk[:, :, 0], blk[:, :, 1]
+    return (g / (1 + np.exp(-g)) * u).reshape(-1)
+
+
+@pytest.mark.parametrize("prec,tol", [("tf32", 1e-3), ("tf32x3", 1e-5), ("ffma", 1e-5)])
+@pytest.mark.parametrize("batch,m,n,k", [(1, 2048, 2048, 256),   # fused in the pair kernel
+                                         (1, 1024, 5120, 384),   # fused, 256x512 tiles
+                                         (2, 300, 640, 96),      # GEMM, then swish * up
+                                         (1, 64, 128, 40)])      # small: SIMT, then swish * up
+def test_gemm_swiglu_epilogue(dev, orc, prec, tol, batch, m, n, k):
+    """act 3 (SwiGLU): the LLaMA gate/up projection writes swish(gate) * up
+    directly, from B's interleaved 32-column gate / up blocks."""
+    r = np.random.default_rng(m + n)
+    a = (r.standard_normal(batch * m * k) * 0.5).astype(np.float32)
+    b = (r.standard_normal(batch * k * n) * 0.1).astype(np.float32)
+    dev.set_precision(prec)
+    try:
+        got = dev.read(dev.gemm_ex(dev.upload(a), dev.upload(b), batch, m, n, k, act=3))
+    finally:
+        dev.set_precision("tf32")
+    assert got.size == batch * m * n // 2
+    prods = [orc.matmul(a[i * m * k:(i + 1) * m * k], b[i * k * n:(i + 1) * k * n], m, n, k,
+                        threads=True) for i in range(batch)]
+    want = np.concatenate([_swiglu_blocks(c, m, n) for c in prods])
+    assert orc.rel_fro(got, want) <= tol
+
+
+def test_gemm_swiglu_errors(dev):
+    from any_gpu import AnyGpuError
+    up = lambda k: dev.upload(np.ones(k, np.float32))
+    for call in (lambda: dev.gemm_ex(up(4 * 8), up(8 * 96), 1, 4, 96, 8, act=3),  # n % 64
+                 lambda: dev.gemm_ex(up(4 * 8), up(8 * 64), 1, 4, 64, 8, bias=up(64), act=3)):
+        with pytest.raises(AnyGpuError) as e:
+            call()
+        assert e.value.status == 1
+
+
 def test_sdpa_strided_packed_qkv(dev, orc):
     """Q, K, V read in place from a packed [B, S, 3, H, D] projection, output
     written as [B, S, H, D] (the layer's layout) -- tensor-core and SIMT paths."""
@@ -106,20 +147,24 @@ def _layer_oracle(orc, x, w, dims):
     x2 = orc.elementwise("add", x, orc.matmul(o, w["wo"], T, d, d, threads=True))
     h2 = orc.rmsnorm(x2, w["ffn_norm"], T, d, dims.eps)
     gu = orc.matmul(h2, w["wgu"], T, 2 * Fd, d, threads=True).reshape(T, 2 * Fd)
-    a = orc.elementwise("mul", orc.elementwise("swish", np.ascontiguousarray(gu[:, :Fd])),
-                        np.ascontiguousarray(gu[:, Fd:]))
+    if dims.fused_swiglu:  # Wgu in interleaved 32-column gate / up blocks
+        a = _swiglu_blocks(gu, T, 2 * Fd).astype(np.float32)
+    else:
+        a = orc.elementwise("mul", orc.elementwise("swish", np.ascontiguousarray(gu[:, :Fd])),
+                            np.ascontiguousarray(gu[:, Fd:]))
     return orc.elementwise("add", x2, orc.matmul(a, w["wd"], T, d, Fd, threads=True))
 
 
+@pytest.mark.parametrize("ffn", [344, 352])  # [Wg | Wu] halves; interleaved blocks, fused
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("prec,tol", [("tf32", 2e-3), ("tf32x3", 1e-5)])
-def test_llama_layer_small(dev, orc, prec, tol, causal):
+def test_llama_layer_small(dev, orc, prec, tol, causal, ffn):
     """The LLaMA-style layer of the benchmark configs at a small size (B2, S128,
     d256, H2 x 128, FFN 344; weights N(0, 0.02), x N(0,1)) against the layer
     restated with the oracle.  TF32: the layer chains five TF32 contractions,
     so its bound is 2e-3; 3xTF32 (attention on the exact kernel) stays at 1e-5."""
     from any_gpu.llama import LlamaDims, layer_forward
-    dims = LlamaDims(batch=2, seq=128, d_model=256, heads=2, ffn=344, causal=causal)
+    dims = LlamaDims(batch=2, seq=128, d_model=256, heads=2, ffn=ffn, causal=causal)
     d, Fd, T = dims.d_model, dims.ffn, dims.tokens
     r = np.random.default_rng(1238)
     w = {"attn_norm": (1 + 0.1 * r.standard_normal(d)).astype(np.float32),
