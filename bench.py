@@ -198,6 +198,41 @@ class Workload:
     def cpu_sample(self, orc, target_s, threads=True):
         raise NotImplementedError
 
+    def _pipelined(self, dev, chunked, shared, chunks, launch):
+        """One e2e step with its PCIe transfers pipelined over the async API:
+        `shared` host inputs go up whole first; per chunk i the `chunked`
+        inputs' i-th slices go up on an upload stream, `launch(i, ptrs,
+        stream)` runs on a compute stream once they are there, and the
+        output's i-th slice comes down on a download stream."""
+        import torch
+        if not hasattr(self, "_pipe"):
+            bufs = {k: dev.alloc(self.host[k].numel()) for k in list(chunked) + list(shared)}
+            bufs["_out"] = dev.alloc(self.out_elems())
+            dev.synchronize()  # the zero fills finish before other streams write
+            self._pipe = (bufs, [torch.cuda.Stream() for _ in range(3)])
+        bufs, (up, comp, down) = self._pipe
+        ptrs = {k: b.device_ptr for k, b in bufs.items()}
+        for k in shared:
+            n = self.host[k].numel()
+            dev.write_async(bufs[k], self.host[k].data_ptr(), n, 0, up.cuda_stream)
+        per_out = self.out_elems() // chunks
+        for i in range(chunks):
+            for k in chunked:
+                n = self.host[k].numel() // chunks
+                dev.write_async(bufs[k], self.host[k].data_ptr() + 4 * i * n, n, i * n,
+                                up.cuda_stream)
+            e_up = torch.cuda.Event()
+            e_up.record(up)
+            comp.wait_event(e_up)
+            launch(i, ptrs, comp.cuda_stream)
+            e_c = torch.cuda.Event()
+            e_c.record(comp)
+            down.wait_event(e_c)
+            dev.read_async(bufs["_out"], self.out_host.data_ptr() + 4 * i * per_out, per_out,
+                           i * per_out, down.cuda_stream)
+        down.synchronize()
+        dev.synchronize()  # surfaces an expired device-side wait, if any
+
     def extra(self, ms_step, ms_dom, peaks, aux_ms=None) -> dict:
         return {}
 
@@ -435,6 +470,20 @@ class Sdpa(Workload):
         for b in g + [go]:
             b.free()
 
+    def e2e_pipelined(self, dev):
+        chunks = next(c for c in (8, 4, 2, 1) if self.bh % c == 0)
+        per = self.bh // chunks
+        hsz = self.s * self.d
+        self.e2e_how = (f"batch*heads split in {chunks} chunks; per chunk agpu_write_async of "
+                        "Q, K, V on an upload stream, attention (launch layer) on a compute "
+                        "stream, agpu_read_async of O on a download stream")
+
+        def launch(i, p, st):
+            off = 4 * i * per * hsz
+            dev.launch_sdpa(p["q"] + off, p["k"] + off, p["v"] + off, p["_out"] + off, per,
+                            self.s, self.d, False, st)
+        self._pipelined(dev, ["q", "k", "v"], [], chunks, launch)
+
     def cpu_sample(self, orc, target_s, threads=True):
         r = np.random.default_rng(1236)
         hsz = self.s * self.d
@@ -517,6 +566,22 @@ class Unet(Workload):
         dev.read(y, out=self.out_host.numpy())
         for b in list(g.values()) + [y]:
             b.free()
+
+    def e2e_pipelined(self, dev):
+        chunks = next(c for c in (4, 2, 1) if self.n % c == 0)
+        per = self.n // chunks
+        img = self.c * self.h * self.w
+        self.e2e_how = (f"images split in {chunks} chunks; the weights, then per chunk the "
+                        "images, up by agpu_write_async on an upload stream, the fused conv2d "
+                        "-> group_norm -> swish (launch layer) on a compute stream, "
+                        "agpu_read_async of the output on a download stream")
+
+        def launch(i, p, st):
+            off = 4 * i * per * img
+            dev.launch_conv2d_group_norm_swish(
+                p["x"] + off, p["w"], 0, p["_out"] + off, per, self.c, self.h, self.w, self.c,
+                3, 3, 1, 1, 1, 1, 1, 1, 1, p["gamma"], p["beta"], self.g, 1e-5, st)
+        self._pipelined(dev, ["x"], ["w", "gamma", "beta"], chunks, launch)
 
     def cpu_sample(self, orc, target_s, threads=True):
         x, w, gamma, beta = self.host_inputs().values()
