@@ -119,6 +119,46 @@ def test_gemm_split_k_cluster(dev, orc, ta, tb, batch, m, n, k):
     np.testing.assert_array_equal(got, again)  # fixed summation order
 
 
+_CHUNK_CASES = [(1, 512, 1024, 768, True, False),   # split-K, MN-major A and B
+                 (2, 1024, 2048, 512, True, False),  # pair kernel, MN-major A and B
+                 (1, 2048, 2048, 256, False, False)]  # pair kernel, MN-major B
+
+
+def _chunk_case_inputs(batch, m, n, k):
+    r = np.random.default_rng(m + 3 * n + 7 * k)
+    return (r.uniform(-1, 1, batch * m * k).astype(np.float32),
+            r.uniform(-1, 1, batch * k * n).astype(np.float32))
+
+
+def test_gemm_chunked_operand_maps_bit_identical(dev, tmp_path):
+    """MN-major operands with MN % 32 == 0 load through one 4-D TMA box per
+    stage; the shared-memory image, hence every output bit, equals the one
+    the per-32-column loads give (AGPU_GEMM_CHUNKED=0, in a child process)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{os.path.join(root, 'any-gpu_b200')!r}, {root!r}]\n"
+        "from tests.test_parity_gpu import _CHUNK_CASES, _chunk_case_inputs\n"
+        "from any_gpu import GpuDevice\n"
+        "d = GpuDevice.gpu(0)\n"
+        "for i, (batch, m, n, k, ta, tb) in enumerate(_CHUNK_CASES):\n"
+        "    a, b = _chunk_case_inputs(batch, m, n, k)\n"
+        "    got = d.read(d.gemm(d.upload(a), d.upload(b), batch, m, n, k, ta, tb))\n"
+        f"    np.save({str(tmp_path)!r} + f'/c{{i}}.npy', got)\n"
+        "d.close()\n")
+    env = dict(os.environ, AGPU_GEMM_CHUNKED="0")
+    out = subprocess.run([sys.executable, "-c", script], env=env, capture_output=True,
+                         text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    for i, (batch, m, n, k, ta, tb) in enumerate(_CHUNK_CASES):
+        a, b = _chunk_case_inputs(batch, m, n, k)
+        got = dev.read(dev.gemm(dev.upload(a), dev.upload(b), batch, m, n, k, ta, tb))
+        np.testing.assert_array_equal(got, np.load(tmp_path / f"c{i}.npy"))
+
+
 @pytest.mark.parametrize("act", [0, 1, 2])
 def test_gemm_split_k_epilogue(dev, orc, act):
     """bias + residual + activation applied once, after the K-slice sum."""
