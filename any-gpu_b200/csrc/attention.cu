@@ -758,22 +758,32 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
       if (!ok) return;
       int q0, head, bat;
       tiles.get(t, CAUSAL, q0, head, bat);
-      const int qrow = q0 + rank * QT + row;
-      const float* qr = qin.p + (long long)bat * qin.b + (long long)head * qin.h +
-                        (long long)qrow * qin.s + h * HD;
+      // 16 rows x 32 columns per store in the 16x256b shape: four lanes
+      // read 32 contiguous bytes of a row (a thread per row would touch 32
+      // lines per load instruction)
+      const int row0 = q0 + rank * QT + q * 32;
+      const float* qh = qin.p + (long long)bat * qin.b + (long long)head * qin.h + h * HD +
+                        2 * (lane & 3);
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t r[32];
+      for (int u = 0; u < 2; ++u) {
+        const int r0 = row0 + 16 * u + (lane >> 2), r1 = r0 + 8;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (qrow < S) f = __ldg(reinterpret_cast<const float4*>(qr + c * 32) + k);
-          r[4 * k] = round_tf32(f.x * scale_log2);
-          r[4 * k + 1] = round_tf32(f.y * scale_log2);
-          r[4 * k + 2] = round_tf32(f.z * scale_log2);
-          r[4 * k + 3] = round_tf32(f.w * scale_log2);
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t r[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int col = c * 32 + 8 * j;
+            float2 f0 = make_float2(0.f, 0.f), f1 = f0;
+            if (r0 < S) f0 = __ldg(reinterpret_cast<const float2*>(qh + (long long)r0 * qin.s + col));
+            if (r1 < S) f1 = __ldg(reinterpret_cast<const float2*>(qh + (long long)r1 * qin.s + col));
+            r[4 * j] = round_tf32(f0.x * scale_log2);
+            r[4 * j + 1] = round_tf32(f0.y * scale_log2);
+            r[4 * j + 2] = round_tf32(f1.x * scale_log2);
+            r[4 * j + 3] = round_tf32(f1.y * scale_log2);
+          }
+          ptx::tmem_st_16x256b_x4(
+              tmem + ((uint32_t)(q * 32 + 16 * u) << 16) + C::Q_COL + h * HD + c * 32, r);
         }
-        ptx::tmem_st32(tmem + lane_off + C::Q_COL + h * HD + c * 32, r);
       }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
@@ -885,21 +895,37 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
       if (ok) {
         ptx::tc_fence_after();
         const float inv = 1.0f / l;
-        float* orow = out + (long long)bat * ol.b + (long long)head * ol.h +
-                      (long long)qrow * ol.s + h * HD;
+        // 16 rows per pass in the 16x256b shape (whole 32-byte sectors per
+        // store), each row scaled by its own 1 / l, fetched from the lane
+        // that owns the row
+        const int row0 = q0 + rank * QT + q * 32;
+        float* oh = out + (long long)bat * ol.b + (long long)head * ol.h + h * HD + 2 * (lane & 3);
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t o[32];
-          ptx::tmem_ld32(tmem + lane_off + C::O_COL + h * HD + c * 32, o);
-          ptx::tmem_wait_ld();
-          if (qrow < S) {
+        for (int u = 0; u < 2; ++u) {
+          const int src = 16 * u + (lane >> 2);
+          const float i0 = __shfl_sync(0xffffffffu, inv, src);
+          const float i1 = __shfl_sync(0xffffffffu, inv, src + 8);
+          const int r0 = row0 + src, r1 = r0 + 8;
+          uint32_t o[HD / 32][16];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              __stcs(reinterpret_cast<float4*>(orow + c * 32) + k,
-                     make_float4(__uint_as_float(o[4 * k]) * inv,
-                                 __uint_as_float(o[4 * k + 1]) * inv,
-                                 __uint_as_float(o[4 * k + 2]) * inv,
-                                 __uint_as_float(o[4 * k + 3]) * inv));
+          for (int c = 0; c < HD / 32; ++c)
+            ptx::tmem_ld_16x256b_x4(
+                tmem + ((uint32_t)(q * 32 + 16 * u) << 16) + C::O_COL + h * HD + c * 32, o[c]);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = c * 32 + 8 * j;
+              if (r0 < S)
+                __stcs(reinterpret_cast<float2*>(oh + (long long)r0 * ol.s + col),
+                       make_float2(__uint_as_float(o[c][4 * j]) * i0,
+                                   __uint_as_float(o[c][4 * j + 1]) * i0));
+              if (r1 < S)
+                __stcs(reinterpret_cast<float2*>(oh + (long long)r1 * ol.s + col),
+                       make_float2(__uint_as_float(o[c][4 * j + 2]) * i1,
+                                   __uint_as_float(o[c][4 * j + 3]) * i1));
+            }
           }
         }
         ptx::tc_fence_before();
