@@ -64,6 +64,9 @@ struct GemmPolicy {
   const float* bias;   // [N] or null (Linear bias, the reference's add_per_col)
   const float* resid;  // [batch, M, N] or null (residual add)
   int act;             // 0 none, 1 swish, 2 relu
+  // MN-major operand loaded through the 4-D chunked view, one TMA box per
+  // stage (else one box per 32-column chunk)
+  bool a_chunked = false, b_chunked = false;
 
   struct Tile { int b, m0, n0; };
 
@@ -90,6 +93,8 @@ struct GemmPolicy {
     const int k0 = kb * BK;
     if (!A_MN) {
       ptx::tma_load_3d(sa, ta, bar, k0, t.m0, t.b);
+    } else if (a_chunked) {
+      ptx::tma_load_4d(sa, ta, bar, 0, k0, t.m0 / 32, t.b);
     } else {
 #pragma unroll
       for (int j = 0; j < BM / 32; ++j)
@@ -97,6 +102,8 @@ struct GemmPolicy {
     }
     if (!B_MN) {
       ptx::tma_load_3d(sb, tb, bar, k0, t.n0, t.b);
+    } else if (b_chunked) {
+      ptx::tma_load_4d(sb, tb, bar, 0, k0, t.n0 / 32, t.b);
     } else {
 #pragma unroll
       for (int j = 0; j < BN / 32; ++j)
@@ -198,8 +205,6 @@ struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
   using Cfg = umma::PairCfg<BN_>;
   static constexpr int PM = 2 * BM;  // tile rows of the pair
   static constexpr int HALF = Cfg::MMA_N / 2;  // B columns per CTA per sub-block
-  bool a_chunked = false;  // MN-major A through one 4-D box per stage
-  bool b_chunked = false;  // MN-major B through one 4-D box per sub-block
 
   __device__ Tile tile(long long t) const {
     const long long per_batch = (long long)this->tiles_m * this->tiles_n;
@@ -228,7 +233,7 @@ struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
     const int m = t.m0 + BM * rank;
     if (!A_MN_) {
       ptx::tma_load_3d_pair(sa, ta, lbar, k0, m, t.b);
-    } else if (a_chunked) {
+    } else if (this->a_chunked) {
       ptx::tma_load_4d_pair(sa, ta, lbar, 0, k0, m / 32, t.b);
     } else {
 #pragma unroll
@@ -240,7 +245,7 @@ struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
       const int n = t.n0 + sub * Cfg::MMA_N + HALF * rank;
       if (!B_MN_) {
         ptx::tma_load_3d_pair(sb + sub * HALF * 128, tb, lbar, k0, n, t.b);
-      } else if (b_chunked) {
+      } else if (this->b_chunked) {
         ptx::tma_load_4d_pair(sb + sub * (HALF / 32) * BK * 128, tb, lbar, 0, k0, n / 32, t.b);
       } else {
 #pragma unroll
@@ -362,6 +367,63 @@ agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner
   return AGPU_OK;
 }
 
+// 4-D fp32 view {32, K, MN/32, batch} of an MN-major operand stored
+// [batch][K][MN] with MN % 32 == 0: the third dimension steps 32-element
+// chunks (128 bytes), so one box {32, BK, chunks, 1} lands as `chunks`
+// consecutive BK x 128-byte MN-major swizzle atoms -- the same shared-memory
+// image as `chunks` boxes of the 3-D view, from one TMA instruction.
+static agpu_status make_tmap_f32_chunked(CUtensorMap* map, const float* base, uint64_t mn,
+                                         uint64_t k, uint64_t batch, uint32_t chunks,
+                                         bool round_tf32) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[4] = {32, k, mn / 32, batch};
+  cuuint64_t strides[3] = {mn * 4, 128, k * mn * 4};
+  cuuint32_t box[4] = {32, BK, chunks, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      round_tf32 ? CU_TENSOR_MAP_DATA_TYPE_TFLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = fn(map, dt, 4, const_cast<float*>(base), dims,
+                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled (chunked) failed (%d) mn=%llu k=%llu",
+                (int)r, (unsigned long long)mn, (unsigned long long)k);
+  return AGPU_OK;
+}
+
+// Tensor maps of both operands of the tensor-core GEMMs; `b_box` = B rows
+// (K-major) or columns (MN-major) one CTA stages per stage.  MN-major
+// operands whose MN extent is a multiple of 32 take the chunked view (one
+// TMA instruction per operand per stage instead of one per 32 columns);
+// AGPU_GEMM_CHUNKED=0 keeps the per-chunk loads.  `round` = TFLOAT32 maps
+// (round to nearest on the way in); 3xTF32 splits exact FLOAT32 operands.
+template <class P>
+static agpu_status make_gemm_maps(CUtensorMap* ta, CUtensorMap* tb, P* pol, const float* a,
+                                  const float* b, uint32_t batch, uint32_t m, uint32_t n,
+                                  uint32_t k, uint32_t b_box, bool round) {
+  static const bool chunk_ok = [] {
+    const char* e = getenv("AGPU_GEMM_CHUNKED");
+    return !(e && e[0] == '0');
+  }();
+  pol->a_chunked = P::A_MN && chunk_ok && m % 32 == 0;
+  pol->b_chunked = P::B_MN && chunk_ok && n % 32 == 0;
+  if (!P::A_MN)
+    AGPU_TRY(make_tmap_f32_3d(ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, round));
+  else if (pol->a_chunked)
+    AGPU_TRY(make_tmap_f32_chunked(ta, a, m, k, batch, BM / 32, round));
+  else
+    AGPU_TRY(make_tmap_f32_3d(ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, round));
+  if (!P::B_MN)
+    AGPU_TRY(make_tmap_f32_3d(tb, b, k, n, batch, (uint64_t)k * n, BK, b_box, false, round));
+  else if (pol->b_chunked)
+    AGPU_TRY(make_tmap_f32_chunked(tb, b, n, k, batch, b_box / 32, round));
+  else
+    AGPU_TRY(make_tmap_f32_3d(tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, round));
+  return AGPU_OK;
+}
+
 template <int BN, bool A_MN, bool B_MN, bool X3>
 static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, float* c,
                           uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
@@ -369,17 +431,10 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   using P = GemmPolicy<BN, A_MN, B_MN>;
   using Cfg = umma::Cfg<BN, X3>;
   CUtensorMap ta, tb;
-  // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
-  if (!A_MN)
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, !X3));
-  else
-    AGPU_TRY(make_tmap_f32_3d(&ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, !X3));
-  // B: MN-major stored [K,N] -> dims {N, K}; K-major stored [N,K] -> dims {K, N}.
-  if (B_MN)
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, !X3));
-  else
-    AGPU_TRY(make_tmap_f32_3d(&tb, b, k, n, batch, (uint64_t)k * n, BK, BN, false, !X3));
   P pol;
+  // A: K-major stored [M,K] -> dims {K, M}; MN-major stored [K,M] -> dims {M, K}.
+  // B: MN-major stored [K,N] -> dims {N, K}; K-major stored [N,K] -> dims {K, N}.
+  AGPU_TRY(make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, BN, !X3));
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, BM);
   pol.tiles_n = (int)ceil_div(n, BN);
@@ -396,58 +451,6 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   return after_launch(dev, "gemm_tf32 (umma_tf32_kernel)");
 }
 
-// 4-D fp32 view {32, K, MN/32, batch} of an MN-major operand stored
-// [batch][K][MN] with MN % 32 == 0: the third dimension steps 32-element
-// chunks (128 bytes), so one box {32, BK, chunks, 1} lands as `chunks`
-// consecutive BK x 128-byte MN-major swizzle atoms -- the same shared-memory
-// image as `chunks` boxes of the 3-D view, from one TMA instruction.
-static agpu_status make_tmap_f32_chunked(CUtensorMap* map, const float* base, uint64_t mn,
-                                         uint64_t k, uint64_t batch, uint32_t chunks) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[4] = {32, k, mn / 32, batch};
-  cuuint64_t strides[3] = {mn * 4, 128, k * mn * 4};
-  cuuint32_t box[4] = {32, BK, chunks, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 4, const_cast<float*>(base), dims,
-                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(AGPU_ERR_CUDA, "cuTensorMapEncodeTiled (chunked) failed (%d) mn=%llu k=%llu",
-                (int)r, (unsigned long long)mn, (unsigned long long)k);
-  return AGPU_OK;
-}
-
-// Tensor maps of both operands of the CTA-pair kernels.  MN-major operands
-// whose MN extent is a multiple of 32 take the chunked view (one TMA
-// instruction per operand per stage instead of one per 32 columns);
-// AGPU_GEMM_CHUNKED=0 keeps the per-chunk loads.
-template <class P>
-static agpu_status make_pair_maps(CUtensorMap* ta, CUtensorMap* tb, P* pol, const float* a,
-                                  const float* b, uint32_t batch, uint32_t m, uint32_t n,
-                                  uint32_t k) {
-  static const bool chunk_ok = [] {
-    const char* e = getenv("AGPU_GEMM_CHUNKED");
-    return !(e && e[0] == '0');
-  }();
-  pol->a_chunked = P::A_MN && chunk_ok && m % 32 == 0;
-  pol->b_chunked = P::B_MN && chunk_ok && n % 32 == 0;
-  if (!P::A_MN)
-    AGPU_TRY(make_tmap_f32_3d(ta, a, k, m, batch, (uint64_t)m * k, BK, BM, false, true));
-  else if (pol->a_chunked)
-    AGPU_TRY(make_tmap_f32_chunked(ta, a, m, k, batch, BM / 32));
-  else
-    AGPU_TRY(make_tmap_f32_3d(ta, a, m, k, batch, (uint64_t)m * k, 32, BK, true, true));
-  if (!P::B_MN)
-    AGPU_TRY(make_tmap_f32_3d(tb, b, k, n, batch, (uint64_t)k * n, BK, P::HALF, false, true));
-  else if (pol->b_chunked)
-    AGPU_TRY(make_tmap_f32_chunked(tb, b, n, k, batch, P::HALF / 32));
-  else
-    AGPU_TRY(make_tmap_f32_3d(tb, b, n, k, batch, (uint64_t)k * n, 32, BK, true, true));
-  return AGPU_OK;
-}
-
 template <int BN, bool A_MN, bool B_MN>
 static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
@@ -455,7 +458,7 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   using P = GemmPairPolicy<BN, A_MN, B_MN>;
   CUtensorMap ta, tb;
   P pol;
-  AGPU_TRY(make_pair_maps(&ta, &tb, &pol, a, b, batch, m, n, k));
+  AGPU_TRY(make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, P::HALF, true));
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, P::PM);
   pol.tiles_n = (int)ceil_div(n, BN);
@@ -478,7 +481,7 @@ static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const fl
   using Cfg = umma::PairCfg<256>;
   CUtensorMap ta, tb;
   P pol;
-  AGPU_TRY(make_pair_maps(&ta, &tb, &pol, a, b, batch, m, n, k));
+  AGPU_TRY(make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, P::HALF, true));
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, P::PM);
   pol.tiles_n = (int)ceil_div(n, 256);

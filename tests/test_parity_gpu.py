@@ -119,9 +119,11 @@ def test_gemm_split_k_cluster(dev, orc, ta, tb, batch, m, n, k):
     np.testing.assert_array_equal(got, again)  # fixed summation order
 
 
-_CHUNK_CASES = [(1, 512, 1024, 768, True, False),   # split-K, MN-major A and B
-                 (2, 1024, 2048, 512, True, False),  # pair kernel, MN-major A and B
-                 (1, 2048, 2048, 256, False, False)]  # pair kernel, MN-major B
+_CHUNK_CASES = [(1, 512, 1024, 768, True, False, "tf32"),    # split-K, MN-major A and B
+                 (2, 1024, 2048, 512, True, False, "tf32"),   # pair kernel, MN-major A and B
+                 (1, 2048, 2048, 256, False, False, "tf32"),  # pair kernel, MN-major B
+                 (2, 128, 1024, 384, True, False, "tf32"),    # single-CTA kernel (m < 256)
+                 (1, 384, 512, 256, True, False, "tf32x3")]   # single-CTA 3xTF32 (exact maps)
 
 
 def _chunk_case_inputs(batch, m, n, k):
@@ -144,8 +146,9 @@ def test_gemm_chunked_operand_maps_bit_identical(dev, tmp_path):
         "from tests.test_parity_gpu import _CHUNK_CASES, _chunk_case_inputs\n"
         "from any_gpu import GpuDevice\n"
         "d = GpuDevice.gpu(0)\n"
-        "for i, (batch, m, n, k, ta, tb) in enumerate(_CHUNK_CASES):\n"
+        "for i, (batch, m, n, k, ta, tb, prec) in enumerate(_CHUNK_CASES):\n"
         "    a, b = _chunk_case_inputs(batch, m, n, k)\n"
+        "    d.set_precision(prec)\n"
         "    got = d.read(d.gemm(d.upload(a), d.upload(b), batch, m, n, k, ta, tb))\n"
         f"    np.save({str(tmp_path)!r} + f'/c{{i}}.npy', got)\n"
         "d.close()\n")
@@ -153,9 +156,13 @@ def test_gemm_chunked_operand_maps_bit_identical(dev, tmp_path):
     out = subprocess.run([sys.executable, "-c", script], env=env, capture_output=True,
                          text=True, timeout=300)
     assert out.returncode == 0, out.stderr[-2000:]
-    for i, (batch, m, n, k, ta, tb) in enumerate(_CHUNK_CASES):
+    for i, (batch, m, n, k, ta, tb, prec) in enumerate(_CHUNK_CASES):
         a, b = _chunk_case_inputs(batch, m, n, k)
-        got = dev.read(dev.gemm(dev.upload(a), dev.upload(b), batch, m, n, k, ta, tb))
+        dev.set_precision(prec)
+        try:
+            got = dev.read(dev.gemm(dev.upload(a), dev.upload(b), batch, m, n, k, ta, tb))
+        finally:
+            dev.set_precision("tf32")
         np.testing.assert_array_equal(got, np.load(tmp_path / f"c{i}.npy"))
 
 
