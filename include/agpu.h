@@ -20,6 +20,19 @@
  * order; `agpu_read` and `agpu_synchronize` block until the stream drains.
  * Inputs are only read; outputs never alias inputs.
  * All element counts are 64-bit, so no `u32` wraparound at BH*S*S >= 2^32.
+ *
+ * Kernel-choice switches, read once per process from the environment (all
+ * on by default; results stay within the documented tolerances either way):
+ *   AGPU_GEMM_PAIR=0      TF32 GEMMs on single-CTA 128-row tiles, not CTA pairs
+ *   AGPU_GEMM_SPLITK=0    no cluster split-K for GEMMs with few tiles
+ *   AGPU_GEMM_WIDE=0|2    never / always 256 x 512 pair tiles (default: estimate)
+ *   AGPU_GEMM_CHUNKED=0   MN-major operands by one TMA box per 32 columns
+ *                         (bit-identical output)
+ *   AGPU_SDPA_PAIR=0      attention on single CTAs for every sequence length
+ *   AGPU_CONV_WIDE=0      conv2d on 256 x 160 tiles instead of 256 x 320
+ *   AGPU_CONV_OVERLAP=0   conv2d staging and conv in one stream (no halves)
+ *   AGPU_BMM_SOFTMAX_PIECES=N  at most N pieces (1, 2, 4, 8) in the fused
+ *                         batch_matmul + softmax pipeline
  */
 #ifndef AGPU_H
 #define AGPU_H
