@@ -562,14 +562,16 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
   const bool leader = rank == 0;
   const long long cluster_id = blockIdx.x / 2, n_clusters = gridDim.x / 2;
   auto lead = [&](uint64_t* bar) { return ptx::mapa(ptx::smem_u32(bar), 0); };
-  // One arrive per warp on a leader barrier, after every lane's prior work:
-  // a CTA-scope arrive in the leader, a cluster-scope release in the peer (a
-  // release per thread showed up as membar stalls).
+  // One arrive per warp on a leader barrier, after every lane's prior work.
+  // Everything these barriers hand over (Q, P, the drained O) is tensor
+  // memory, ordered by tcgen05.wait + the tcgen05 fence pair, so the peer's
+  // remote arrive keeps the default CTA-scope release (a cluster-scope
+  // release cost ~1.4k cycles per warp and key block).
   auto warp_arrive = [&](uint64_t* bar) {
     __syncwarp();
     if (lane == 0) {
       if (leader) ptx::mbar_arrive(bar);
-      else ptx::mbar_arrive_cluster(lead(bar));
+      else ptx::mbar_arrive_remote(lead(bar));
     }
   };
   auto load = [&](void* dst, const CUtensorMap* m, uint32_t bar, int d0, int s0, int head,

@@ -225,11 +225,13 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
           pol.store(tile, q * 32 + lane, c * 32, v, stg, lane, false, true);
         }
       }
+      // the accumulator (tensor memory) is free again; the handoff carries
+      // no generic-memory data, so the peer's remote arrive is CTA-scope
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         if (leader) ptx::mbar_arrive(&tempty[acc]);
-        else ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(&tempty[acc]), 0));
+        else ptx::mbar_arrive_remote(ptx::mapa(ptx::smem_u32(&tempty[acc]), 0));
       }
     }
   }
