@@ -81,8 +81,10 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 
 // try_wait with cluster-scope acquire: for barriers that threads of the
-// other CTA of a pair arrive on (release.cluster), so their writes before the
-// arrive are visible after the wait.
+// other CTA of a pair arrive on.  (Those arrives are CTA-scope releases over
+// tensor-memory handoffs, which the tcgen05 fence pair orders; the acquire
+// costs the waiter little and keeps generic-memory writes before a
+// cluster-scope arrive visible too.)
 __device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
