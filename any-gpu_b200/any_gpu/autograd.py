@@ -18,6 +18,11 @@ the library's kernels; the backward rules are the reference's
 * MseLoss: 2 (pred - target) / n, the upstream gradient not applied, as in
   the reference (:368-374, the loss is the tape's last node).
 
+One fused op has no reference counterpart: `linear` records matmul + bias +
+ReLU as a single op whose forward is one GEMM with the bias and activation
+in its epilogue, and whose backward is the ReLU mask, the two GEMMs and the
+bias's `sum_rows`.
+
 Gradients are accumulated with `add` into a fresh buffer (:267-279); the
 pass-through gradients of Add, Sub and the broadcast adds share the upstream
 buffer instead of copying it (buffers are never written after creation).
@@ -157,6 +162,21 @@ class Tape:
         out = self.dev.add_per_col(self.buf(a), self.buf(b), rows, cols)
         return self._push(out, "add_per_col", a=a, b=b, rows=rows, cols=cols)
 
+    def linear(self, x, w, bias, m: int, n: int, k: int, act: str = "none"):
+        """act(x @ w + bias[col]) as ONE recorded op and one launch: the bias
+        and the activation run in the GEMM's epilogue (`agpu_gemm_ex`).  No
+        reference counterpart: it records what `matmul` -> `add_per_col` ->
+        `relu` record as three ops (three launches, two [m, n] intermediates)
+        and has the same gradients.  `bias` may be None; `act` is "none" or
+        "relu" (the ReLU mask is read from the output, so no pre-activation
+        is kept)."""
+        codes = {"none": 0, "relu": 2}
+        if act not in codes:
+            raise ValueError(f"linear: act must be one of {sorted(codes)}, got {act!r}")
+        out = self.dev.gemm_ex(self.buf(x), self.buf(w), 1, m, n, k,
+                               bias=None if bias is None else self.buf(bias), act=codes[act])
+        return self._push(out, "linear", a=x, b=w, bias=bias, m=m, n=n, k=k, act=act)
+
     # ----------------------------------------------------------- backward --
     def backward(self, loss: TensorId) -> None:
         """Gradients of every recorded tensor w.r.t. the 1-element `loss`
@@ -228,6 +248,14 @@ class Tape:
             elif e.op == "add_per_col":
                 self._accum(a["a"], g)
                 self._accum(a["b"], d.sum_rows(g, a["rows"], a["cols"]))
+            elif e.op == "linear":
+                m, n, k = a["m"], a["n"], a["k"]
+                if a["act"] == "relu":  # out > 0 exactly where the pre-activation is
+                    g = d.relu_backward(g, self.buf(e.output))
+                self._accum(a["a"], d.gemm(g, self.buf(a["b"]), 1, m, k, n, trans_b=True))
+                self._accum(a["b"], d.gemm(self.buf(a["a"]), g, 1, k, n, m, trans_a=True))
+                if a["bias"] is not None:
+                    self._accum(a["bias"], d.sum_rows(g, m, n))
             else:  # pragma: no cover - every recorded op is handled above
                 raise KeyError(e.op)
 

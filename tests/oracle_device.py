@@ -59,6 +59,14 @@ class OracleDevice:
         return OracleBuffer(self.o.matmul(np.ascontiguousarray(A), np.ascontiguousarray(B),
                                           m, n, k))
 
+    def gemm_ex(self, a, b, batch, m, n, k, bias=None, resid=None, act=0, trans_a=False,
+                trans_b=False):
+        assert batch == 1 and resid is None and act in (0, 2)
+        c = self.gemm(a, b, batch, m, n, k, trans_a, trans_b)
+        if bias is not None:
+            c = self.add_per_col(c, bias, m, n)
+        return self.relu(c) if act == 2 else c
+
     def mse_loss(self, p, t):
         return OracleBuffer(self.o.mse_loss(p.data, t.data))
 

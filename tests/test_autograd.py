@@ -265,3 +265,56 @@ def test_unet_graph_gradients(new_tape):
         w = want[name]
         err = np.linalg.norm(got.astype(np.float64) - w) / max(np.linalg.norm(w), 1e-30)
         assert err < 5e-3, (name, err)
+
+
+@pytest.mark.parametrize("act", ["none", "relu"])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_linear_fused_matches_unfused(new_tape, act, with_bias):
+    """`Tape.linear` (one op, one launch: bias and ReLU in the GEMM epilogue)
+    gives the forward values and gradients of matmul -> add_per_col -> relu
+    recorded separately."""
+    m, n, k = 48, 40, 36
+    r = np.random.default_rng(17)
+    xv = r.standard_normal(m * k).astype(np.float32)
+    wv = (r.standard_normal(k * n) * 0.3).astype(np.float32)
+    bv = r.standard_normal(n).astype(np.float32)
+    tv = r.standard_normal(m * n).astype(np.float32)
+
+    fused = new_tape()
+    x, w = fused.leaf(xv), fused.leaf(wv)
+    b = fused.leaf(bv) if with_bias else None
+    launches = getattr(fused.dev, "launch_count", None)
+    y = fused.linear(x, w, b, m, n, k, act)
+    if launches is not None:
+        assert fused.dev.launch_count - launches == 1
+    loss = fused.mse_loss(y, fused.leaf(tv))
+    fused.backward(loss)
+
+    ref = new_tape()
+    x2, w2 = ref.leaf(xv), ref.leaf(wv)
+    y2 = ref.matmul(x2, w2, m, n, k)
+    if with_bias:
+        b2 = ref.leaf(bv)
+        y2 = ref.add_per_col(y2, b2, m, n)
+    if act == "relu":
+        y2 = ref.relu(y2)
+    loss2 = ref.mse_loss(y2, ref.leaf(tv))
+    ref.backward(loss2)
+
+    def close(got, want, tol=1e-5):
+        got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+        assert np.linalg.norm(got - want) <= tol * max(np.linalg.norm(want), 1e-30)
+
+    close(fused.read(y), ref.read(y2))
+    close(fused.read(loss), ref.read(loss2))
+    close(fused.read_grad(x), ref.read_grad(x2))
+    close(fused.read_grad(w), ref.read_grad(w2))
+    if with_bias:
+        close(fused.read_grad(b), ref.read_grad(b2))
+
+
+def test_linear_rejects_unsupported_activation(new_tape):
+    tape = new_tape()
+    x, w = tape.leaf(np.ones(4, np.float32)), tape.leaf(np.ones(4, np.float32))
+    with pytest.raises(ValueError):
+        tape.linear(x, w, None, 2, 2, 2, act="swish")
