@@ -19,9 +19,9 @@ the library's kernels; the backward rules are the reference's
   the reference (:368-374, the loss is the tape's last node).
 
 One fused op has no reference counterpart: `linear` records matmul + bias +
-ReLU as a single op whose forward is one GEMM with the bias and activation
-in its epilogue, and whose backward is the ReLU mask, the two GEMMs and the
-bias's `sum_rows`.
+activation as a single op whose forward is one GEMM with the bias (and a
+ReLU) in its epilogue, and whose backward is the activation's mask, the two
+GEMMs and the bias's `sum_rows`.
 
 Gradients are accumulated with `add` into a fresh buffer (:267-279); the
 pass-through gradients of Add, Sub and the broadcast adds share the upstream
@@ -167,15 +167,19 @@ class Tape:
         and the activation run in the GEMM's epilogue (`agpu_gemm_ex`).  No
         reference counterpart: it records what `matmul` -> `add_per_col` ->
         `relu` record as three ops (three launches, two [m, n] intermediates)
-        and has the same gradients.  `bias` may be None; `act` is "none" or
+        and has the same gradients.  `bias` may be None; `act` is "none",
         "relu" (the ReLU mask is read from the output, so no pre-activation
-        is kept)."""
-        codes = {"none": 0, "relu": 2}
+        is kept) or "swish" (its backward needs the pre-activation, so the
+        GEMM fuses only the bias and the swish is a second launch)."""
+        codes = {"none": 0, "relu": 2, "swish": 0}
         if act not in codes:
             raise ValueError(f"linear: act must be one of {sorted(codes)}, got {act!r}")
         out = self.dev.gemm_ex(self.buf(x), self.buf(w), 1, m, n, k,
                                bias=None if bias is None else self.buf(bias), act=codes[act])
-        return self._push(out, "linear", a=x, b=w, bias=bias, m=m, n=n, k=k, act=act)
+        pre = None
+        if act == "swish":
+            pre, out = out, self.dev.swish(out)
+        return self._push(out, "linear", a=x, b=w, bias=bias, m=m, n=n, k=k, act=act, pre=pre)
 
     # ----------------------------------------------------------- backward --
     def backward(self, loss: TensorId) -> None:
@@ -252,6 +256,8 @@ class Tape:
                 m, n, k = a["m"], a["n"], a["k"]
                 if a["act"] == "relu":  # out > 0 exactly where the pre-activation is
                     g = d.relu_backward(g, self.buf(e.output))
+                elif a["act"] == "swish":
+                    g = d.swish_backward(g, a["pre"])
                 self._accum(a["a"], d.gemm(g, self.buf(a["b"]), 1, m, k, n, trans_b=True))
                 self._accum(a["b"], d.gemm(self.buf(a["a"]), g, 1, k, n, m, trans_a=True))
                 if a["bias"] is not None:

@@ -267,12 +267,12 @@ def test_unet_graph_gradients(new_tape):
         assert err < 5e-3, (name, err)
 
 
-@pytest.mark.parametrize("act", ["none", "relu"])
+@pytest.mark.parametrize("act", ["none", "relu", "swish"])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_linear_fused_matches_unfused(new_tape, act, with_bias):
-    """`Tape.linear` (one op, one launch: bias and ReLU in the GEMM epilogue)
-    gives the forward values and gradients of matmul -> add_per_col -> relu
-    recorded separately."""
+    """`Tape.linear` (one op; bias and ReLU in the GEMM epilogue, swish as a
+    second launch) gives the forward values and gradients of matmul ->
+    add_per_col -> activation recorded separately."""
     m, n, k = 48, 40, 36
     r = np.random.default_rng(17)
     xv = r.standard_normal(m * k).astype(np.float32)
@@ -286,7 +286,7 @@ def test_linear_fused_matches_unfused(new_tape, act, with_bias):
     launches = getattr(fused.dev, "launch_count", None)
     y = fused.linear(x, w, b, m, n, k, act)
     if launches is not None:
-        assert fused.dev.launch_count - launches == 1
+        assert fused.dev.launch_count - launches == (2 if act == "swish" else 1)
     loss = fused.mse_loss(y, fused.leaf(tv))
     fused.backward(loss)
 
@@ -298,6 +298,8 @@ def test_linear_fused_matches_unfused(new_tape, act, with_bias):
         y2 = ref.add_per_col(y2, b2, m, n)
     if act == "relu":
         y2 = ref.relu(y2)
+    elif act == "swish":
+        y2 = ref.swish(y2)
     loss2 = ref.mse_loss(y2, ref.leaf(tv))
     ref.backward(loss2)
 
@@ -317,4 +319,4 @@ def test_linear_rejects_unsupported_activation(new_tape):
     tape = new_tape()
     x, w = tape.leaf(np.ones(4, np.float32)), tape.leaf(np.ones(4, np.float32))
     with pytest.raises(ValueError):
-        tape.linear(x, w, None, 2, 2, 2, act="swish")
+        tape.linear(x, w, None, 2, 2, 2, act="tanh")
