@@ -14,6 +14,7 @@ handles and host arrays.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 from typing import Optional, Sequence
 
@@ -139,6 +140,26 @@ class GpuDevice:
         v = C.c_int()
         _check(_lib.load().agpu_get_precision(self._h, C.byref(v)))
         return {v_: k for k, v_ in PRECISIONS.items()}[v.value]
+
+    @staticmethod
+    @contextlib.contextmanager
+    def precision(mode: str):
+        """Per-call precision: contractions enqueued by this thread inside the
+        block use `mode`; the devices' own settings and other threads are
+        untouched (agpu_set_thread_precision)."""
+        lib = _lib.load()
+        prev = lib.agpu_get_thread_precision()
+        _check(lib.agpu_set_thread_precision(PRECISIONS[mode]))
+        try:
+            yield
+        finally:
+            lib.agpu_set_thread_precision(prev)
+
+    def selftest_wait_timeout(self, limit_us: int = 1000, stream: int = 0) -> None:
+        """Launch the bounded-wait failure self-test (agpu_selftest_wait_timeout):
+        the next synchronize() on the device stream raises a TIMEOUT error."""
+        _check(_lib.load().agpu_selftest_wait_timeout(self._h, int(limit_us),
+                                                      C.c_void_p(stream or None)))
 
     def _new(self, fn, *args) -> GpuBuffer:
         out = C.c_void_p()

@@ -31,6 +31,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_synchronize": (c_status, [c_dev]),
     "agpu_set_precision": (c_status, [c_dev, i32]),
     "agpu_get_precision": (c_status, [c_dev, C.POINTER(i32)]),
+    "agpu_set_thread_precision": (c_status, [i32]),
+    "agpu_get_thread_precision": (i32, []),
     "agpu_device_launch_count": (u64, [c_dev]),
     "agpu_upload": (c_status, [c_dev, C.c_void_p, u64, P_buf]),
     "agpu_alloc": (c_status, [c_dev, u64, P_buf]),
@@ -121,6 +123,7 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
     "agpu_group_norm_noalloc": (c_status, [C.c_void_p] * 4 + [u32, u32, u32, u32, f32, i32,
                                                               C.c_void_p]),
+    "agpu_selftest_wait_timeout": (c_status, [c_dev, u32, C.c_void_p]),
 }
 
 class AttnLayout(C.Structure):

@@ -17,8 +17,12 @@ struct agpu_device {
   // second stream for work a launcher forks off and joins back (created on
   // first use, under `mu`)
   cudaStream_t aux = nullptr;
+  // this device's own stream-ordered pool (cudaMemPoolCreate), so that its
+  // release threshold and cached blocks touch no other user of the device
   cudaMemPool_t pool = nullptr;
-  agpu_precision precision = AGPU_PREC_TF32;
+  // device-wide default arithmetic of the contractions; read once per call
+  // through effective_precision(), which a thread-scoped override shadows
+  std::atomic<int> precision{AGPU_PREC_TF32};
   char name[256] = {0};
   // Device-side status word written by kernels whose bounded waits expire.
   unsigned int* d_status = nullptr;
@@ -71,6 +75,18 @@ cudaStream_t aux_stream(agpu_device* dev);
 
 // Allocate an output buffer of n floats on the device stream.
 agpu_status new_buffer(agpu_device* dev, uint64_t n, agpu_buffer** out);
+
+// Precision set by agpu_set_thread_precision for calls made from this host
+// thread (-1: none, use the device's).
+extern thread_local int g_thread_precision;
+
+// The arithmetic a contraction enqueued now from this thread uses: the
+// thread's override if set, else the device's setting.  Each launcher reads
+// it once, so one call never mixes modes.
+inline agpu_precision effective_precision(const agpu_device* dev) {
+  const int t = g_thread_precision;
+  return static_cast<agpu_precision>(t >= 0 ? t : dev->precision.load(std::memory_order_relaxed));
+}
 
 inline cudaStream_t pick_stream(agpu_device* dev, void* s) {
   return s ? static_cast<cudaStream_t>(s) : dev->stream;

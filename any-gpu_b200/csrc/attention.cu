@@ -1139,7 +1139,7 @@ agpu_status launch_attention_strided(agpu_device* dev, const float* q, const flo
   const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15u) == 0;
   // fp32-level accuracy modes (3xTF32, FFMA) take the exact SIMT kernel
-  const bool tc = dev->precision == AGPU_PREC_TF32 && aligned && pitch_ok &&
+  const bool tc = effective_precision(dev) == AGPU_PREC_TF32 && aligned && pitch_ok &&
                   (d == 64 || d == 128) && s >= 64 && H <= 65535 && B <= 65535;
   // sequences of >= 256 rows run on CTA pairs (AGPU_SDPA_PAIR=0: single CTAs)
   static const bool pair_ok = [] {

@@ -729,8 +729,9 @@ agpu_status launch_conv2d(agpu_device* dev, const ConvParams& p, const float* x,
                           const float* bias, float* y, cudaStream_t s) {
   const long long total = (long long)p.n * p.cout * p.ho * p.wo;
   if (total == 0) return AGPU_OK;
-  if (dev->precision != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
-    if (dev->precision == AGPU_PREC_TF32X3) return dispatch_conv_tc<true>(dev, p, x, w, bias, y, s);
+  const agpu_precision prec = effective_precision(dev);
+  if (prec != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
+    if (prec == AGPU_PREC_TF32X3) return dispatch_conv_tc<true>(dev, p, x, w, bias, y, s);
     return dispatch_conv_tc<false>(dev, p, x, w, bias, y, s);
   }
   conv2d_direct_kernel<<<grid_for(dev, total), 256, 0, s>>>(
@@ -744,8 +745,9 @@ agpu_status launch_conv2d_gn(agpu_device* dev, const ConvParams& p, const float*
                              cudaStream_t s) {
   const long long total = (long long)p.n * p.cout * p.ho * p.wo;
   if (total == 0) return AGPU_OK;
-  if (dev->precision != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
-    if (dev->precision == AGPU_PREC_TF32X3)
+  const agpu_precision prec = effective_precision(dev);
+  if (prec != AGPU_PREC_FFMA && conv_tc_eligible(p)) {
+    if (prec == AGPU_PREC_TF32X3)
       return dispatch_conv_tc<true>(dev, p, x, w, bias, y, s, &gn);
     return dispatch_conv_tc<false>(dev, p, x, w, bias, y, s, &gn);
   }
@@ -767,7 +769,8 @@ agpu_status launch_conv_transpose2d(agpu_device* dev, const ConvParams& p, const
   const int php = p.dh * (p.kh - 1) - p.ph, pwp = p.dw * (p.kw - 1) - p.pw;
   ConvParams q{p.n, p.cin, p.h, p.w, p.cout, p.kh, p.kw, 1, 1, php, pwp, p.dh, p.dw, 1, p.ho,
                p.wo};
-  if (dev->precision != AGPU_PREC_FFMA && p.sh == 1 && p.sw == 1 && p.groups == 1 && php >= 0 &&
+  if (effective_precision(dev) != AGPU_PREC_FFMA && p.sh == 1 && p.sw == 1 && p.groups == 1 &&
+      php >= 0 &&
       pwp >= 0 && p.ho == p.h + p.dh * (p.kh - 1) - 2 * p.ph &&
       p.wo == p.w + p.dw * (p.kw - 1) - 2 * p.pw && conv_tc_eligible(q)) {
     const long long wn = (long long)p.cin * p.cout * p.kh * p.kw;
@@ -791,10 +794,11 @@ agpu_status launch_conv2d_grad_weight(agpu_device* dev, const ConvParams& p, con
   const long long nw = (long long)p.cout * (p.cin / p.groups) * p.kh * p.kw;
   if (nw == 0) return AGPU_OK;
   // tensor cores: stride 1, one group, output rows in whole 32-pixel blocks
-  if (dev->precision != AGPU_PREC_FFMA && p.groups == 1 && p.sh == 1 && p.sw == 1 &&
+  const agpu_precision prec = effective_precision(dev);
+  if (prec != AGPU_PREC_FFMA && p.groups == 1 && p.sh == 1 && p.sw == 1 &&
       p.wo % 32 == 0 && p.n > 0 && p.n <= 65535 &&
       (long long)p.n * p.cout * p.ho * p.wo * p.cin * p.kh * p.kw >= (1LL << 22)) {
-    if (dev->precision == AGPU_PREC_TF32X3) {
+    if (prec == AGPU_PREC_TF32X3) {
       if (p.cin > 128) return run_wgrad_tc<256, true>(dev, p, x, gy, gw, s);
       return run_wgrad_tc<128, true>(dev, p, x, gy, gw, s);
     }

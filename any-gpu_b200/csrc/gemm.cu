@@ -672,7 +672,7 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
     AGPU_CUDA(cudaMemsetAsync(c, 0, (size_t)batch * m * n * sizeof(float), s));
     return AGPU_OK;
   }
-  const agpu_precision p = dev->precision;
+  const agpu_precision p = effective_precision(dev);
   if (ep.act == 3) {
     // SwiGLU: fused into the CTA-pair kernel's epilogue when that kernel runs
     // the GEMM whole; otherwise the plain GEMM into scratch, then swish * up

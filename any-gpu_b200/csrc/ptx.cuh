@@ -98,25 +98,34 @@ __device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// writes `code` into *status) if it did not within the time limit, or if
-// another thread of the CTA already flagged an abort in *abort_flag.
+// writes `code` into *status) if it did not within `limit_ns` of global time,
+// or if another thread of the CTA already flagged an abort in *abort_flag.
 template <bool CLUSTER = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          unsigned int* status, unsigned int code,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              unsigned int* status, unsigned int code,
+                                              volatile int* abort_flag,
+                                              unsigned long long limit_ns) {
   if (CLUSTER ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
   unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (CLUSTER ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         if (status) atomicCAS(status, 0u, code);
         if (abort_flag) *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// The same with the library-wide limit (kWaitLimitNs).
+template <bool CLUSTER = false>
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned int* status, unsigned int code,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for<CLUSTER>(bar, parity, status, code, abort_flag, kWaitLimitNs);
 }
 
 // ------------------------------------------------------------------ TMA --

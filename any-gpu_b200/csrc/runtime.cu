@@ -9,10 +9,12 @@
 #include <cstring>
 
 #include "agpu_internal.cuh"
+#include "ptx.cuh"
 
 namespace agpu {
 
 static thread_local char g_err[1024] = {0};
+thread_local int g_thread_precision = -1;
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -75,6 +77,9 @@ void device_release(agpu_device* dev) {
     cudaStreamSynchronize(dev->aux);
     cudaStreamDestroy(dev->aux);
   }
+  // Blocks still out (scratch freed on a caller stream that has not reached
+  // the free yet) keep the pool alive until they come back.
+  if (dev->pool) cudaMemPoolDestroy(dev->pool);
   delete dev;
 }
 
@@ -103,6 +108,25 @@ agpu_status check_device_status(agpu_device* dev) {
     return fail(AGPU_ERR_TIMEOUT, "a device-side bounded wait expired (code 0x%x)", h);
   }
   return AGPU_OK;
+}
+
+// Failure-path self-test: one warp waits on an mbarrier that no thread ever
+// arrives on.  The wait gives up after limit_ns, records `code` in the device
+// status word and the kernel returns: the path every pipeline wait of the
+// contraction kernels takes when its producer never arrives, exercised
+// without TMA, tensor cores or tensor memory.
+__global__ void wait_timeout_selftest_kernel(unsigned int* status, unsigned long long limit_ns,
+                                             unsigned int code) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  ptx::mbar_wait_for(&bar, 0, status, code, &abort_flag, limit_ns);
+  __syncthreads();
 }
 
 }  // namespace agpu
@@ -150,14 +174,31 @@ agpu_status agpu_device_create(int ordinal, agpu_device** out) {
   snprintf(d->name, sizeof(d->name), "%s", prop.name);
   e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaStreamCreate"); }
-  e = cudaDeviceGetDefaultMemPool(&d->pool, ordinal);
-  if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaDeviceGetDefaultMemPool"); }
-  // Keep freed blocks cached in the pool instead of returning them to the
-  // driver at every synchronisation: steady-state ops never hit cudaMalloc.
+  // A pool of this handle's own (not the device's default pool, which other
+  // libraries in the process, torch's async allocator among them, share):
+  // freed blocks stay cached in it instead of going back to the driver at
+  // every synchronisation, so steady-state ops never reach cudaMalloc, and
+  // no other pool user sees that setting.
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.handleTypes = cudaMemHandleTypeNone;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = ordinal;
+  e = cudaMemPoolCreate(&d->pool, &props);
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(d->stream);
+    delete d;
+    return cuda_status(e, "cudaMemPoolCreate");
+  }
   uint64_t threshold = UINT64_MAX;
   cudaMemPoolSetAttribute(d->pool, cudaMemPoolAttrReleaseThreshold, &threshold);
   e = cudaMalloc(&d->d_status, sizeof(unsigned int));
-  if (e != cudaSuccess) { delete d; return cuda_status(e, "cudaMalloc(status)"); }
+  if (e != cudaSuccess) {
+    cudaMemPoolDestroy(d->pool);
+    cudaStreamDestroy(d->stream);
+    delete d;
+    return cuda_status(e, "cudaMalloc(status)");
+  }
   cudaMemset(d->d_status, 0, sizeof(unsigned int));
   *out = d;
   return AGPU_OK;
@@ -201,15 +242,24 @@ agpu_status agpu_set_precision(agpu_device* dev, agpu_precision p) {
   if (!dev) return fail(AGPU_ERR_INVALID, "agpu_set_precision: NULL device");
   if (p != AGPU_PREC_TF32 && p != AGPU_PREC_TF32X3 && p != AGPU_PREC_FFMA)
     return fail(AGPU_ERR_INVALID, "agpu_set_precision: unknown mode %d", (int)p);
-  dev->precision = p;
+  dev->precision.store(p, std::memory_order_relaxed);
   return AGPU_OK;
 }
 
 agpu_status agpu_get_precision(const agpu_device* dev, agpu_precision* p) {
   if (!dev || !p) return fail(AGPU_ERR_INVALID, "agpu_get_precision: bad argument");
-  *p = dev->precision;
+  *p = static_cast<agpu_precision>(dev->precision.load(std::memory_order_relaxed));
   return AGPU_OK;
 }
+
+agpu_status agpu_set_thread_precision(int mode) {
+  if (mode != -1 && mode != AGPU_PREC_TF32 && mode != AGPU_PREC_TF32X3 && mode != AGPU_PREC_FFMA)
+    return fail(AGPU_ERR_INVALID, "agpu_set_thread_precision: unknown mode %d", mode);
+  g_thread_precision = mode;
+  return AGPU_OK;
+}
+
+int agpu_get_thread_precision(void) { return g_thread_precision; }
 
 uint64_t agpu_device_launch_count(const agpu_device* dev) {
   return dev ? dev->launches.load() : 0;
@@ -252,6 +302,7 @@ agpu_status agpu_write(agpu_device* dev, agpu_buffer* buf, const float* host, ui
   if (n != buf->len)
     return fail(AGPU_ERR_SHAPE, "agpu_write: buffer has %llu elems, host has %llu",
                 (unsigned long long)buf->len, (unsigned long long)n);
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
   AGPU_CUDA(cudaMemcpyAsync(buf->dptr, host, n * sizeof(float), cudaMemcpyHostToDevice,
                             dev->stream));
   return AGPU_OK;
@@ -297,6 +348,17 @@ agpu_status agpu_write_async(agpu_device* dev, agpu_buffer* buf, uint64_t offset
 agpu_status agpu_read_async(agpu_device* dev, const agpu_buffer* buf, uint64_t offset,
                             float* host, uint64_t n, void* stream) {
   return copy_async(dev, buf, offset, n, host, false, stream, "agpu_read_async");
+}
+
+agpu_status agpu_selftest_wait_timeout(agpu_device* dev, uint32_t limit_us, void* stream) {
+  if (!dev) return fail(AGPU_ERR_INVALID, "agpu_selftest_wait_timeout: NULL device");
+  if (limit_us == 0 || limit_us > 1000000u)
+    return fail(AGPU_ERR_INVALID, "agpu_selftest_wait_timeout: limit_us %u outside [1, 1000000]",
+                limit_us);
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  wait_timeout_selftest_kernel<<<1, 32, 0, pick_stream(dev, stream)>>>(
+      dev->d_status, 1000ull * limit_us, AGPU_SELFTEST_WAIT_CODE);
+  return after_launch(dev, "wait_timeout_selftest_kernel");
 }
 
 agpu_status agpu_buffer_free(agpu_buffer* buf) {

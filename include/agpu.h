@@ -91,8 +91,16 @@ AGPU_API agpu_status agpu_device_ordinal(const agpu_device* dev, int* out);
 /* The device's CUDA stream as an opaque cudaStream_t. */
 AGPU_API void* agpu_device_stream(const agpu_device* dev);
 AGPU_API agpu_status agpu_synchronize(agpu_device* dev);
+/* Device-wide default arithmetic of the contractions (initially TF32). */
 AGPU_API agpu_status agpu_set_precision(agpu_device* dev, agpu_precision p);
 AGPU_API agpu_status agpu_get_precision(const agpu_device* dev, agpu_precision* p);
+/* Per-call precision without touching the shared device: every contraction
+ * this host thread enqueues after the call, on any device, uses `mode`
+ * (an agpu_precision) until the thread sets -1 again, which returns it to
+ * each device's own setting.  Other threads are unaffected.  No counterpart
+ * in the reference (its shaders have one arithmetic). */
+AGPU_API agpu_status agpu_set_thread_precision(int mode);
+AGPU_API int agpu_get_thread_precision(void);
 /* Number of this library's kernels launched on `dev` since creation. */
 AGPU_API uint64_t agpu_device_launch_count(const agpu_device* dev);
 
@@ -122,7 +130,11 @@ AGPU_API agpu_status agpu_write_async(agpu_device* dev, agpu_buffer* buf, uint64
                                       const float* host, uint64_t n, void* stream);
 AGPU_API agpu_status agpu_read_async(agpu_device* dev, const agpu_buffer* buf, uint64_t offset,
                                      float* host, uint64_t n, void* stream);
-/* Replaces Drop for GpuBuffer: returns memory to the device pool. */
+/* Replaces Drop for GpuBuffer: returns memory to the device pool, ordered
+ * on the device stream.  Work that uses the buffer on another stream
+ * (agpu_read_async / agpu_write_async / a launch-layer call given its
+ * address) must have been reached by that stream first: synchronise the
+ * stream, or make the device stream wait on it, before freeing. */
 AGPU_API agpu_status agpu_buffer_free(agpu_buffer* buf);
 /* GpuBuffer::len (src/device.rs:25). */
 AGPU_API uint64_t agpu_buffer_len(const agpu_buffer* buf);
@@ -489,6 +501,20 @@ AGPU_API agpu_status agpu_group_norm_noalloc(const float* x, const float* gamma,
                                              uint32_t channels, uint32_t spatial,
                                              uint32_t groups, float eps, int apply_swish,
                                              void* stream);
+
+/* ---------------------------------------------------- failure self-test -- */
+/* No counterpart in the reference.  Exercises the failure path of the
+ * bounded device-side waits without faulting or hanging anything: launches
+ * one warp on `stream` (NULL = the device stream) that waits on an mbarrier
+ * no thread arrives on, gives up after `limit_us` microseconds (1..1e6),
+ * records AGPU_SELFTEST_WAIT_CODE in the device status word and returns.
+ * The next agpu_synchronize / agpu_read on the device stream then returns
+ * AGPU_ERR_TIMEOUT (the message names the code) and clears the word; the
+ * device stays usable.  Every pipeline wait of the contraction kernels
+ * expires the same way, after 2 s. */
+#define AGPU_SELFTEST_WAIT_CODE 0x7e57u
+AGPU_API agpu_status agpu_selftest_wait_timeout(agpu_device* dev, uint32_t limit_us,
+                                                void* stream);
 
 #ifdef __cplusplus
 }

@@ -61,6 +61,23 @@ def test_status_strings_and_null_handling():
     assert lib.agpu_matmul(None, None, None, 1, 1, 1, C.byref(out)) == 2
     assert b"NULL" in lib.agpu_last_error_message()
     assert lib.agpu_device_create(0, None) == 2
+    assert lib.agpu_selftest_wait_timeout(None, 1000, None) == 2
+
+
+def test_thread_precision_override_is_thread_local():
+    import threading
+    from any_gpu import _lib
+    lib = _lib.load()
+    assert lib.agpu_get_thread_precision() == -1
+    assert lib.agpu_set_thread_precision(5) == 2
+    assert lib.agpu_set_thread_precision(1) == 0
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.agpu_get_thread_precision()))
+    t.start()
+    t.join()
+    assert lib.agpu_get_thread_precision() == 1 and seen == [-1]
+    assert lib.agpu_set_thread_precision(-1) == 0
+    assert lib.agpu_get_thread_precision() == -1
 
 
 @pytest.mark.skipif(cuda_available(), reason="checks the no-GPU path")
