@@ -27,3 +27,29 @@ def test_reference_arm_json_line():
     e2e = line["e2e"]
     assert e2e["value"] == line["value"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    # the step is the bounded sample that ran, not the extrapolated full step
+    assert line["ms_per_step"] < line["ms_per_full_step_extrapolated"]
+    assert line["dtype"] == "f32" and "fp32" in line["precision"]
+    assert "tf32" not in json.dumps(line["config"])
+
+
+def test_bench_workload_plans_cpu():
+    """The bench's workloads build their shard plans and job sizes on CPU: the
+    job (items, FLOPs) is the same at every N, and each rank's share adds up."""
+    sys.path.insert(0, str(ROOT))
+    import argparse
+    import bench
+    args = argparse.Namespace(batch=64, size=512, precision="tf32", bh=256, seq=2048, images=16,
+                              llama_batch=32, graph=None)
+    for cls in (bench.BmmSoftmax, bench.Sdpa, bench.Unet, bench.Llama):
+        one = cls(args, 1, 0)
+        assert one.scaling() == "strong" and one.local == one.total
+        for world in (2, 4, 8):
+            ranks = [cls(args, world, r) for r in range(world)]
+            assert all(w.flops == one.flops for w in ranks)
+            assert sum(w.local for w in ranks) == one.total
+            assert all(w.scaling() == "strong" and w.sharded for w in ranks)
+            rep = cls(args, world, 0, replicas=True)
+            assert rep.scaling() == "weak" and rep.flops == world * one.flops
+    mm = bench.Matmul(args, 4, 1)
+    assert not mm.sharded and mm.scaling() == "weak" and mm.flops == 4 * 2.0 * 512 ** 3

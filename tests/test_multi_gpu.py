@@ -1,7 +1,11 @@
-"""GPU, 2 ranks over NCCL (skipped with fewer than 2 GPUs): each rank runs
-batch_matmul + softmax on its shard of the batch through the library's launch
-layer, the shards are all-gathered, and every rank checks the full result
-against a single-GPU run of the whole batch."""
+"""GPU, 2 ranks over NCCL (skipped with fewer than 2 GPUs): the sharded step
+the bench runs.  Each rank runs its items of each round through the library's
+launch layer, writing its slots of the full-size output, and the rounds are
+all-gathered in place (any_gpu.dist.run_rounds).  Checked: every rank holds
+the same bytes, and the whole result matches the oracle.  Covers batch_matmul
++ softmax in two rounds (GEMMs on one stream, softmaxes on another), an
+uneven split (5 items over 2 ranks: in-place broadcasts), and attention
+sharded by heads."""
 from __future__ import annotations
 
 import os
@@ -32,38 +36,72 @@ def _worker(rank, world, port, q):
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
     sys.path.insert(0, str(root / "any-gpu_b200"))
+    sys.path.insert(0, str(root))
     import datetime
 
     import torch
     import torch.distributed as dist
     from any_gpu import GpuDevice
-    from any_gpu.dist import all_gather_shards, batch_shard
+    from any_gpu.dist import ShardPlan, run_rounds
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", rank))
-        batch, m, n, k = 6, 256, 512, 384
-        r = np.random.default_rng(3)
-        a = (r.standard_normal(batch * m * k) * 0.05).astype(np.float32)
-        b = (r.standard_normal(batch * k * n) * 0.05).astype(np.float32)
         dev = GpuDevice.gpu(rank)
-        s = torch.cuda.Stream()
-        torch.cuda.set_stream(s)
-        start, cnt = batch_shard(batch, world, rank)
-        A = torch.from_numpy(a[start * m * k:(start + cnt) * m * k]).cuda()
-        B = torch.from_numpy(b[start * k * n:(start + cnt) * k * n]).cuda()
-        C = torch.empty(cnt * m * n, device="cuda")
-        S = torch.empty_like(C)
-        dev.launch_batch_matmul(A.data_ptr(), B.data_ptr(), C.data_ptr(), cnt, m, n, k,
-                                s.cuda_stream)
-        dev.launch_softmax(C.data_ptr(), S.data_ptr(), cnt * m, n, s.cuda_stream)
-        full = all_gather_shards(S, batch, m * n).cpu().numpy()
-        # the same batch on this one GPU, through the buffer API
-        want = dev.read(dev.softmax(dev.batch_matmul(dev.upload(a), dev.upload(b), batch, m, n,
-                                                     k), batch * m, n))
-        q.put((rank, float(np.abs(full - want).max()), None))
+        stream = torch.cuda.Stream()
+        aux = torch.cuda.Stream()
+        torch.cuda.set_stream(stream)
+        results = {}
+
+        # batch_matmul + softmax: (batch, rounds)
+        m, n, k = 256, 512, 384
+        for batch, rounds in ((8, 2), (5, 1)):
+            r = np.random.default_rng(3 + batch)
+            a = (r.standard_normal(batch * m * k) * 0.05).astype(np.float32)
+            b = (r.standard_normal(batch * k * n) * 0.05).astype(np.float32)
+            plan = ShardPlan(batch, world, rank, rounds)
+            items = plan.my_items()
+            A = torch.from_numpy(np.concatenate([a[g * m * k:(g + 1) * m * k]
+                                                 for g in items])).cuda()
+            B = torch.from_numpy(np.concatenate([b[g * k * n:(g + 1) * k * n]
+                                                 for g in items])).cuda()
+            out = torch.full((batch * m * n,), float("nan"), device="cuda")
+
+            def launch(rd):
+                cnt = rd.counts[rank]
+                c = out.data_ptr() + 4 * rd.offsets[rank] * m * n
+                dev.launch_batch_matmul(A.data_ptr() + 4 * rd.local * m * k,
+                                        B.data_ptr() + 4 * rd.local * k * n, c, cnt, m, n, k,
+                                        stream.cuda_stream)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                aux.wait_event(ev)
+                dev.launch_softmax(c, c, cnt * m, n, aux.cuda_stream)
+                return aux
+            run_rounds(plan, out, m * n, launch, stream)
+            stream.synchronize()
+            results[f"bmm{batch}"] = (out.cpu().numpy(), a, b)
+
+        # attention, heads split over the ranks in one round
+        bh, s, d = 6, 256, 128
+        r = np.random.default_rng(9)
+        qkv = [r.standard_normal(bh * s * d).astype(np.float32) for _ in range(3)]
+        plan = ShardPlan(bh, world, rank, 1)
+        st, cnt = plan.spans[0].offsets[rank], plan.spans[0].counts[rank]
+        Q, K, V = (torch.from_numpy(x[st * s * d:(st + cnt) * s * d]).cuda() for x in qkv)
+        O = torch.full((bh * s * d,), float("nan"), device="cuda")
+
+        def launch_attn(rd):
+            dev.launch_sdpa(Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                            O.data_ptr() + 4 * st * s * d, cnt, s, d, False, stream.cuda_stream)
+            return stream
+        run_rounds(plan, O, s * d, launch_attn, stream)
+        stream.synchronize()
+        results["sdpa"] = (O.cpu().numpy(), *qkv)
+        dev.synchronize()
+        q.put((rank, results, None))
         torch.cuda.synchronize()
         dist.destroy_process_group()
         dev.close()
@@ -72,7 +110,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_two_gpu_sharded_batch_matmul_softmax():
+def test_two_gpu_sharded_rounds_gather_in_place(orc):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -80,10 +118,20 @@ def test_two_gpu_sharded_batch_matmul_softmax():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in procs]
+    res = sorted((q.get(timeout=300) for _ in procs), key=lambda x: x[0])
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, diff, err in res:
+    for rank, _, err in res:
         assert err is None, f"rank {rank}: {err}"
-        assert diff == 0.0, f"rank {rank}: max |diff| {diff}"
+    r0, r1 = res[0][1], res[1][1]
+    m, n, k = 256, 512, 384
+    for batch in (8, 5):
+        got0, a, b = r0[f"bmm{batch}"]
+        got1 = r1[f"bmm{batch}"][0]
+        assert np.array_equal(got0, got1), f"bmm{batch}: ranks hold different results"
+        want = orc.softmax(orc.batch_matmul(a, b, batch, m, n, k), batch * m, n)
+        assert orc.rel_fro(got0, want) <= 1e-3
+    got0, qh, kh, vh = r0["sdpa"]
+    assert np.array_equal(got0, r1["sdpa"][0])
+    assert orc.rel_fro(got0, orc.attention(qh, kh, vh, 6, 256, 128)) <= 1e-3
