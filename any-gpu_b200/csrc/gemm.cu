@@ -34,6 +34,7 @@
 #include "umma_kernel.cuh"
 #include "umma2_kernel.cuh"
 #include "umma2_splitk_kernel.cuh"
+#include "umma2_x3_kernel.cuh"
 #include "pair_launch.cuh"
 
 namespace agpu {
@@ -257,6 +258,14 @@ struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
   }
 };
 
+// 3xTF32 on CTA pairs (umma2_x3_kernel.cuh): the pair tile plus the number
+// of K-blocks each accumulator segment sums before the epilogue folds it into
+// the running sum in tensor memory.
+template <int BN_, bool A_MN_, bool B_MN_>
+struct GemmPairX3Policy : GemmPairPolicy<BN_, A_MN_, B_MN_> {
+  int seg = 16;
+};
+
 // ------------------------------------------------------------ SIMT FFMA --
 // Exact fp32 GEMM, 64x64 tile per 256 threads, 4x4 outputs per thread,
 // arbitrary strides/alignment.  a_trans: A stored [K,M]; b_trans: B stored [N,K].
@@ -472,6 +481,83 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
                      "gemm_tf32 (umma_tf32_pair_kernel)");
 }
 
+// K-blocks (of 32) per accumulator segment of the 3xTF32 pair kernel:
+// AGPU_X3_SEG in the environment, default 16 (K = 512); 0 = no segments.
+static int x3_seg() {
+  static const int v = [] {
+    const char* e = getenv("AGPU_X3_SEG");
+    return e ? std::max(0, atoi(e)) : 16;
+  }();
+  return v;
+}
+
+// 3xTF32 GEMM on 256 x 256 CTA-pair tiles: lo(A), lo(B) into pool scratch by
+// one elementwise pass, then the pair kernel reads each operand twice (as
+// stored: its hi part; and its lo part) and sums three products per slice.
+template <bool A_MN, bool B_MN>
+static agpu_status run_tc_pair_x3(agpu_device* dev, const float* a, const float* b, float* c,
+                                  uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
+                                  const GemmEpilogue& ep, cudaStream_t s) {
+  using P = GemmPairX3Policy<256, A_MN, B_MN>;
+  using Cfg = umma::PairX3Cfg<256>;
+  const uint64_t na = (uint64_t)batch * m * k, nb = (uint64_t)batch * k * n;
+  void* scratch = nullptr;
+  AGPU_TRY(pool_alloc(dev, (na + nb) * sizeof(float), &scratch, s));
+  float* alo = static_cast<float*>(scratch);
+  float* blo = alo + na;  // na % 4 == 0 (k % 4 == 0): 16-byte aligned
+  auto lo_pass = [&](const float* x, float* lo, uint64_t nx) {
+    const long long n4 = (long long)(nx / 4);
+    const long long grid = std::min<long long>((n4 + 255) / 256, 8LL * dev->sm_count);
+    umma::tf32_lo_kernel<<<(unsigned)std::max<long long>(grid, 1), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(lo), n4);
+  };
+  lo_pass(a, alo, na);
+  lo_pass(b, blo, nb);
+  agpu_status st = after_launch(dev, "tf32_lo_kernel", 2);
+  CUtensorMap ta, tb, tal, tbl;
+  P pol, pol_lo;
+  if (st == AGPU_OK)
+    st = make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, P::HALF, false);
+  if (st == AGPU_OK)
+    st = make_gemm_maps(&tal, &tbl, &pol_lo, alo, blo, batch, m, n, k, P::HALF, false);
+  if (st == AGPU_OK) {
+    pol.M = m; pol.N = n; pol.K = k;
+    pol.tiles_m = (int)ceil_div(m, P::PM);
+    pol.tiles_n = (int)ceil_div(n, 256);
+    pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
+    pol.C = c;
+    pol.c_batch = (long long)m * n;
+    pol.bias = ep.bias;
+    pol.resid = ep.resid;
+    pol.act = ep.act;
+    pol.seg = x3_seg();
+    auto kern = umma::umma_x3_pair_kernel<P>;
+    cudaError_t e = set_smem_once<umma::umma_x3_pair_kernel<P>>(dev, Cfg::SMEM);
+    if (e == cudaSuccess) {
+      const long long clusters = std::min<long long>(pol.tiles, std::max(1, dev->sm_count / 2));
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tal, tbl, pol, dev->d_status);
+    }
+    st = e == cudaSuccess ? after_launch(dev, "gemm_3xtf32 (umma_x3_pair_kernel)")
+                          : cuda_status(e, "gemm_3xtf32 (umma_x3_pair_kernel)");
+  }
+  pool_free(dev, scratch, s);
+  return st;
+}
+
 // Split-K over a cluster of S CTA pairs per 256 x 256 tile (S = 2 or 4).
 template <bool A_MN, bool B_MN, int S>
 static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const float* b, float* c,
@@ -605,6 +691,12 @@ static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at,
                                bool bt, const GemmEpilogue& ep, cudaStream_t s) {
   const bool wide = n > 128;
+  if (X3 && use_pair(m, n)) {
+    if (!at && !bt) return run_tc_pair_x3<false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (!at && bt) return run_tc_pair_x3<false, false>(dev, a, b, c, batch, m, n, k, ep, s);
+    if (at && !bt) return run_tc_pair_x3<true, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    return run_tc_pair_x3<true, false>(dev, a, b, c, batch, m, n, k, ep, s);
+  }
   if (!X3 && use_pair(m, n)) {
     const int sl = splitk_slices(dev, batch, m, n, k);
     if (sl == 4) {

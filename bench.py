@@ -188,6 +188,7 @@ class Workload:
     item_elems: dict = {}  # per-item input name -> elements
     out_item = 0           # output elements per item
     item_flops = 0.0
+    dom_item_flops = 0.0   # the dominant kernel's FLOPs per item (0: item_flops)
 
     def __init__(self, args, world, rank, replicas=False):
         self.args, self.world, self.rank = args, world, rank
@@ -199,7 +200,8 @@ class Workload:
         self.local = self.plan.my_count
         self.job_items = self.total if (self.sharded or world == 1) else self.total * world
         self.flops = self.job_items * self.item_flops
-        self.local_flops = self.local * self.item_flops
+        # FLOPs of the dominant kernel's launch over this rank's items
+        self.dom_flops = self.local * (self.dom_item_flops or self.item_flops)
 
     # ---- description
     def total_items(self) -> int:
@@ -757,6 +759,7 @@ class Llama(Workload):
         self.item_elems = {"x": one.seq * one.d_model}
         self.out_item = one.seq * one.d_model
         self.item_flops = one.gemm_flops() + one.attention_flops()
+        self.dom_item_flops = 2.0 * one.tokens * one.d_model * 2 * one.ffn  # gate/up GEMM
         super().__init__(args, world, rank, replicas)
 
     def dims(self, batch):
@@ -1065,7 +1068,7 @@ def _measure(ctx, wl, dev, stream, cpu_seconds, cpu_single, e2e_steps, steps, wa
     if ctx.rank != 0:
         return None
 
-    achieved = wl.local_flops / (dom_ms * 1e-3) / 1e12
+    achieved = wl.dom_flops / (dom_ms * 1e-3) / 1e12
     h2d, d2h = wl.e2e_bytes()
     e2e_flops = wl.flops
     entry = {
