@@ -505,15 +505,12 @@ static agpu_status run_tc_pair_x3(agpu_device* dev, const float* a, const float*
   AGPU_TRY(pool_alloc(dev, (na + nb) * sizeof(float), &scratch, s));
   float* alo = static_cast<float*>(scratch);
   float* blo = alo + na;  // na % 4 == 0 (k % 4 == 0): 16-byte aligned
-  auto lo_pass = [&](const float* x, float* lo, uint64_t nx) {
-    const long long n4 = (long long)(nx / 4);
-    const long long grid = std::min<long long>((n4 + 255) / 256, 8LL * dev->sm_count);
-    umma::tf32_lo_kernel<<<(unsigned)std::max<long long>(grid, 1), 256, 0, s>>>(
-        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(lo), n4);
-  };
-  lo_pass(a, alo, na);
-  lo_pass(b, blo, nb);
-  agpu_status st = after_launch(dev, "tf32_lo_kernel", 2);
+  const long long n4 = (long long)((na + nb) / 4);
+  const long long grid = std::min<long long>((n4 + 255) / 256, 8LL * dev->sm_count);
+  umma::tf32_lo_kernel<<<(unsigned)std::max<long long>(grid, 1), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(a), reinterpret_cast<float4*>(alo), (long long)(na / 4),
+      reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(blo), (long long)(nb / 4));
+  agpu_status st = after_launch(dev, "tf32_lo_kernel");
   CUtensorMap ta, tb, tal, tbl;
   P pol, pol_lo;
   if (st == AGPU_OK)

@@ -55,18 +55,25 @@ struct PairX3Cfg {
 };
 
 // lo = x - hi(x), hi(x) = x with the low 13 mantissa bits cleared (what the
-// tensor core reads from x in kind::tf32).  n4 float4s; 16-byte aligned.
-__global__ void __launch_bounds__(256) tf32_lo_kernel(const float4* __restrict__ x,
-                                                      float4* __restrict__ lo, long long n4) {
+// tensor core reads from x in kind::tf32), for two operands in one launch:
+// elements [0, n4a) of the float4 range are A's, the rest B's.  16-byte
+// aligned, lengths in float4s.
+__device__ __forceinline__ float tf32_lo(float v) {
+  return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+}
+
+__global__ void __launch_bounds__(256) tf32_lo_kernel(const float4* __restrict__ a,
+                                                      float4* __restrict__ alo, long long n4a,
+                                                      const float4* __restrict__ b,
+                                                      float4* __restrict__ blo, long long n4b) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-    const float4 v = __ldg(x + i);
-    float4 l;
-    l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-    lo[i] = l;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4a + n4b;
+       i += stride) {
+    const bool in_a = i < n4a;
+    const long long j = in_a ? i : i - n4a;
+    const float4 v = __ldg((in_a ? a : b) + j);
+    (in_a ? alo : blo)[j] =
+        make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
   }
 }
 

@@ -41,6 +41,34 @@ def test_library_exports_every_declared_symbol():
     assert set(declared_functions()) <= exported
 
 
+def _header_arities() -> dict:
+    out = {}
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for name, params in re.findall(r"AGPU_API\s+[\w\s\*]+?\b(agpu_\w+)\s*\(([^;]*?)\)\s*;",
+                                       text, flags=re.S):
+            params = " ".join(params.split())
+            out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_rust_ffi_matches_header():
+    """The Rust crate's raw bindings (any-gpu_b200/rust/src/ffi.rs) declare
+    every function of the header with the same number of arguments (it is not
+    compiled in this image, so this keeps it in step with the header)."""
+    ffi = (ROOT / "any-gpu_b200" / "rust" / "src" / "ffi.rs").read_text()
+    rust = {}
+    for name, params in re.findall(r"pub fn (agpu_\w+)\s*\(([^)]*)\)", ffi, flags=re.S):
+        params = [p for p in params.split(",") if p.strip()]
+        rust[name] = len(params)
+    assert rust == _header_arities()
+    device = (ROOT / "any-gpu_b200" / "rust" / "src" / "device.rs").read_text()
+    for fn in ("pub fn gpu(", "pub fn upload(", "pub fn alloc(", "pub fn read(", "pub fn matmul(",
+               "pub fn batch_matmul(", "pub fn softmax(", "pub fn scaled_dot_product_attention(",
+               "pub fn conv2d(", "pub fn group_norm(", "pub fn transpose(", "pub fn swish("):
+        assert fn in device, fn
+
+
 def test_ctypes_table_matches_header():
     from any_gpu import _lib
     assert set(_lib.SIGNATURES) == set(declared_functions())

@@ -46,7 +46,9 @@ def test_matmul_ragged_tensor_core(dev, orc, m, n, k, prec):
     try:
         before = dev.launch_count
         got = dev.read(dev.matmul(dev.upload(a), dev.upload(b), m, n, k))
-        assert dev.launch_count == before + 1
+        # one GEMM launch; 3xTF32 on CTA pairs (m, n >= 256) adds its lo-split pass
+        pair_x3 = prec == "tf32x3" and m >= 256 and n >= 256
+        assert dev.launch_count == before + (2 if pair_x3 else 1)
     finally:
         dev.set_precision("tf32")
     want = orc.matmul(a, b, m, n, k, threads=True)
