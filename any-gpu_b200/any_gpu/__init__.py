@@ -322,6 +322,21 @@ class GpuDevice:
         return self._new(_lib.load().agpu_sdpa_causal, q.handle, k.handle, v.handle,
                          batch_heads, seq_len, d_k)
 
+    def sdpa_backward(self, q, k, v, grad_out, batch_heads: int, seq_len: int, d_k: int,
+                      causal: bool = False):
+        """dQ, dK, dV of scaled_dot_product_attention from dO (agpu_sdpa_backward)."""
+        outs = [C.c_void_p(), C.c_void_p(), C.c_void_p()]
+        _check(_lib.load().agpu_sdpa_backward(self._h, q.handle, k.handle, v.handle,
+                                              grad_out.handle, batch_heads, seq_len, d_k,
+                                              int(causal), *(C.byref(o) for o in outs)))
+        return tuple(GpuBuffer(o.value, self) for o in outs)
+
+    def launch_sdpa_backward(self, q_ptr, k_ptr, v_ptr, do_ptr, dq_ptr, dk_ptr, dv_ptr, bh, s, d,
+                             causal=False, stream: int = 0) -> None:
+        _check(_lib.load().agpu_launch_sdpa_backward(self._h, q_ptr, k_ptr, v_ptr, do_ptr, dq_ptr,
+                                                     dk_ptr, dv_ptr, bh, s, d, int(causal),
+                                                     stream or None))
+
     def launch_sdpa(self, q_ptr, k_ptr, v_ptr, o_ptr, bh, s, d, causal=False,
                     stream: int = 0) -> None:
         _check(_lib.load().agpu_launch_sdpa(self._h, q_ptr, k_ptr, v_ptr, o_ptr, bh, s, d,

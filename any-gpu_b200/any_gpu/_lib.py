@@ -65,6 +65,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_scaled_dot_product_attention": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32,
                                                      P_buf]),
     "agpu_sdpa_causal": (c_status, [c_dev, c_buf, c_buf, c_buf, u32, u32, u32, P_buf]),
+    "agpu_sdpa_backward": (c_status, [c_dev, c_buf, c_buf, c_buf, c_buf, u32, u32, u32, i32,
+                                      P_buf, P_buf, P_buf]),
     "agpu_rmsnorm": (c_status, [c_dev, c_buf, c_buf, u32, u32, f32, P_buf]),
     "agpu_rope": (c_status, [c_dev, c_buf, u32, u32, u32, u32, f32, P_buf]),
     "agpu_swish_mul": (c_status, [c_dev, c_buf, c_buf, P_buf]),
@@ -111,6 +113,8 @@ SIGNATURES: dict[str, tuple] = {
                                      C.c_void_p]),
     "agpu_launch_sdpa": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32, u32, u32, i32,
                                                                  C.c_void_p]),
+    "agpu_launch_sdpa_backward": (c_status, [c_dev] + [C.c_void_p] * 7 + [u32, u32, u32, i32,
+                                                                      C.c_void_p]),
     "agpu_launch_gemm_ex": (c_status, [c_dev] + [C.c_void_p] * 3 + [u32] * 4 + [i32, i32]
                             + [C.c_void_p] * 2 + [i32, C.c_void_p]),
     "agpu_launch_sdpa_strided": (c_status, [c_dev] + [C.c_void_p] * 4 + [u32] * 4

@@ -18,10 +18,13 @@ the library's kernels; the backward rules are the reference's
 * MseLoss: 2 (pred - target) / n, the upstream gradient not applied, as in
   the reference (:368-374, the loss is the tape's last node).
 
-One fused op has no reference counterpart: `linear` records matmul + bias +
+Two ops have no reference counterpart.  `linear` records matmul + bias +
 activation as a single op whose forward is one GEMM with the bias (and a
 ReLU) in its epilogue, and whose backward is the activation's mask, the two
-GEMMs and the bias's `sum_rows`.
+GEMMs and the bias's `sum_rows`.  `scaled_dot_product_attention` records the
+fused attention forward as one op; its backward (`agpu_sdpa_backward`) is the
+reference's SDPA composition (src/ops/attention.rs:149-169) differentiated
+with its matmul and scale rules and the softmax Jacobian.
 
 Gradients are accumulated with `add` into a fresh buffer (:267-279); the
 pass-through gradients of Add, Sub and the broadcast adds share the upstream
@@ -181,6 +184,15 @@ class Tape:
             pre, out = out, self.dev.swish(out)
         return self._push(out, "linear", a=x, b=w, bias=bias, m=m, n=n, k=k, act=act, pre=pre)
 
+    def scaled_dot_product_attention(self, q, k, v, batch_heads: int, seq_len: int, d_k: int,
+                                     causal: bool = False):
+        """softmax(Q K^T / sqrt(d_k)) V per head as one recorded op (the fused
+        forward kernel); gradients for Q, K and V from agpu_sdpa_backward."""
+        f = self.dev.sdpa_causal if causal else self.dev.scaled_dot_product_attention
+        out = f(self.buf(q), self.buf(k), self.buf(v), batch_heads, seq_len, d_k)
+        return self._push(out, "sdpa", q=q, k=k, v=v, bh=batch_heads, s=seq_len, d=d_k,
+                          causal=causal)
+
     # ----------------------------------------------------------- backward --
     def backward(self, loss: TensorId) -> None:
         """Gradients of every recorded tensor w.r.t. the 1-element `loss`
@@ -262,6 +274,12 @@ class Tape:
                 self._accum(a["b"], d.gemm(self.buf(a["a"]), g, 1, k, n, m, trans_a=True))
                 if a["bias"] is not None:
                     self._accum(a["bias"], d.sum_rows(g, m, n))
+            elif e.op == "sdpa":
+                dq, dk, dv = d.sdpa_backward(self.buf(a["q"]), self.buf(a["k"]), self.buf(a["v"]),
+                                             g, a["bh"], a["s"], a["d"], a["causal"])
+                self._accum(a["q"], dq)
+                self._accum(a["k"], dk)
+                self._accum(a["v"], dv)
             else:  # pragma: no cover - every recorded op is handled above
                 raise KeyError(e.op)
 

@@ -564,6 +564,44 @@ extern "C" agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
   return sdpa_impl(dev, q, k, v, bh, s, d, true, out, "sdpa_causal");
 }
 
+extern "C" agpu_status agpu_sdpa_backward(agpu_device* dev, const agpu_buffer* q,
+                                          const agpu_buffer* k, const agpu_buffer* v,
+                                          const agpu_buffer* grad_out, uint32_t bh, uint32_t s,
+                                          uint32_t d, int causal, agpu_buffer** d_q,
+                                          agpu_buffer** d_k, agpu_buffer** d_v) {
+  const char* fn = "sdpa_backward";
+  if (!dev) return fail(AGPU_ERR_INVALID, "%s: NULL device", fn);
+  if (!q || !k || !v || !grad_out) return fail(AGPU_ERR_INVALID, "%s: input is NULL", fn);
+  if (!d_q || !d_k || !d_v) return fail(AGPU_ERR_INVALID, "%s: out is NULL", fn);
+  *d_q = *d_k = *d_v = nullptr;
+  AGPU_CUDA(cudaSetDevice(dev->ordinal));
+  // the forward's checks (each of Q, K, V holds bh*s*d elements), and dO has
+  // the output's shape
+  const uint64_t n = (uint64_t)bh * s * d;
+  if (q->len != n || k->len != n || v->len != n || grad_out->len != n)
+    return fail(AGPU_ERR_SHAPE, "%s: Q/K/V/dO have %llu/%llu/%llu/%llu elems, expected %llu", fn,
+                (unsigned long long)q->len, (unsigned long long)k->len,
+                (unsigned long long)v->len, (unsigned long long)grad_out->len,
+                (unsigned long long)n);
+  agpu_buffer *dq = nullptr, *dk = nullptr, *dv = nullptr;
+  agpu_status st = new_buffer(dev, n, &dq);
+  if (st == AGPU_OK) st = new_buffer(dev, n, &dk);
+  if (st == AGPU_OK) st = new_buffer(dev, n, &dv);
+  if (st == AGPU_OK)
+    st = launch_attention_backward(dev, q->dptr, k->dptr, v->dptr, grad_out->dptr, dq->dptr,
+                                   dk->dptr, dv->dptr, bh, s, d, causal != 0, dev->stream);
+  if (st != AGPU_OK) {
+    agpu_buffer_free(dq);
+    agpu_buffer_free(dk);
+    agpu_buffer_free(dv);
+    return st;
+  }
+  *d_q = dq;
+  *d_k = dk;
+  *d_v = dv;
+  return AGPU_OK;
+}
+
 // ----------------------------------------------------------- elementwise --
 agpu_status agpu_add(agpu_device* d, const agpu_buffer* a, const agpu_buffer* b, agpu_buffer** o) {
   return binary(d, a, b, o, Binary::Add, "add");
@@ -842,6 +880,17 @@ agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k, c
                              void* stream) {
   CHECK_DEV(dev, "launch_sdpa");
   return launch_attention(dev, q, k, v, out, bh, s, d, causal != 0, pick_stream(dev, stream));
+}
+
+agpu_status agpu_launch_sdpa_backward(agpu_device* dev, const float* q, const float* k,
+                                      const float* v, const float* grad_out, float* d_q,
+                                      float* d_k, float* d_v, uint32_t bh, uint32_t s, uint32_t d,
+                                      int causal, void* stream) {
+  CHECK_DEV(dev, "launch_sdpa_backward");
+  if ((!q || !k || !v || !grad_out || !d_q || !d_k || !d_v) && (uint64_t)bh * s * d)
+    return fail(AGPU_ERR_INVALID, "launch_sdpa_backward: NULL pointer");
+  return launch_attention_backward(dev, q, k, v, grad_out, d_q, d_k, d_v, bh, s, d, causal != 0,
+                                   pick_stream(dev, stream));
 }
 
 agpu_status agpu_launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,

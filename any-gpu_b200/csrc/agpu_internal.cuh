@@ -159,6 +159,12 @@ agpu_status launch_attention_strided(agpu_device* dev, const float* q, const flo
 agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
                              cudaStream_t st);
+// dQ, dK, dV of attention from dO (recomputes P; tensor-core GEMMs + two row
+// kernels; scratch from the device pool).
+agpu_status launch_attention_backward(agpu_device* dev, const float* q, const float* k,
+                                      const float* v, const float* dout, float* dq, float* dk,
+                                      float* dv, uint32_t bh, uint32_t s, uint32_t d,
+                                      bool causal, cudaStream_t st);
 
 // conv2d geometry (NCHW); ho/wo already computed.
 struct ConvParams {

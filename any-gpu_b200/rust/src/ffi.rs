@@ -336,6 +336,20 @@ extern "C" {
         d_k: u32,
         out: *mut *mut AgpuBuffer,
     ) -> AgpuStatus;
+    pub fn agpu_sdpa_backward(
+        dev: *mut AgpuDevice,
+        q: *const AgpuBuffer,
+        k: *const AgpuBuffer,
+        v: *const AgpuBuffer,
+        grad_out: *const AgpuBuffer,
+        batch_heads: u32,
+        seq_len: u32,
+        d_k: u32,
+        causal: c_int,
+        d_q: *mut *mut AgpuBuffer,
+        d_k_out: *mut *mut AgpuBuffer,
+        d_v: *mut *mut AgpuBuffer,
+    ) -> AgpuStatus;
     pub fn agpu_rmsnorm(
         dev: *mut AgpuDevice,
         x: *const AgpuBuffer,
@@ -661,6 +675,21 @@ extern "C" {
         batch_heads: u32,
         seq_len: u32,
         d_k: u32,
+        causal: c_int,
+        stream: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_launch_sdpa_backward(
+        dev: *mut AgpuDevice,
+        q: *const f32,
+        k: *const f32,
+        v: *const f32,
+        grad_out: *const f32,
+        d_q: *mut f32,
+        d_k: *mut f32,
+        d_v: *mut f32,
+        batch_heads: u32,
+        seq_len: u32,
+        d_k_dim: u32,
         causal: c_int,
         stream: *mut c_void,
     ) -> AgpuStatus;

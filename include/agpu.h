@@ -281,6 +281,23 @@ AGPU_API agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
                                       uint32_t batch_heads, uint32_t seq_len, uint32_t d_k,
                                       agpu_buffer** out);
 
+/* Gradients of attention: dQ, dK, dV (new buffers, [batch_heads, seq_len,
+ * d_k]) from dO = grad_out, for the non-causal (causal = 0) or causal
+ * forward.  No counterpart in the reference (its tape has no attention
+ * node); the result is its SDPA composition (src/ops/attention.rs:149-169)
+ * differentiated with its own matmul rule (src/autograd.rs:357-366), the
+ * scale rule and the softmax Jacobian: P = softmax(Q K^T / sqrt(d_k)) is
+ * recomputed, dV = P^T dO, dS = P o (dO V^T - rowsum(P o dO V^T)) / sqrt(d_k),
+ * dQ = dS K, dK = dS^T Q.  The products run on the tensor-core GEMMs in the
+ * current precision mode; P and dS use 2 x min(batch_heads, 2^30 / seq_len^2)
+ * x seq_len^2 floats of pool scratch.  Shape checks as the forward. */
+AGPU_API agpu_status agpu_sdpa_backward(agpu_device* dev, const agpu_buffer* q,
+                                        const agpu_buffer* k, const agpu_buffer* v,
+                                        const agpu_buffer* grad_out, uint32_t batch_heads,
+                                        uint32_t seq_len, uint32_t d_k, int causal,
+                                        agpu_buffer** d_q, agpu_buffer** d_k_out,
+                                        agpu_buffer** d_v);
+
 /* ------------------------------------------------- LLaMA-layer ops -------- */
 /* No counterparts in the reference (its ops have no RMSNorm or RoPE); they
  * complete the decoder layer of the benchmark configs from the ops above. */
@@ -446,6 +463,11 @@ AGPU_API agpu_status agpu_launch_group_norm_backward(agpu_device* dev, const flo
 AGPU_API agpu_status agpu_launch_sdpa(agpu_device* dev, const float* q, const float* k,
                                       const float* v, float* out, uint32_t batch_heads,
                                       uint32_t seq_len, uint32_t d_k, int causal, void* stream);
+AGPU_API agpu_status agpu_launch_sdpa_backward(agpu_device* dev, const float* q,
+                                               const float* k, const float* v,
+                                               const float* grad_out, float* d_q, float* d_k,
+                                               float* d_v, uint32_t batch_heads, uint32_t seq_len,
+                                               uint32_t d_k_dim, int causal, void* stream);
 AGPU_API agpu_status agpu_launch_gemm_ex(agpu_device* dev, const float* a, const float* b,
                                          float* c, uint32_t batch, uint32_t m, uint32_t n,
                                          uint32_t k, int trans_a, int trans_b, const float* bias,

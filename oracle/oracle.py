@@ -131,6 +131,50 @@ def attention(q, k, v, bh, seq, dk, threads: bool = False, causal: bool = False)
     return out
 
 
+def attention_backward(q, k, v, dout, bh, seq, dk, causal: bool = False):
+    """dQ, dK, dV of attention: the reference's SDPA composition
+    (src/ops/attention.rs:149-169: kt = transpose(K); scores = batch_matmul(Q,
+    kt); scaled = scale(scores, 1/sqrt(dk)); attn = softmax(scaled); out =
+    batch_matmul(attn, V)) differentiated in reverse with its own rules: the
+    matmul rule of src/autograd.rs:357-366 (dA = dC B^T, dB = A^T dC, through
+    transposes), the scale rule (:317-320) and the softmax Jacobian-vector
+    product dx = y * (dy - sum(y * dy)) per row (the reference's tape has no
+    softmax node; this is the derivative of cpu_softmax).  Per head, with
+    cpu_matmul / cpu_softmax / transpose from the C restatement; the causal
+    variant masks scaled scores above the diagonal to -inf before softmax."""
+    q, k, v, dout = _a(q), _a(k), _a(v), _a(dout)
+    c = np.float32(1.0 / np.sqrt(np.float32(dk)))
+    hs = seq * dk
+    dq, dkk, dv = (np.empty(bh * hs, np.float32) for _ in range(3))
+    for h in range(bh):
+        sl = slice(h * hs, (h + 1) * hs)
+        qh, kh, vh, doh = q[sl], k[sl], v[sl], dout[sl]
+        kt = transpose(kh, 1, seq, dk, 1)                       # [dk, seq]
+        scores = matmul(qh, kt, seq, seq, dk)
+        scaled = elementwise("scale", scores, None, float(c))
+        if causal:
+            sc = scaled.reshape(seq, seq)
+            sc[np.triu_indices(seq, 1)] = -np.inf
+        attn = softmax(scaled, seq, seq)
+        # out = attn @ V
+        vt = transpose(vh, 1, seq, dk, 1)
+        d_attn = matmul(doh, vt, seq, seq, dk)                  # dO V^T
+        at = transpose(attn, 1, seq, seq, 1)
+        dv[sl] = matmul(at, doh, seq, dk, seq)                  # attn^T dO
+        # attn = softmax(scaled)
+        y, dy = attn.reshape(seq, seq), d_attn.reshape(seq, seq)
+        rows = np.sum(y * dy, axis=1, dtype=np.float32, keepdims=True)
+        d_scaled = (y * (dy - rows)).astype(np.float32).reshape(-1)
+        d_scores = elementwise("scale", d_scaled, None, float(c))
+        # scores = Q @ kt
+        ktt = transpose(kt, 1, dk, seq, 1)                      # kt^T = K
+        dq[sl] = matmul(d_scores, ktt, seq, dk, seq)
+        qt = transpose(qh, 1, seq, dk, 1)
+        d_kt = matmul(qt, d_scores, dk, seq, seq)               # Q^T dS  [dk, seq]
+        dkk[sl] = transpose(d_kt, 1, dk, seq, 1)                # back through transpose(K)
+    return dq, dkk, dv
+
+
 def conv_out(n, k, stride, pad, dil) -> int:
     return int(lib().oracle_conv_out(n, k, stride, pad, dil))
 

@@ -67,6 +67,16 @@ class OracleDevice:
             c = self.add_per_col(c, bias, m, n)
         return self.relu(c) if act == 2 else c
 
+    def scaled_dot_product_attention(self, q, k, v, bh, s, d):
+        return OracleBuffer(self.o.attention(q.data, k.data, v.data, bh, s, d))
+
+    def sdpa_causal(self, q, k, v, bh, s, d):
+        return OracleBuffer(self.o.attention(q.data, k.data, v.data, bh, s, d, causal=True))
+
+    def sdpa_backward(self, q, k, v, go, bh, s, d, causal=False):
+        return tuple(OracleBuffer(x) for x in self.o.attention_backward(
+            q.data, k.data, v.data, go.data, bh, s, d, causal=causal))
+
     def mse_loss(self, p, t):
         return OracleBuffer(self.o.mse_loss(p.data, t.data))
 

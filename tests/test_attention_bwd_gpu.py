@@ -1,0 +1,92 @@
+"""GPU parity of the attention backward (agpu_sdpa_backward) through the C ABI.
+
+Against the oracle's restatement of the reference's SDPA composition
+differentiated with its own rules (oracle.attention_backward), in TF32
+(rel. Frobenius <= 1e-3) and in 3xTF32 / FFMA against float64 (<= 1e-5);
+at the SDPA benchmark size (B8 H32 S2048 D128), sampled heads against
+float64."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(got, want):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    return float(np.linalg.norm(got - want) / np.linalg.norm(want))
+
+
+def _f64_backward(q, k, v, do, s, d, causal):
+    """dQ, dK, dV of one head in float64."""
+    Q, K, V, dO = (x.reshape(s, d).astype(np.float64) for x in (q, k, v, do))
+    sc = Q @ K.T / np.sqrt(d)
+    if causal:
+        sc[np.triu_indices(s, 1)] = -np.inf
+    P = np.exp(sc - sc.max(axis=1, keepdims=True))
+    P /= P.sum(axis=1, keepdims=True)
+    dV = P.T @ dO
+    dP = dO @ V.T
+    dS = P * (dP - (P * dP).sum(axis=1, keepdims=True)) / np.sqrt(d)
+    return dS @ K, dS.T @ Q, dV
+
+
+def _inputs(bh, s, d, seed):
+    r = np.random.default_rng(seed)
+    return [r.standard_normal(bh * s * d).astype(np.float32) for _ in range(4)]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("bh,s,d", [(4, 256, 128), (3, 200, 64), (2, 130, 64), (1, 512, 128)])
+def test_sdpa_backward_tf32_vs_oracle(dev, orc, bh, s, d, causal):
+    q, k, v, do = _inputs(bh, s, d, bh * s + d + causal)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d, causal=causal)]
+    want = orc.attention_backward(q, k, v, do, bh, s, d, causal=causal)
+    for name, a, b in zip(("dq", "dk", "dv"), got, want):
+        assert _rel(a, b) <= 1e-3, (name, _rel(a, b))
+
+
+@pytest.mark.parametrize("prec", ["tf32x3", "ffma"])
+def test_sdpa_backward_fp32_modes_vs_float64(dev, orc, prec):
+    from any_gpu import GpuDevice
+    bh, s, d = 2, 256, 64
+    q, k, v, do = _inputs(bh, s, d, 5)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    with GpuDevice.precision(prec):
+        got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d)]
+    hs = s * d
+    for h in range(bh):
+        sl = slice(h * hs, (h + 1) * hs)
+        want = _f64_backward(q[sl], k[sl], v[sl], do[sl], s, d, False)
+        for name, a, w in zip(("dq", "dk", "dv"), got, want):
+            assert _rel(a[sl], w) <= 1e-5, (prec, h, name, _rel(a[sl], w))
+
+
+def test_sdpa_backward_benchmark_size_sampled(dev):
+    """B8 H32 S2048 D128 (the SDPA benchmark config): three heads against
+    float64 (P and dS scratch: 2 x 4 GiB in head chunks)."""
+    bh, s, d = 256, 2048, 128
+    q, k, v, do = _inputs(bh, s, d, 77)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d)]
+    hs = s * d
+    for h in (0, 131, 255):
+        sl = slice(h * hs, (h + 1) * hs)
+        want = _f64_backward(q[sl], k[sl], v[sl], do[sl], s, d, False)
+        for name, a, w in zip(("dq", "dk", "dv"), got, want):
+            assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
+
+
+def test_sdpa_backward_errors(dev):
+    from any_gpu import AnyGpuError
+    q = dev.upload(np.zeros(2 * 8 * 4, np.float32))
+    bad = dev.upload(np.zeros(10, np.float32))
+    with pytest.raises(AnyGpuError) as e:
+        dev.sdpa_backward(q, q, q, bad, 2, 8, 4)
+    assert e.value.status == 1
+    with pytest.raises(AnyGpuError) as e:
+        dev.sdpa_backward(q, bad, q, q, 2, 8, 4)
+    assert e.value.status == 1

@@ -320,3 +320,60 @@ def test_linear_rejects_unsupported_activation(new_tape):
     x, w = tape.leaf(np.ones(4, np.float32)), tape.leaf(np.ones(4, np.float32))
     with pytest.raises(ValueError):
         tape.linear(x, w, None, 2, 2, 2, act="tanh")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec,tol", [("tf32", 1e-3), ("tf32x3", 1e-5), ("ffma", 1e-5)])
+@pytest.mark.parametrize("act", ["none", "relu", "swish"])
+def test_linear_fused_epilogue_precisions_vs_oracle(dev, orc, prec, tol, act):
+    """`Tape.linear` on the GPU at a size that takes the tensor-core pair /
+    split-K kernels (fused bias + ReLU in their epilogue), in every precision
+    mode, against the same graph on the oracle device."""
+    from any_gpu import GpuDevice
+    from any_gpu.autograd import Tape
+    m, n, k = 512, 384, 640
+    r = np.random.default_rng(23)
+    xv = r.standard_normal(m * k).astype(np.float32)
+    wv = (r.standard_normal(k * n) / np.sqrt(k)).astype(np.float32)
+    bv = r.standard_normal(n).astype(np.float32)
+    tv = r.standard_normal(m * n).astype(np.float32)
+
+    def run(tape):
+        x, w, b = tape.leaf(xv), tape.leaf(wv), tape.leaf(bv)
+        y = tape.linear(x, w, b, m, n, k, act)
+        tape.backward(tape.mse_loss(y, tape.leaf(tv)))
+        return [tape.read(y), tape.read_grad(x), tape.read_grad(w), tape.read_grad(b)]
+
+    with GpuDevice.precision(prec):
+        got = run(Tape(dev))
+    want = run(_cpu_tape(orc)())
+    for g, w_, name in zip(got, want, ("y", "dx", "dw", "db")):
+        assert orc.rel_fro(g, w_) <= tol, (prec, act, name, orc.rel_fro(g, w_))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_tape_attention_backward(new_tape, causal):
+    """`Tape.scaled_dot_product_attention` + mse_loss: forward and Q/K/V
+    gradients against float64 autograd (oracle device and GPU; TF32
+    tolerance on the GPU)."""
+    import torch
+    bh, s, d = 2, 64, 64
+    r = np.random.default_rng(31 + causal)
+    qv, kv, vv, tv = (r.standard_normal(bh * s * d).astype(np.float32) for _ in range(4))
+    tape = new_tape()
+    q, k, v = tape.leaf(qv), tape.leaf(kv), tape.leaf(vv)
+    o = tape.scaled_dot_product_attention(q, k, v, bh, s, d, causal=causal)
+    tape.backward(tape.mse_loss(o, tape.leaf(tv)))
+    Q, K, V = (torch.tensor(x.reshape(bh, s, d), dtype=torch.float64, requires_grad=True)
+               for x in (qv, kv, vv))
+    sc = Q @ K.transpose(1, 2) / np.sqrt(d)
+    if causal:
+        sc = sc.masked_fill(torch.ones(s, s, dtype=torch.bool).triu(1), float("-inf"))
+    out = torch.softmax(sc, -1) @ V
+    ((out - torch.tensor(tv.reshape(bh, s, d), dtype=torch.float64)) ** 2).mean().backward()
+    tol = 1e-3 if hasattr(tape.dev, "launch_count") else 1e-5
+    ow = out.detach().numpy().ravel()
+    assert np.linalg.norm(tape.read(o) - ow) / np.linalg.norm(ow) < tol
+    for t, w in ((q, Q.grad), (k, K.grad), (v, V.grad)):
+        w = w.numpy().ravel()
+        assert np.linalg.norm(tape.read_grad(t) - w) / np.linalg.norm(w) < tol

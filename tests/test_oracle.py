@@ -228,3 +228,24 @@ def test_oracle_tape_ops_vs_numpy(orc):
     t = r.standard_normal(a.size).astype(np.float32)
     d = a.ravel().astype(np.float64) - t
     np.testing.assert_allclose(orc.mse_loss(a, t)[0], (d * d).mean(), rtol=1e-5)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_oracle_attention_backward_matches_float64(orc, causal):
+    """The oracle's attention backward (the reference's SDPA composition
+    differentiated with its own matmul / scale rules and the softmax Jacobian)
+    against float64 autograd of the same function."""
+    import torch
+    bh, s, d = 3, 40, 16
+    r = np.random.default_rng(8 + causal)
+    q, k, v, do = (r.standard_normal(bh * s * d).astype(np.float32) for _ in range(4))
+    got = orc.attention_backward(q, k, v, do, bh, s, d, causal=causal)
+    Q, K, V = (torch.tensor(x.reshape(bh, s, d), dtype=torch.float64, requires_grad=True)
+               for x in (q, k, v))
+    sc = Q @ K.transpose(1, 2) / np.sqrt(d)
+    if causal:
+        sc = sc.masked_fill(torch.ones(s, s, dtype=torch.bool).triu(1), float("-inf"))
+    (torch.softmax(sc, -1) @ V).backward(torch.tensor(do.reshape(bh, s, d), dtype=torch.float64))
+    for g, w in zip(got, (Q.grad, K.grad, V.grad)):
+        w = w.numpy().ravel()
+        assert np.linalg.norm(g - w) / np.linalg.norm(w) < 1e-5
