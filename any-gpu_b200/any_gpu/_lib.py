@@ -127,6 +127,15 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_launch_softmax": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, u32, C.c_void_p]),
     "agpu_group_norm_noalloc": (c_status, [C.c_void_p] * 4 + [u32, u32, u32, u32, f32, i32,
                                                               C.c_void_p]),
+    "agpu_ipc_export": (c_status, [c_dev, C.c_void_p, C.c_void_p, C.POINTER(u64)]),
+    "agpu_ipc_import": (c_status, [c_dev, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "agpu_ipc_close": (c_status, [c_dev, C.c_void_p]),
+    "agpu_ipc_event_create": (c_status, [c_dev, C.POINTER(C.c_void_p), C.c_void_p]),
+    "agpu_ipc_event_import": (c_status, [c_dev, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "agpu_event_destroy": (c_status, [c_dev, C.c_void_p]),
+    "agpu_event_record": (c_status, [c_dev, C.c_void_p, C.c_void_p]),
+    "agpu_stream_wait_event": (c_status, [c_dev, C.c_void_p, C.c_void_p]),
+    "agpu_copy_async": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, C.c_void_p]),
     "agpu_selftest_wait_timeout": (c_status, [c_dev, u32, C.c_void_p]),
 }
 

@@ -9,6 +9,11 @@ all-gathered in place (NCCL over NVLink on GPUs, gloo on CPU), so that every
 rank ends with the whole result and nothing is padded, copied or
 concatenated.
 
+Gathers.  PeerGather pushes each finished round into every peer's copy of
+the output with the copy engines over CUDA IPC (no SMs, so it overlaps the
+persistent contraction kernels); NcclGather runs the in-place NCCL
+collectives instead.
+
 Rounds.  To overlap the gather with compute, the items are cut into
 `rounds` consecutive spans; inside each span every rank owns one
 contiguous run, in rank order.  A span's output is then one contiguous
@@ -120,29 +125,139 @@ def gather_round(out, item_elems: int, rd: Round, rank: int, group=None,
     return works
 
 
-def run_rounds(plan: ShardPlan, out, item_elems: int,
-               launch_round: Callable[[Round], object], stream, group=None,
-               gather: bool = True) -> None:
+class NcclGather:
+    """Round gathers as in-place NCCL collectives (gather_round), each issued
+    from the stream on which its round's output is complete, so NCCL's stream
+    starts it as soon as the round is done."""
+    kind = "nccl"
+
+    def __init__(self, plan: ShardPlan, out, item_elems: int, group=None):
+        self.plan, self.out, self.ie, self.group = plan, out, item_elems, group
+        self._works: list = []
+
+    def round(self, rd: Round, ready) -> None:
+        import torch
+        with torch.cuda.stream(ready):
+            self._works += gather_round(self.out, self.ie, rd, self.plan.rank, self.group,
+                                        async_op=True)
+
+    def finish(self, stream) -> None:
+        import torch
+        with torch.cuda.stream(stream):
+            for w in self._works:
+                w.wait()
+        self._works = []
+
+    def close(self) -> None:
+        pass
+
+
+class PeerGather:
+    """Round gathers on the copy engines: every rank pushes its run of each
+    finished round straight into the same slot of every peer's output over
+    NVLink (agpu_copy_async into the peer's buffer, mapped with CUDA IPC),
+    one copy stream per peer, so the pushes use no SMs and run beside the next
+    round's kernels.  At the end of a step each rank records an interprocess
+    event after its pushes, the ranks meet at a host barrier (`host_group`, a
+    gloo group: no device work), and each rank's stream waits on every peer's
+    event -- after which every rank holds the whole output.  Uneven runs need
+    no special case.  `out` must come from cudaMalloc (torch's default
+    allocator does)."""
+    kind = "ce"
+
+    def __init__(self, dev, plan: ShardPlan, out, item_elems: int, host_group):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _check, _lib
+        self.lib, self._check = _lib.load(), _check
+        self.dev, self.plan, self.out, self.ie = dev, plan, out, item_elems
+        self.group = host_group
+        lib, h = self.lib, dev.handle
+        mem, off = (C.c_ubyte * 64)(), C.c_uint64()
+        _check(lib.agpu_ipc_export(h, out.data_ptr(), mem, C.byref(off)))
+        ev, evh = C.c_void_p(), (C.c_ubyte * 64)()
+        _check(lib.agpu_ipc_event_create(h, C.byref(ev), evh))
+        self.event = ev
+        world, rank = plan.world, plan.rank
+        table = [None] * world
+        dist.all_gather_object(table, (bytes(mem), off.value, bytes(evh)), group=host_group)
+        self.peers = []  # (rank, base, dst pointer of the peer's out, event)
+        for p in range(world):
+            if p == rank:
+                continue
+            mb, poff, eb = table[p]
+            base, pev = C.c_void_p(), C.c_void_p()
+            _check(lib.agpu_ipc_import(h, (C.c_ubyte * 64).from_buffer_copy(mb), C.byref(base)))
+            _check(lib.agpu_ipc_event_import(h, (C.c_ubyte * 64).from_buffer_copy(eb),
+                                             C.byref(pev)))
+            self.peers.append((p, base, base.value + poff, pev))
+        self.streams = [torch.cuda.Stream() for _ in self.peers]
+
+    def round(self, rd: Round, ready) -> None:
+        import torch
+        n = rd.counts[self.plan.rank]
+        if n == 0:
+            return
+        ev = torch.cuda.Event()
+        ev.record(ready)
+        nbytes = 4 * n * self.ie
+        off = 4 * rd.offsets[self.plan.rank] * self.ie
+        src = self.out.data_ptr() + off
+        for (_, _, dst, _), cs in zip(self.peers, self.streams):
+            cs.wait_event(ev)
+            self._check(self.lib.agpu_copy_async(self.dev.handle, dst + off, src, nbytes,
+                                                 cs.cuda_stream))
+
+    def finish(self, stream) -> None:
+        import torch.distributed as dist
+        for cs in self.streams:
+            stream.wait_stream(cs)
+        h = self.dev.handle
+        self._check(self.lib.agpu_event_record(h, self.event, stream.cuda_stream))
+        dist.barrier(group=self.group)  # every rank's record is issued
+        for _, _, _, pev in self.peers:
+            self._check(self.lib.agpu_stream_wait_event(h, stream.cuda_stream, pev))
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after every rank's pushes are done)."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        h = self.dev.handle
+        for _, base, _, pev in self.peers:
+            self.lib.agpu_event_destroy(h, pev)
+            self.lib.agpu_ipc_close(h, base)
+        self.lib.agpu_event_destroy(h, self.event)
+        self.peers = []
+        dist.barrier(group=self.group)
+
+
+def run_rounds(plan: ShardPlan, launch_round: Callable[[Round], object], stream,
+               gatherer=None) -> None:
     """One sharded step on the GPU: for each round, `launch_round(rd)` enqueues
-    this rank's part of the round (writing its slot of `out`) and returns
-    the torch CUDA stream on which that output is complete; the round's
-    in-place gather is issued from that stream, so it starts as soon as the
-    round is done and runs beside the next round's compute.  On return
-    `stream` waits for every launch and gather (nothing blocks the host)."""
-    import torch
-    works, ready_streams = [], []
+    this rank's part of the round (writing its slots of the output) and
+    returns the torch CUDA stream on which that output is complete; the
+    gatherer (NcclGather or PeerGather; None: no gather) starts that round's
+    gather from there, so it runs beside the next round's compute.  On return
+    `stream` waits for every launch and gather (nothing blocks the host but
+    the PeerGather host barrier)."""
+    ready_streams = []
     for rd in plan.spans:
         ready = launch_round(rd)
-        if ready is not None and ready is not stream:
+        if ready is None:
+            ready = stream
+        if ready is not stream:
             ready_streams.append(ready)
-        if gather and plan.world > 1:
-            with torch.cuda.stream(ready if ready is not None else stream):
-                works += gather_round(out, item_elems, rd, plan.rank, group, async_op=True)
-    with torch.cuda.stream(stream):
-        for s in ready_streams:
-            stream.wait_stream(s)
-        for w in works:
-            w.wait()
+        if gatherer is not None and plan.world > 1:
+            gatherer.round(rd, ready)
+    for s in ready_streams:
+        stream.wait_stream(s)
+    if gatherer is not None and plan.world > 1:
+        gatherer.finish(stream)
 
 
 def all_gather_shards(local, total: int, item_elems: int, group=None):

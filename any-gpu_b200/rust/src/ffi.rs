@@ -37,6 +37,13 @@ pub struct AgpuBuffer {
     _private: [u8; 0],
 }
 
+/// `agpu_ipc_handle`: a CUDA IPC handle of memory or of an event, as bytes.
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct AgpuIpcHandle {
+    pub bytes: [u8; 64],
+}
+
 /// `agpu_attn_layout`: element strides of one attention operand.
 #[repr(C)]
 #[derive(Clone, Copy, Debug, Default)]
@@ -779,6 +786,46 @@ extern "C" {
         groups: u32,
         eps: f32,
         apply_swish: c_int,
+        stream: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_ipc_export(
+        dev: *mut AgpuDevice,
+        dptr: *const c_void,
+        handle: *mut AgpuIpcHandle,
+        offset: *mut u64,
+    ) -> AgpuStatus;
+    pub fn agpu_ipc_import(
+        dev: *mut AgpuDevice,
+        handle: *const AgpuIpcHandle,
+        base: *mut *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_ipc_close(dev: *mut AgpuDevice, base: *mut c_void) -> AgpuStatus;
+    pub fn agpu_ipc_event_create(
+        dev: *mut AgpuDevice,
+        event: *mut *mut c_void,
+        handle: *mut AgpuIpcHandle,
+    ) -> AgpuStatus;
+    pub fn agpu_ipc_event_import(
+        dev: *mut AgpuDevice,
+        handle: *const AgpuIpcHandle,
+        event: *mut *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_event_destroy(dev: *mut AgpuDevice, event: *mut c_void) -> AgpuStatus;
+    pub fn agpu_event_record(
+        dev: *mut AgpuDevice,
+        event: *mut c_void,
+        stream: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_stream_wait_event(
+        dev: *mut AgpuDevice,
+        stream: *mut c_void,
+        event: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_copy_async(
+        dev: *mut AgpuDevice,
+        dst: *mut c_void,
+        src: *const c_void,
+        bytes: u64,
         stream: *mut c_void,
     ) -> AgpuStatus;
     pub fn agpu_selftest_wait_timeout(

@@ -60,7 +60,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "any-gpu_b200"))
 sys.path.insert(0, str(ROOT))
 
-from any_gpu.dist import ShardPlan, gather_round, run_rounds  # noqa: E402
+from any_gpu.dist import NcclGather, PeerGather, ShardPlan, run_rounds  # noqa: E402
 
 METRIC = "TFLOPS (matmul, SDPA) and GB/s (softmax/norm) at 1/2/4/8 B200, % of roofline"
 
@@ -227,6 +227,8 @@ class Workload:
         cfg.update({"parallelism": self.parallelism(), "l2": self.l2,
                     "items": f"{self.total} {self.item}s",
                     "rounds": len(self.plan.spans) if self.sharded else 1})
+        if self.sharded:
+            cfg["gather"] = self.args.comm
         return cfg
 
     # ---- data
@@ -257,8 +259,19 @@ class Workload:
                                     pin_memory=True)
         self.aux = torch.cuda.Stream(device=local)
 
+    def make_gatherer(self, dev, ctx):
+        """The round gatherer of a sharded step: copy-engine pushes over CUDA
+        IPC (`--comm ce`, default) or in-place NCCL collectives (`--comm nccl`)."""
+        self.gatherer = None
+        if self.sharded:
+            self.gatherer = (PeerGather(dev, self.plan, self.out, self.out_item, ctx.host_group)
+                             if ctx.args.comm == "ce" else
+                             NcclGather(self.plan, self.out, self.out_item))
+
     def teardown(self):
-        for k in ("host", "d", "out", "out_host", "aux", "_pipe", "_scratch"):
+        if getattr(self, "gatherer", None) is not None:
+            self.gatherer.close()
+        for k in ("host", "d", "out", "out_host", "aux", "_pipe", "_scratch", "gatherer"):
             if hasattr(self, k):
                 delattr(self, k)
 
@@ -275,12 +288,11 @@ class Workload:
         raise NotImplementedError
 
     def step(self, dev, stream, gather=True):
-        run_rounds(self.plan, self.out, self.out_item,
-                   lambda rd: self.launch_round(dev, rd, stream), stream,
-                   gather=gather and self.sharded)
+        run_rounds(self.plan, lambda rd: self.launch_round(dev, rd, stream), stream,
+                   self.gatherer if gather else None)
 
     def gather_only(self, stream):
-        run_rounds(self.plan, self.out, self.out_item, lambda rd: stream, stream)
+        run_rounds(self.plan, lambda rd: stream, stream, self.gatherer)
 
     def dom_step(self, dev, stream):
         raise NotImplementedError
@@ -927,6 +939,13 @@ class Ctx:
         import torch
         self.torch, self.args, self.world, self.rank, self.local = torch, args, world, rank, local
         self.peaks = load_peaks()
+        self.host_group = None
+        if world > 1:
+            import torch.distributed as dist
+            # host-side exchange and barriers of the copy-engine gathers (no
+            # device work, so they never wait behind queued kernels)
+            self.host_group = dist.new_group(backend="gloo",
+                                             timeout=datetime.timedelta(seconds=180))
 
     def barrier(self):
         if self.world > 1:
@@ -955,6 +974,7 @@ def measure(ctx: Ctx, wl: Workload, cpu_seconds: float, cpu_single: float, e2e_s
     stream = torch.cuda.Stream(device=ctx.local)
     torch.cuda.set_stream(stream)
     wl.setup(torch, ctx.local)
+    wl.make_gatherer(dev, ctx)
     prec = GpuDevice.precision(wl.precision) if wl.precision != "tf32" else \
         contextlib.nullcontext()
     try:
@@ -1097,10 +1117,16 @@ def _measure(ctx, wl, dev, stream, cpu_seconds, cpu_single, e2e_steps, steps, wa
                                 "outputs down over its own PCIe link (no gather)")
     if wl.sharded:
         recv = (wl.total - wl.local) * wl.out_item * 4
+        if ctx.args.comm == "ce":
+            how = ("copy-engine pushes over CUDA IPC: each rank copies its run of every round "
+                   "into every peer's output (agpu_copy_async, one stream per peer, no SMs), "
+                   "then interprocess events + a host barrier end the step")
+        elif all(r.even for r in wl.plan.spans):
+            how = "in-place all_gather_into_tensor (ncclAllGather over NVLink) per round"
+        else:
+            how = "in-place broadcast per rank (uneven runs)"
         entry["comm"] = {
-            "collective": ("in-place all_gather_into_tensor (ncclAllGather over NVLink) per "
-                           "round" if all(r.even for r in wl.plan.spans) else
-                           "in-place broadcast per rank (uneven runs)"),
+            "collective": how, "comm": ctx.args.comm,
             "rounds": len(wl.plan.spans), "recv_bytes_per_rank": recv,
             "gather_ms": gather_ms, "compute_ms": compute_ms,
             "exposed_gather_ms": ms_per_step - compute_ms,
@@ -1166,6 +1192,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bmm_softmax")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: every rank runs the whole config, no collective (weak)")
+    ap.add_argument("--comm", choices=["ce", "nccl"], default="ce",
+                    help="N > 1 output gathers: copy engines over CUDA IPC, or NCCL collectives")
     ap.add_argument("--no-workloads", action="store_true",
                     help="headline only (no `workloads` object)")
     ap.add_argument("--e2e-steps", type=int, default=5)

@@ -524,6 +524,43 @@ AGPU_API agpu_status agpu_group_norm_noalloc(const float* x, const float* gamma,
                                              uint32_t groups, float eps, int apply_swish,
                                              void* stream);
 
+/* ------------------------------------------- peer memory (multi-GPU) ----- */
+/* No counterpart in the reference (it has no multi-GPU code).  For sharded
+ * jobs with one process per GPU of a node: a rank shares its output buffer
+ * and an event with its peers through CUDA IPC, then pushes each finished
+ * part of its results into every peer's copy of the buffer with
+ * agpu_copy_async (copy engines over NVLink, no SMs), records its event after
+ * the pushes, and -- once every rank has issued its record (a host barrier)
+ * -- makes its stream wait on every peer's event.  Handles are plain bytes,
+ * exchanged by the caller (e.g. over torch.distributed or a socket). */
+typedef struct agpu_ipc_handle {
+  unsigned char bytes[64];
+} agpu_ipc_handle;
+/* Handle of the allocation holding `dptr` (memory from cudaMalloc, torch's
+ * default allocator included; pool memory cannot be shared ->
+ * AGPU_ERR_UNSUPPORTED) and dptr's byte offset inside it. */
+AGPU_API agpu_status agpu_ipc_export(agpu_device* dev, const void* dptr, agpu_ipc_handle* handle,
+                                     uint64_t* offset);
+/* Map a peer's allocation into this process; *base + offset is the peer's
+ * dptr.  agpu_ipc_close unmaps it (every copy into it must be complete). */
+AGPU_API agpu_status agpu_ipc_import(agpu_device* dev, const agpu_ipc_handle* handle,
+                                     void** base);
+AGPU_API agpu_status agpu_ipc_close(agpu_device* dev, void* base);
+/* An interprocess event (no timing) and its handle; a peer's copy from
+ * agpu_ipc_event_import.  Both are released with agpu_event_destroy. */
+AGPU_API agpu_status agpu_ipc_event_create(agpu_device* dev, void** event,
+                                           agpu_ipc_handle* handle);
+AGPU_API agpu_status agpu_ipc_event_import(agpu_device* dev, const agpu_ipc_handle* handle,
+                                           void** event);
+AGPU_API agpu_status agpu_event_destroy(agpu_device* dev, void* event);
+/* cudaEventRecord / cudaStreamWaitEvent (stream NULL = the device stream). */
+AGPU_API agpu_status agpu_event_record(agpu_device* dev, void* event, void* stream);
+AGPU_API agpu_status agpu_stream_wait_event(agpu_device* dev, void* stream, void* event);
+/* Stream-ordered device-to-device copy of `bytes` (either side may be a
+ * peer's memory from agpu_ipc_import). */
+AGPU_API agpu_status agpu_copy_async(agpu_device* dev, void* dst, const void* src, uint64_t bytes,
+                                     void* stream);
+
 /* ---------------------------------------------------- failure self-test -- */
 /* No counterpart in the reference.  Exercises the failure path of the
  * bounded device-side waits without faulting or hanging anything: launches

@@ -5,7 +5,8 @@ all-gathered in place (any_gpu.dist.run_rounds).  Checked: every rank holds
 the same bytes, and the whole result matches the oracle.  Covers batch_matmul
 + softmax in two rounds (GEMMs on one stream, softmaxes on another), an
 uneven split (5 items over 2 ranks: in-place broadcasts), and attention
-sharded by heads."""
+sharded by heads -- each through both gatherers: copy-engine pushes over CUDA
+IPC (PeerGather) and in-place NCCL collectives (NcclGather)."""
 from __future__ import annotations
 
 import os
@@ -42,13 +43,14 @@ def _worker(rank, world, port, q):
     import torch
     import torch.distributed as dist
     from any_gpu import GpuDevice
-    from any_gpu.dist import ShardPlan, run_rounds
+    from any_gpu.dist import NcclGather, PeerGather, ShardPlan, run_rounds
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", rank))
+        host = dist.new_group(backend="gloo")
         dev = GpuDevice.gpu(rank)
         stream = torch.cuda.Stream()
         aux = torch.cuda.Stream()
@@ -67,9 +69,8 @@ def _worker(rank, world, port, q):
                                                  for g in items])).cuda()
             B = torch.from_numpy(np.concatenate([b[g * k * n:(g + 1) * k * n]
                                                  for g in items])).cuda()
-            out = torch.full((batch * m * n,), float("nan"), device="cuda")
 
-            def launch(rd):
+            def launch(rd, out):
                 cnt = rd.counts[rank]
                 c = out.data_ptr() + 4 * rd.offsets[rank] * m * n
                 dev.launch_batch_matmul(A.data_ptr() + 4 * rd.local * m * k,
@@ -80,9 +81,18 @@ def _worker(rank, world, port, q):
                 aux.wait_event(ev)
                 dev.launch_softmax(c, c, cnt * m, n, aux.cuda_stream)
                 return aux
-            run_rounds(plan, out, m * n, launch, stream)
-            stream.synchronize()
-            results[f"bmm{batch}"] = (out.cpu().numpy(), a, b)
+            for kind in ("nccl", "ce"):
+                out = torch.full((batch * m * n,), float("nan"), device="cuda")
+                g = NcclGather(plan, out, m * n) if kind == "nccl" else \
+                    PeerGather(dev, plan, out, m * n, host)
+                for _ in range(2):  # twice: the second step reuses the events and mappings
+                    out.fill_(float("nan"))
+                    stream.synchronize()
+                    dist.barrier(group=host)
+                    run_rounds(plan, lambda rd: launch(rd, out), stream, g)
+                stream.synchronize()
+                g.close()
+                results[f"bmm{batch}_{kind}"] = (out.cpu().numpy(), a, b)
 
         # attention, heads split over the ranks in one round
         bh, s, d = 6, 256, 128
@@ -91,15 +101,20 @@ def _worker(rank, world, port, q):
         plan = ShardPlan(bh, world, rank, 1)
         st, cnt = plan.spans[0].offsets[rank], plan.spans[0].counts[rank]
         Q, K, V = (torch.from_numpy(x[st * s * d:(st + cnt) * s * d]).cuda() for x in qkv)
-        O = torch.full((bh * s * d,), float("nan"), device="cuda")
+        for kind in ("nccl", "ce"):
+            O = torch.full((bh * s * d,), float("nan"), device="cuda")
 
-        def launch_attn(rd):
-            dev.launch_sdpa(Q.data_ptr(), K.data_ptr(), V.data_ptr(),
-                            O.data_ptr() + 4 * st * s * d, cnt, s, d, False, stream.cuda_stream)
-            return stream
-        run_rounds(plan, O, s * d, launch_attn, stream)
-        stream.synchronize()
-        results["sdpa"] = (O.cpu().numpy(), *qkv)
+            def launch_attn(rd):
+                dev.launch_sdpa(Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                O.data_ptr() + 4 * st * s * d, cnt, s, d, False,
+                                stream.cuda_stream)
+                return stream
+            g = NcclGather(plan, O, s * d) if kind == "nccl" else \
+                PeerGather(dev, plan, O, s * d, host)
+            run_rounds(plan, launch_attn, stream, g)
+            stream.synchronize()
+            g.close()
+            results[f"sdpa_{kind}"] = (O.cpu().numpy(), *qkv)
         dev.synchronize()
         q.put((rank, results, None))
         torch.cuda.synchronize()
@@ -126,12 +141,15 @@ def test_two_gpu_sharded_rounds_gather_in_place(orc):
         assert err is None, f"rank {rank}: {err}"
     r0, r1 = res[0][1], res[1][1]
     m, n, k = 256, 512, 384
-    for batch in (8, 5):
-        got0, a, b = r0[f"bmm{batch}"]
-        got1 = r1[f"bmm{batch}"][0]
-        assert np.array_equal(got0, got1), f"bmm{batch}: ranks hold different results"
-        want = orc.softmax(orc.batch_matmul(a, b, batch, m, n, k), batch * m, n)
-        assert orc.rel_fro(got0, want) <= 1e-3
-    got0, qh, kh, vh = r0["sdpa"]
-    assert np.array_equal(got0, r1["sdpa"][0])
-    assert orc.rel_fro(got0, orc.attention(qh, kh, vh, 6, 256, 128)) <= 1e-3
+    for kind in ("nccl", "ce"):
+        for batch in (8, 5):
+            got0, a, b = r0[f"bmm{batch}_{kind}"]
+            got1 = r1[f"bmm{batch}_{kind}"][0]
+            assert np.array_equal(got0, got1), f"bmm{batch} {kind}: ranks hold different results"
+            want = orc.softmax(orc.batch_matmul(a, b, batch, m, n, k), batch * m, n)
+            assert orc.rel_fro(got0, want) <= 1e-3, kind
+        got0, qh, kh, vh = r0[f"sdpa_{kind}"]
+        assert np.array_equal(got0, r1[f"sdpa_{kind}"][0]), kind
+        assert orc.rel_fro(got0, orc.attention(qh, kh, vh, 6, 256, 128)) <= 1e-3, kind
+    # both gatherers move the same bytes
+    assert np.array_equal(r0["bmm8_nccl"][0], r0["bmm8_ce"][0])
