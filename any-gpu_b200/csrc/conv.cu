@@ -529,66 +529,6 @@ agpu_status conv_tc_staged(agpu_device* dev, const ConvParams& p, const float* x
   return st;
 }
 
-// conv2d followed by group norm (+ swish) in `pieces` pieces of the batch:
-// the convs run back to back on `s`, each with every SM; every piece's group
-// norm runs on `s2` as soon as its conv is done, beside the next piece's
-// conv, so only the last piece's group norm is exposed.  The first piece and
-// the weights are staged on `s`, the other pieces on `s2` up front (each conv
-// waits for its piece's staging).  `s` waits for `s2` before returning.
-template <int BN, bool X3, bool PAIR>
-agpu_status conv_gn_pieces(agpu_device* dev, const ConvParams& p, const float* x, float* xs,
-                           const float* w, float* w2, const float* bias, float* y, int Cs,
-                           int Cw, const GnEpilogue* gn, int pieces, cudaStream_t s,
-                           cudaStream_t s2) {
-  const uint64_t x_img = (uint64_t)p.cin * p.h * p.w, y_img = (uint64_t)p.cout * p.ho * p.wo;
-  const uint64_t xs_img = (uint64_t)p.h * p.w * Cs;
-  auto first = [&](int i) { return (int)((long long)p.n * i / pieces); };
-  constexpr int kMaxPieces = 16;
-  pieces = std::min(pieces, kMaxPieces);
-  cudaEvent_t ev[kMaxPieces + 3] = {};
-  const int nev = pieces + 3;  // staged[1..], conv done, forked, joined
-  for (int i = 0; i < nev; ++i)
-    if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) {
-      for (int j = 0; j < i; ++j) cudaEventDestroy(ev[j]);
-      return cuda_status(cudaGetLastError(), "conv2d + group_norm: event create");
-    }
-  cudaEvent_t conv_done = ev[pieces], forked = ev[pieces + 1], joined = ev[pieces + 2];
-  agpu_status st = AGPU_OK;
-  launch_conv_stage(dev, x, xs, first(1), p.cin, p.h * p.w, Cs, w, w2, p.cout, p.cin,
-                    p.kh * p.kw, Cw, s);
-  st = after_launch(dev, "conv_stage_kernel");
-  cudaError_t e = st == AGPU_OK ? cudaEventRecord(forked, s) : cudaSuccess;
-  if (st == AGPU_OK && e == cudaSuccess) e = cudaStreamWaitEvent(s2, forked, 0);
-  for (int i = 1; i < pieces && st == AGPU_OK && e == cudaSuccess; ++i) {
-    const int b0 = first(i), nb = first(i + 1) - b0;
-    launch_conv_stage(dev, x + b0 * x_img, xs + b0 * xs_img, nb, p.cin, p.h * p.w, Cs, nullptr,
-                      nullptr, 0, 0, 0, 0, s2);
-    st = after_launch(dev, "conv_stage_kernel");
-    if (st == AGPU_OK) e = cudaEventRecord(ev[i], s2);
-  }
-  for (int i = 0; i < pieces && st == AGPU_OK && e == cudaSuccess; ++i) {
-    const int b0 = first(i);
-    ConvParams q = p;
-    q.n = first(i + 1) - b0;
-    if (i > 0) e = cudaStreamWaitEvent(s, ev[i], 0);
-    if (e != cudaSuccess) break;
-    st = conv_tc_staged<BN, X3, PAIR>(dev, q, xs + b0 * xs_img, w2, bias, y + b0 * y_img, s);
-    // each wait takes the event's latest record: this piece's conv
-    if (st == AGPU_OK) e = cudaEventRecord(conv_done, s);
-    if (st == AGPU_OK && e == cudaSuccess) e = cudaStreamWaitEvent(s2, conv_done, 0);
-    if (st == AGPU_OK && e == cudaSuccess)
-      st = launch_group_norm(dev, y + b0 * y_img, gn->gamma, gn->beta, y + b0 * y_img, q.n,
-                             q.cout, q.ho * q.wo, gn->groups, gn->eps, gn->swish, s2);
-  }
-  // join in every case, so that nothing on s2 outlives the call's stream order
-  const cudaError_t ej = cudaEventRecord(joined, s2);
-  const cudaError_t ew = ej == cudaSuccess ? cudaStreamWaitEvent(s, joined, 0) : ej;
-  for (int i = 0; i < nev; ++i) cudaEventDestroy(ev[i]);
-  if (e == cudaSuccess) e = ew;
-  if (e != cudaSuccess && st == AGPU_OK) st = cuda_status(e, "conv2d + group_norm: fork/join");
-  return st;
-}
-
 // Stage, then convolve.  With the CTA-pair kernel and >= 4 images the batch
 // runs as two halves: the weights and the first half's input are staged on
 // `s`; the second half's input is staged on the device's auxiliary stream
@@ -620,17 +560,6 @@ agpu_status run_conv_tc(agpu_device* dev, const ConvParams& p, const float* x, c
     return !(e && e[0] == '0');
   }();
   cudaStream_t s2 = (PAIR && overlap_ok && p.n >= 4) ? aux_stream(dev) : nullptr;
-  // conv2d + group norm with >= 2 images per piece: GN_PIECES pieces, see below
-  static const int gn_pieces = [] {
-    const char* e = getenv("AGPU_CONV_GN_PIECES");
-    return e ? std::max(1, atoi(e)) : 4;
-  }();
-  if (s2 && gn && gn_pieces > 2 && p.n >= 2 * gn_pieces) {
-    const agpu_status r = conv_gn_pieces<BN, X3, PAIR>(dev, p, x, xs, w, w2, bias, y, Cs, Cw,
-                                                       gn, gn_pieces, s, s2);
-    pool_free(dev, scratch, s);
-    return r;
-  }
   const int na = s2 ? p.n / 2 : p.n;
   launch_conv_stage(dev, x, xs, na, p.cin, p.h * p.w, Cs, w, w2, p.cout, p.cin, p.kh * p.kw, Cw,
                     s);

@@ -639,6 +639,90 @@ class Sdpa(Workload):
                 f"{done} heads of S={self.s}, D={self.D} (cpu_attention per head), {t:.1f} s")
 
 
+class SdpaBwd(Workload):
+    """Attention backward (agpu_launch_sdpa_backward) at the SDPA config: dQ,
+    dK, dV from Q, K, V, dO; FLOPs counted as its five products
+    (S = QK^T recomputed, dV = P^T dO, dP = dO V^T, dQ = dS K, dK = dS^T Q),
+    5 * 2 * BH * S^2 * D.  Three outputs: runs as replicas at N > 1."""
+    name = "sdpa_bwd"
+    l2 = "Q, K, V, dO, dQ, dK, dV 1.75 GiB + P, dS scratch 8 GiB > 126 MB L2"
+    item = "head"
+    seed = 1240
+    shardable = False
+    D = 128
+    dom_kernel = ("umma_tf32_pair_kernel<GemmPairPolicy> (the five products; timed as the "
+                  "whole backward call)")
+
+    def __init__(self, args, world, rank, replicas=False):
+        self.s = args.seq
+        hs = self.s * self.D
+        self.item_elems = {"q": hs, "k": hs, "v": hs, "do": hs}
+        self.out_item = hs
+        self.item_flops = 5 * 2.0 * self.s * self.s * self.D
+        super().__init__(args, world, rank, replicas)
+
+    def total_items(self):
+        return self.args.bh
+
+    def config(self):
+        return {"workload": "scaled_dot_product_attention backward", "batch_heads": self.total,
+                "seq_len": self.s, "d_k": self.D, "causal": False,
+                "inputs": "Q, K, V, dO N(0,1) seeded per head",
+                "flops": "5 * 2*BH*S^2*D (S recomputed, dV, dP, dQ, dK)"}
+
+    def fill_item(self, g, v):
+        r = item_rng(self.seed, g)
+        for k in ("q", "k", "v", "do"):
+            _normal_into(r, v[k])
+
+    def setup(self, torch, local):
+        super().setup(torch, local)
+        n = self.total * self.out_item
+        self.dk = torch.empty(n, dtype=torch.float32, device=f"cuda:{local}")
+        self.dv = torch.empty_like(self.dk)
+
+    def teardown(self):
+        super().teardown()
+        for k in ("dk", "dv"):
+            if hasattr(self, k):
+                delattr(self, k)
+
+    def launch_round(self, dev, rd, stream):
+        dev.launch_sdpa_backward(self.ptr("q"), self.ptr("k"), self.ptr("v"), self.ptr("do"),
+                                 self.out.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(),
+                                 self.total, self.s, self.D, False, stream.cuda_stream)
+        return stream
+
+    def dom_step(self, dev, stream):
+        self.launch_round(dev, None, stream)
+
+    def e2e_bytes(self):
+        h2d = sum(v.numel() * 4 for v in self.host.values())
+        return h2d, 3 * self.total * self.out_item * 4
+
+    def e2e_step(self, dev):
+        g = [dev.upload(self.host[n].numpy()) for n in ("q", "k", "v", "do")]
+        outs = dev.sdpa_backward(*g, self.total, self.s, self.D)
+        for b in outs:
+            dev.read(b, out=self.out_host.numpy())
+        for b in g + list(outs):
+            b.free()
+
+    def cpu_sample(self, orc, target_s, threads=True):
+        hs = self.s * self.D
+        x = {k: np.empty(hs, np.float32) for k in ("q", "k", "v", "do")}
+        self.fill_item(0, x)
+        done, t = 0, 0.0
+        while t < target_s:
+            t0 = time.perf_counter()
+            orc.attention_backward(x["q"], x["k"], x["v"], x["do"], 1, self.s, self.D)
+            t += time.perf_counter() - t0
+            done += 1
+        return (self.item_flops * done / t / 1e12,
+                f"{done} head(s) of S={self.s}, D={self.D} (the reference's SDPA composition "
+                f"differentiated with its own rules, one head), {t:.1f} s")
+
+
 class Unet(Workload):
     name = "unet"
     l2 = "x 80 MiB + conv out 80 MiB + y 80 MiB > 126 MB L2"
@@ -873,8 +957,8 @@ class Llama(Workload):
                 "the layer's dominant op, extrapolated by FLOPs")
 
 
-WORKLOADS = {"bmm_softmax": BmmSoftmax, "matmul": Matmul, "sdpa": Sdpa, "unet": Unet,
-             "llama": Llama}
+WORKLOADS = {"bmm_softmax": BmmSoftmax, "matmul": Matmul, "sdpa": Sdpa, "sdpa_bwd": SdpaBwd,
+             "unet": Unet, "llama": Llama}
 
 # the `workloads` object of the default line: name -> constructor kwargs
 EXTRA_WORKLOADS = [
@@ -885,6 +969,7 @@ EXTRA_WORKLOADS = [
     ("matmul_8192", Matmul, {"size": 8192}),
     ("matmul_8192_tf32x3", Matmul, {"size": 8192, "precision": "tf32x3"}),
     ("sdpa", Sdpa, {}),
+    ("sdpa_bwd", SdpaBwd, {}),
     ("unet", Unet, {}),
     ("llama", Llama, {}),
 ]

