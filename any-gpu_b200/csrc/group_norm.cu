@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kThreads) gn_apply_kernel(
 // flight, then normalises.  x is read twice, but a tensor that fits in L2
 // (126 MB) is mostly served from there the second time.
 constexpr int kChunkVec = 8;  // float4 per thread: 8192-element chunks
+constexpr int kMergeBatch = 8;  // chunk summaries fetched together by the apply kernel
 
 // Load with an L2 evict-last policy: the chunk stays in L2 for the apply
 // kernel's second read (measured: UNet block group norm 52 -> 50 us).
@@ -205,21 +206,39 @@ __global__ void __launch_bounds__(kThreads) gn_apply_vec_kernel(
     if (i < nvec) v[j] = __ldcs(src + i);  // last use of x
   }
   // every thread merges the group's chunk summaries (Chan et al., fixed
-  // order), while its loads are in flight
+  // order), while its loads are in flight; the first kMergeBatch summaries
+  // are fetched together (one L2 round trip, not one per merge step)
+  auto chunk_n = [&](int c) {
+    return (float)(std::min<long long>((long long)(c + 1) * chunk, gsize) - (long long)c * chunk);
+  };
+  const float2* gp = partials + grp * nchunks;
+  float2 pp[kMergeBatch];
+#pragma unroll
+  for (int c = 0; c < kMergeBatch; ++c)
+    if (c < nchunks) pp[c] = __ldg(gp + c);
   float n = 0.f, mean = 0.f, m2 = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float2 p = __ldg(partials + grp * nchunks + c);
-    const float nb = (float)(std::min<long long>((long long)(c + 1) * chunk, gsize) -
-                             (long long)c * chunk);
-    chan_merge(n, mean, m2, nb, p.x, p.y);
+#pragma unroll
+  for (int c = 0; c < kMergeBatch; ++c)
+    if (c < nchunks) chan_merge(n, mean, m2, chunk_n(c), pp[c].x, pp[c].y);
+  for (int c = kMergeBatch; c < nchunks; ++c) {
+    const float2 q = __ldg(gp + c);
+    chan_merge(n, mean, m2, chunk_n(c), q.x, q.y);
   }
   const float rstd = 1.0f / sqrtf(m2 / n + eps);
   float4* dst = reinterpret_cast<float4*>(y + grp * gsize + c0);
+  const float inv_sp = 1.0f / (float)spatial;
 #pragma unroll
   for (int j = 0; j < kChunkVec; ++j) {
     const int i = threadIdx.x + j * kThreads;
     if (i < nvec) {
-      const int ch = g * cpg + (int)((c0 + 4LL * i) / spatial);  // spatial % 4 == 0
+      // channel of element c0 + 4i inside the group (spatial % 4 == 0): a
+      // reciprocal estimate, then exact by one correction step either way
+      // (the quotient is below cpg, so the estimate is off by at most one)
+      const long long e = c0 + 4LL * i;
+      int cq = (int)((float)e * inv_sp);
+      if ((long long)cq * spatial > e) --cq;
+      else if ((long long)(cq + 1) * spatial <= e) ++cq;
+      const int ch = g * cpg + cq;
       const float ga = __ldg(gamma + ch) * rstd, be = __ldg(beta + ch);
       float4 o;
       o.x = act_fast((v[j].x - mean) * ga + be, SWISH);
