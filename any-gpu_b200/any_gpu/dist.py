@@ -155,8 +155,8 @@ class NcclGather:
 class PeerGather:
     """Round gathers on the copy engines: every rank pushes its run of each
     finished round straight into the same slot of every peer's output over
-    NVLink (agpu_copy_async into the peer's buffer, mapped with CUDA IPC),
-    one copy stream per peer, so the pushes use no SMs and run beside the next
+    NVLink (agpu_copy_async into the peer's buffer, mapped with CUDA IPC), on
+    `streams` copy streams, so the pushes use no SMs and run beside the next
     round's kernels.  At the end of a step each rank records an interprocess
     event after its pushes, the ranks meet at a host barrier (`host_group`, a
     gloo group: no device work), and each rank's stream waits on every peer's
@@ -165,7 +165,8 @@ class PeerGather:
     allocator does)."""
     kind = "ce"
 
-    def __init__(self, dev, plan: ShardPlan, out, item_elems: int, host_group):
+    def __init__(self, dev, plan: ShardPlan, out, item_elems: int, host_group,
+                 streams: int = 1):
         import ctypes as C
 
         import torch
@@ -185,16 +186,20 @@ class PeerGather:
         table = [None] * world
         dist.all_gather_object(table, (bytes(mem), off.value, bytes(evh)), group=host_group)
         self.peers = []  # (rank, base, dst pointer of the peer's out, event)
-        for p in range(world):
-            if p == rank:
-                continue
+        # peers in rotated order (rank+1, rank+2, ...): at any moment every rank
+        # pushes to a different peer
+        for p in ((rank + i) % world for i in range(1, world)):
             mb, poff, eb = table[p]
             base, pev = C.c_void_p(), C.c_void_p()
             _check(lib.agpu_ipc_import(h, (C.c_ubyte * 64).from_buffer_copy(mb), C.byref(base)))
             _check(lib.agpu_ipc_event_import(h, (C.c_ubyte * 64).from_buffer_copy(eb),
                                              C.byref(pev)))
             self.peers.append((p, base, base.value + poff, pev))
-        self.streams = [torch.cuda.Stream() for _ in self.peers]
+        # `streams` copy streams, peer i on stream i % streams: a few engines
+        # each streaming one copy after another beat one copy per engine per
+        # peer, which contend for the copy engines at 7 peers
+        n = max(1, min(streams, len(self.peers)))
+        self.streams = [torch.cuda.Stream() for _ in range(n)]
 
     def round(self, rd: Round, ready) -> None:
         import torch
@@ -206,8 +211,10 @@ class PeerGather:
         nbytes = 4 * n * self.ie
         off = 4 * rd.offsets[self.plan.rank] * self.ie
         src = self.out.data_ptr() + off
-        for (_, _, dst, _), cs in zip(self.peers, self.streams):
+        for cs in self.streams:
             cs.wait_event(ev)
+        for i, (_, _, dst, _) in enumerate(self.peers):
+            cs = self.streams[i % len(self.streams)]
             self._check(self.lib.agpu_copy_async(self.dev.handle, dst + off, src, nbytes,
                                                  cs.cuda_stream))
 

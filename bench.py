@@ -264,7 +264,8 @@ class Workload:
         IPC (`--comm ce`, default) or in-place NCCL collectives (`--comm nccl`)."""
         self.gatherer = None
         if self.sharded:
-            self.gatherer = (PeerGather(dev, self.plan, self.out, self.out_item, ctx.host_group)
+            self.gatherer = (PeerGather(dev, self.plan, self.out, self.out_item, ctx.host_group,
+                                        ctx.args.ce_streams)
                              if ctx.args.comm == "ce" else
                              NcclGather(self.plan, self.out, self.out_item))
 
@@ -1204,8 +1205,9 @@ def _measure(ctx, wl, dev, stream, cpu_seconds, cpu_single, e2e_steps, steps, wa
         recv = (wl.total - wl.local) * wl.out_item * 4
         if ctx.args.comm == "ce":
             how = ("copy-engine pushes over CUDA IPC: each rank copies its run of every round "
-                   "into every peer's output (agpu_copy_async, one stream per peer, no SMs), "
-                   "then interprocess events + a host barrier end the step")
+                   f"into every peer's output (agpu_copy_async on {ctx.args.ce_streams} copy "
+                   "stream(s), peers in rotated order, no SMs), then interprocess events + a "
+                   "host barrier end the step")
         elif all(r.even for r in wl.plan.spans):
             how = "in-place all_gather_into_tensor (ncclAllGather over NVLink) per round"
         else:
@@ -1279,6 +1281,8 @@ def main():
                     help="N > 1: every rank runs the whole config, no collective (weak)")
     ap.add_argument("--comm", choices=["ce", "nccl"], default="ce",
                     help="N > 1 output gathers: copy engines over CUDA IPC, or NCCL collectives")
+    ap.add_argument("--ce-streams", type=int, default=1,
+                    help="copy streams of the copy-engine gathers (peers spread over them)")
     ap.add_argument("--no-workloads", action="store_true",
                     help="headline only (no `workloads` object)")
     ap.add_argument("--e2e-steps", type=int, default=5)
