@@ -136,6 +136,8 @@ SIGNATURES: dict[str, tuple] = {
     "agpu_event_record": (c_status, [c_dev, C.c_void_p, C.c_void_p]),
     "agpu_stream_wait_event": (c_status, [c_dev, C.c_void_p, C.c_void_p]),
     "agpu_copy_async": (c_status, [c_dev, C.c_void_p, C.c_void_p, u64, C.c_void_p]),
+    "agpu_signal_peers": (c_status, [c_dev, C.POINTER(C.c_void_p), u32, u32, C.c_void_p]),
+    "agpu_wait_flags": (c_status, [c_dev, C.c_void_p, u32, u32, u32, C.c_void_p]),
     "agpu_selftest_wait_timeout": (c_status, [c_dev, u32, C.c_void_p]),
 }
 

@@ -156,45 +156,81 @@ class PeerGather:
     """Round gathers on the copy engines: every rank pushes its run of each
     finished round straight into the same slot of every peer's output over
     NVLink (agpu_copy_async into the peer's buffer, mapped with CUDA IPC), on
-    `streams` copy streams, so the pushes use no SMs and run beside the next
-    round's kernels.  At the end of a step each rank records an interprocess
-    event after its pushes, the ranks meet at a host barrier (`host_group`, a
-    gloo group: no device work), and each rank's stream waits on every peer's
-    event -- after which every rank holds the whole output.  Uneven runs need
-    no special case.  `out` must come from cudaMalloc (torch's default
-    allocator does)."""
+    `streams` copy streams with the peers in rotated order, so the pushes use
+    no SMs and run beside the next round's kernels.
+
+    End of step (`sync="flags"`, default): after its pushes a rank stores the
+    step number into its slot of every rank's flag array
+    (agpu_signal_peers, a system-scope release after the copies), and its
+    stream waits until all slots of its own array reach the step
+    (agpu_wait_flags: one warp, a bounded spin whose expiry is reported as
+    AGPU_ERR_TIMEOUT) -- no host round trip, so the host keeps queueing the
+    next step.  `sync="events"`: interprocess events plus a host barrier on
+    `host_group` instead.  Either way every rank then holds the whole
+    output.  Uneven runs need no special case.  `out` must come from
+    cudaMalloc (torch's default allocator does)."""
     kind = "ce"
 
     def __init__(self, dev, plan: ShardPlan, out, item_elems: int, host_group,
-                 streams: int = 1):
+                 streams: int = 1, sync: str = "flags", wait_limit_us: int = 2_000_000):
         import ctypes as C
 
         import torch
         import torch.distributed as dist
 
         from . import _check, _lib
-        self.lib, self._check = _lib.load(), _check
+        if sync not in ("flags", "events"):
+            raise ValueError(f"sync must be 'flags' or 'events', got {sync!r}")
+        self.lib, self._check, self.C = _lib.load(), _check, C
         self.dev, self.plan, self.out, self.ie = dev, plan, out, item_elems
-        self.group = host_group
+        self.group, self.sync, self.limit = host_group, sync, wait_limit_us
         lib, h = self.lib, dev.handle
-        mem, off = (C.c_ubyte * 64)(), C.c_uint64()
-        _check(lib.agpu_ipc_export(h, out.data_ptr(), mem, C.byref(off)))
+        world, rank = plan.world, plan.rank
+        self.flags = torch.zeros(world, dtype=torch.int32, device=out.device)
+        self.step = 0
+
+        def export(ptr):
+            mem, off = (C.c_ubyte * 64)(), C.c_uint64()
+            _check(lib.agpu_ipc_export(h, ptr, mem, C.byref(off)))
+            return bytes(mem), off.value
+
         ev, evh = C.c_void_p(), (C.c_ubyte * 64)()
         _check(lib.agpu_ipc_event_create(h, C.byref(ev), evh))
         self.event = ev
-        world, rank = plan.world, plan.rank
+        mine = (export(out.data_ptr()), export(self.flags.data_ptr()), bytes(evh))
         table = [None] * world
-        dist.all_gather_object(table, (bytes(mem), off.value, bytes(evh)), group=host_group)
-        self.peers = []  # (rank, base, dst pointer of the peer's out, event)
+        dist.all_gather_object(table, mine, group=host_group)
+        torch.cuda.synchronize()  # the zeroed flags are in place before any peer signals
+        dist.barrier(group=host_group)
+        self._bases = []
+        imported = {}
+
+        def import_(mb):
+            if mb not in imported:  # one mapping per allocation
+                base = C.c_void_p()
+                _check(lib.agpu_ipc_import(h, (C.c_ubyte * 64).from_buffer_copy(mb),
+                                           C.byref(base)))
+                imported[mb] = base
+                self._bases.append(base)
+            return imported[mb].value
+
+        self.peers = []  # (rank, dst pointer of the peer's out, its event)
+        flag_slots = []  # this rank's slot in every rank's flag array
+        for p in range(world):
+            (mb, moff), (fb, foff), eb = table[p]
+            if p == rank:
+                flag_slots.append(self.flags.data_ptr() + 4 * rank)
+                continue
+            flag_slots.append(import_(fb) + foff + 4 * rank)
         # peers in rotated order (rank+1, rank+2, ...): at any moment every rank
         # pushes to a different peer
         for p in ((rank + i) % world for i in range(1, world)):
-            mb, poff, eb = table[p]
-            base, pev = C.c_void_p(), C.c_void_p()
-            _check(lib.agpu_ipc_import(h, (C.c_ubyte * 64).from_buffer_copy(mb), C.byref(base)))
+            (mb, moff), _, eb = table[p]
+            pev = C.c_void_p()
             _check(lib.agpu_ipc_event_import(h, (C.c_ubyte * 64).from_buffer_copy(eb),
                                              C.byref(pev)))
-            self.peers.append((p, base, base.value + poff, pev))
+            self.peers.append((p, import_(mb) + moff, pev))
+        self.flag_slots = (C.c_void_p * world)(*flag_slots)
         # `streams` copy streams, peer i on stream i % streams: a few engines
         # each streaming one copy after another beat one copy per engine per
         # peer, which contend for the copy engines at 7 peers
@@ -213,19 +249,27 @@ class PeerGather:
         src = self.out.data_ptr() + off
         for cs in self.streams:
             cs.wait_event(ev)
-        for i, (_, _, dst, _) in enumerate(self.peers):
+        for i, (_, dst, _) in enumerate(self.peers):
             cs = self.streams[i % len(self.streams)]
             self._check(self.lib.agpu_copy_async(self.dev.handle, dst + off, src, nbytes,
                                                  cs.cuda_stream))
 
     def finish(self, stream) -> None:
-        import torch.distributed as dist
+        h = self.dev.handle
         for cs in self.streams:
             stream.wait_stream(cs)
-        h = self.dev.handle
+        if self.sync == "flags":
+            self.step += 1
+            # the signal follows every push of this step (stream order)
+            self._check(self.lib.agpu_signal_peers(h, self.flag_slots, self.plan.world,
+                                                   self.step, stream.cuda_stream))
+            self._check(self.lib.agpu_wait_flags(h, self.flags.data_ptr(), self.plan.world,
+                                                 self.step, self.limit, stream.cuda_stream))
+            return
+        import torch.distributed as dist
         self._check(self.lib.agpu_event_record(h, self.event, stream.cuda_stream))
         dist.barrier(group=self.group)  # every rank's record is issued
-        for _, _, _, pev in self.peers:
+        for _, _, pev in self.peers:
             self._check(self.lib.agpu_stream_wait_event(h, stream.cuda_stream, pev))
 
     def close(self) -> None:
@@ -235,11 +279,12 @@ class PeerGather:
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         h = self.dev.handle
-        for _, base, _, pev in self.peers:
+        for _, _, pev in self.peers:
             self.lib.agpu_event_destroy(h, pev)
+        for base in self._bases:
             self.lib.agpu_ipc_close(h, base)
         self.lib.agpu_event_destroy(h, self.event)
-        self.peers = []
+        self.peers, self._bases = [], []
         dist.barrier(group=self.group)
 
 

@@ -6,9 +6,14 @@
 // using no SMs, so the pushes run beside the next round's kernels (NCCL's
 // gather kernels need SMs, which the persistent contraction kernels hold).
 //
-// Completion crosses processes through interprocess events: a rank records
-// its event after its pushes; a peer's stream waits on it once the host
-// side knows the record was issued (a host barrier between the two).
+// Completion crosses processes either through interprocess events (a rank
+// records its event after its pushes; a peer's stream waits on it once the
+// host side knows the record was issued) or through flag words in device
+// memory: after its pushes a rank's stream stores the step number into every
+// peer's flag (signal_peers_kernel, a system-scope release), and each rank's
+// stream waits until all its flags reach the step (wait_flags_kernel, a
+// bounded spin: on expiry it records a code in the device status word, which
+// the next agpu_synchronize reports as AGPU_ERR_TIMEOUT, and returns).
 #include <cuda.h>
 
 #include <cstring>
@@ -47,9 +52,79 @@ agpu_status select(agpu_device* dev, const char* fn) {
   return AGPU_OK;
 }
 
+constexpr int kMaxPeers = 16;
+
+struct PeerFlags {
+  unsigned int* p[kMaxPeers];
+};
+
+// Store `value` into each peer's flag word (system-scope release: every write
+// this stream made before -- the copies of the data -- is complete first).
+__global__ void signal_peers_kernel(PeerFlags flags, int count, unsigned int value) {
+  const int i = threadIdx.x;
+  if (i < count)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags.p[i]), "r"(value) : "memory");
+}
+
+// One warp: wait until flags[i] >= target (wrapping compare) for every i <
+// count, each read an acquire at system scope; give up after limit_ns of
+// global time, record `code` in the status word and return.
+__global__ void wait_flags_kernel(const unsigned int* flags, int count, unsigned int target,
+                                  unsigned long long limit_ns, unsigned int* status,
+                                  unsigned int code) {
+  const int lane = threadIdx.x;
+  unsigned long long t0 = 0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 0;; ++it) {
+    bool done = true;
+    if (lane < count) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + lane) : "memory");
+      done = (int)(v - target) >= 0;
+    }
+    if (__all_sync(0xffffffffu, done)) return;
+    if ((it & 63u) == 63u) {
+      unsigned long long t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if (t1 - t0 > limit_ns) {
+        if (lane == 0) atomicCAS(status, 0u, code);
+        return;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+agpu_status agpu_signal_peers(agpu_device* dev, unsigned int* const* peer_flags, uint32_t count,
+                              uint32_t value, void* stream) {
+  AGPU_TRY(select(dev, "agpu_signal_peers"));
+  if (count == 0) return AGPU_OK;
+  if (!peer_flags || count > kMaxPeers)
+    return fail(AGPU_ERR_INVALID, "agpu_signal_peers: %u flags (at most %d)", count, kMaxPeers);
+  PeerFlags f = {};
+  for (uint32_t i = 0; i < count; ++i) {
+    if (!peer_flags[i]) return fail(AGPU_ERR_INVALID, "agpu_signal_peers: NULL flag %u", i);
+    f.p[i] = peer_flags[i];
+  }
+  signal_peers_kernel<<<1, 32, 0, pick_stream(dev, stream)>>>(f, (int)count, value);
+  return after_launch(dev, "signal_peers_kernel");
+}
+
+agpu_status agpu_wait_flags(agpu_device* dev, const unsigned int* flags, uint32_t count,
+                            uint32_t target, uint32_t limit_us, void* stream) {
+  AGPU_TRY(select(dev, "agpu_wait_flags"));
+  if (count == 0) return AGPU_OK;
+  if (!flags || count > 32 || limit_us == 0 || limit_us > 10000000u)
+    return fail(AGPU_ERR_INVALID, "agpu_wait_flags: %u flags (at most 32), limit %u us", count,
+                limit_us);
+  wait_flags_kernel<<<1, 32, 0, pick_stream(dev, stream)>>>(flags, (int)count, target,
+                                                            1000ull * limit_us, dev->d_status,
+                                                            AGPU_WAIT_FLAGS_CODE);
+  return after_launch(dev, "wait_flags_kernel");
+}
 
 agpu_status agpu_ipc_export(agpu_device* dev, const void* dptr, agpu_ipc_handle* handle,
                             uint64_t* offset) {

@@ -4,7 +4,7 @@
 //! crate's `GpuDevice` / `GpuBuffer` API.
 #![allow(non_camel_case_types, dead_code)]
 
-use std::os::raw::{c_char, c_int, c_void};
+use std::os::raw::{c_char, c_int, c_uint, c_void};
 
 /// `agpu_status`: 0 = ok; see `AgpuError` in device.rs for the others.
 pub type AgpuStatus = c_int;
@@ -19,6 +19,9 @@ pub const AGPU_ERR_UNSUPPORTED: AgpuStatus = 7;
 
 /// `AGPU_SELFTEST_WAIT_CODE`: the status code agpu_selftest_wait_timeout records.
 pub const AGPU_SELFTEST_WAIT_CODE: u32 = 0x7e57;
+
+/// `AGPU_WAIT_FLAGS_CODE`: the status code an expired agpu_wait_flags records.
+pub const AGPU_WAIT_FLAGS_CODE: u32 = 0x5157;
 
 /// `agpu_precision`.
 pub const AGPU_PREC_TF32: c_int = 0;
@@ -826,6 +829,21 @@ extern "C" {
         dst: *mut c_void,
         src: *const c_void,
         bytes: u64,
+        stream: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_signal_peers(
+        dev: *mut AgpuDevice,
+        peer_flags: *const *mut c_uint,
+        count: u32,
+        value: u32,
+        stream: *mut c_void,
+    ) -> AgpuStatus;
+    pub fn agpu_wait_flags(
+        dev: *mut AgpuDevice,
+        flags: *const c_uint,
+        count: u32,
+        target: u32,
+        limit_us: u32,
         stream: *mut c_void,
     ) -> AgpuStatus;
     pub fn agpu_selftest_wait_timeout(

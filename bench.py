@@ -265,7 +265,7 @@ class Workload:
         self.gatherer = None
         if self.sharded:
             self.gatherer = (PeerGather(dev, self.plan, self.out, self.out_item, ctx.host_group,
-                                        ctx.args.ce_streams)
+                                        ctx.args.ce_streams, ctx.args.ce_sync)
                              if ctx.args.comm == "ce" else
                              NcclGather(self.plan, self.out, self.out_item))
 
@@ -1206,8 +1206,10 @@ def _measure(ctx, wl, dev, stream, cpu_seconds, cpu_single, e2e_steps, steps, wa
         if ctx.args.comm == "ce":
             how = ("copy-engine pushes over CUDA IPC: each rank copies its run of every round "
                    f"into every peer's output (agpu_copy_async on {ctx.args.ce_streams} copy "
-                   "stream(s), peers in rotated order, no SMs), then interprocess events + a "
-                   "host barrier end the step")
+                   "stream(s), peers in rotated order, no SMs); the step ends on "
+                   + ("device flag words (agpu_signal_peers / agpu_wait_flags)"
+                      if ctx.args.ce_sync == "flags" else
+                      "interprocess events + a host barrier"))
         elif all(r.even for r in wl.plan.spans):
             how = "in-place all_gather_into_tensor (ncclAllGather over NVLink) per round"
         else:
@@ -1283,6 +1285,9 @@ def main():
                     help="N > 1 output gathers: copy engines over CUDA IPC, or NCCL collectives")
     ap.add_argument("--ce-streams", type=int, default=1,
                     help="copy streams of the copy-engine gathers (peers spread over them)")
+    ap.add_argument("--ce-sync", choices=["flags", "events"], default="flags",
+                    help="end of a copy-engine gather step: device flag words, or "
+                         "interprocess events + a host barrier")
     ap.add_argument("--no-workloads", action="store_true",
                     help="headline only (no `workloads` object)")
     ap.add_argument("--e2e-steps", type=int, default=5)

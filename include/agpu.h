@@ -566,6 +566,21 @@ AGPU_API agpu_status agpu_stream_wait_event(agpu_device* dev, void* stream, void
 AGPU_API agpu_status agpu_copy_async(agpu_device* dev, void* dst, const void* src, uint64_t bytes,
                                      void* stream);
 
+/* Completion without events or host barriers: agpu_signal_peers stores
+ * `value` into each of `count` (<= 16) flag words in peers' memory (mapped
+ * with agpu_ipc_import) on `stream`, after all earlier work of that stream
+ * (a system-scope release); agpu_wait_flags makes `stream` wait until each
+ * of `count` (<= 32) local flag words is >= `target` (serial-number compare),
+ * spinning one warp for at most `limit_us` (1 us - 10 s) -- on expiry it
+ * records AGPU_WAIT_FLAGS_CODE in the device status word, reported as
+ * AGPU_ERR_TIMEOUT by the next agpu_synchronize / agpu_read, and returns. */
+#define AGPU_WAIT_FLAGS_CODE 0x5157u
+AGPU_API agpu_status agpu_signal_peers(agpu_device* dev, unsigned int* const* peer_flags,
+                                       uint32_t count, uint32_t value, void* stream);
+AGPU_API agpu_status agpu_wait_flags(agpu_device* dev, const unsigned int* flags,
+                                     uint32_t count, uint32_t target, uint32_t limit_us,
+                                     void* stream);
+
 /* ---------------------------------------------------- failure self-test -- */
 /* No counterpart in the reference.  Exercises the failure path of the
  * bounded device-side waits without faulting or hanging anything: launches

@@ -110,3 +110,45 @@ def test_thread_precision_is_per_call_and_per_thread(dev, orc):
     assert e_tf32 > 1e-5 and e_after > 1e-5, (e_tf32, e_after)
     assert other["mode"] == -1
     assert other["err"] > 1e-5, other
+
+
+def test_wait_flags_expires_without_a_signal(dev, orc):
+    """The end-of-step wait of the copy-engine gathers: a flag no peer ever
+    sets makes agpu_wait_flags give up after its limit and report
+    AGPU_ERR_TIMEOUT (code 0x5157) -- a peer that died shows up as an error,
+    not a hung GPU -- and the device stays usable."""
+    import ctypes as C
+
+    import torch
+    from any_gpu import AnyGpuError, _lib
+    lib = _lib.load()
+    flags = torch.zeros(3, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    assert lib.agpu_wait_flags(dev.handle, C.c_void_p(flags.data_ptr()), 3, 1, 2000, None) == 0
+    with pytest.raises(AnyGpuError) as e:
+        dev.synchronize()
+    assert e.value.status == 6 and "0x5157" in str(e.value)
+    dev.synchronize()
+    _matmul_ok(dev, orc)
+
+
+def test_signal_then_wait_flags_round_trip(dev):
+    """agpu_signal_peers stores the step into each flag word (here local ones
+    standing in for the peers' slots) and agpu_wait_flags returns once every
+    word has reached it; serial-number compare across the 2^32 wrap."""
+    import ctypes as C
+
+    import torch
+    from any_gpu import _lib
+    lib = _lib.load()
+    flags = torch.zeros(4, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    slots = (C.c_void_p * 4)(*[flags.data_ptr() + 4 * i for i in range(4)])
+    for value in (1, 2, 0xFFFFFFFF, 0):  # the last two wrap
+        assert lib.agpu_signal_peers(dev.handle, slots, 4, value, None) == 0
+        assert lib.agpu_wait_flags(dev.handle, C.c_void_p(flags.data_ptr()), 4, value, 1_000_000,
+                                   None) == 0
+        dev.synchronize()
+    assert flags.cpu().tolist() == [0, 0, 0, 0]
+    assert lib.agpu_wait_flags(dev.handle, C.c_void_p(flags.data_ptr()), 33, 1, 10, None) == 2
+    assert lib.agpu_signal_peers(dev.handle, slots, 17, 1, None) == 2

@@ -6,7 +6,8 @@ the same bytes, and the whole result matches the oracle.  Covers batch_matmul
 + softmax in two rounds (GEMMs on one stream, softmaxes on another), an
 uneven split (5 items over 2 ranks: in-place broadcasts), and attention
 sharded by heads -- each through both gatherers: copy-engine pushes over CUDA
-IPC (PeerGather) and in-place NCCL collectives (NcclGather)."""
+IPC (PeerGather, ending each step on device flag words or on interprocess
+events) and in-place NCCL collectives (NcclGather)."""
 from __future__ import annotations
 
 import os
@@ -81,10 +82,11 @@ def _worker(rank, world, port, q):
                 aux.wait_event(ev)
                 dev.launch_softmax(c, c, cnt * m, n, aux.cuda_stream)
                 return aux
-            for kind in ("nccl", "ce"):
+            for kind in ("nccl", "ce", "ce_events"):
                 out = torch.full((batch * m * n,), float("nan"), device="cuda")
                 g = NcclGather(plan, out, m * n) if kind == "nccl" else \
-                    PeerGather(dev, plan, out, m * n, host)
+                    PeerGather(dev, plan, out, m * n, host,
+                               sync="events" if kind == "ce_events" else "flags")
                 for _ in range(2):  # twice: the second step reuses the events and mappings
                     out.fill_(float("nan"))
                     stream.synchronize()
@@ -141,15 +143,18 @@ def test_two_gpu_sharded_rounds_gather_in_place(orc):
         assert err is None, f"rank {rank}: {err}"
     r0, r1 = res[0][1], res[1][1]
     m, n, k = 256, 512, 384
-    for kind in ("nccl", "ce"):
+    for kind in ("nccl", "ce", "ce_events"):
         for batch in (8, 5):
             got0, a, b = r0[f"bmm{batch}_{kind}"]
             got1 = r1[f"bmm{batch}_{kind}"][0]
             assert np.array_equal(got0, got1), f"bmm{batch} {kind}: ranks hold different results"
             want = orc.softmax(orc.batch_matmul(a, b, batch, m, n, k), batch * m, n)
             assert orc.rel_fro(got0, want) <= 1e-3, kind
+        if kind == "ce_events":
+            continue
         got0, qh, kh, vh = r0[f"sdpa_{kind}"]
         assert np.array_equal(got0, r1[f"sdpa_{kind}"][0]), kind
         assert orc.rel_fro(got0, orc.attention(qh, kh, vh, 6, 256, 128)) <= 1e-3, kind
-    # both gatherers move the same bytes
+    # the gatherers move the same bytes
     assert np.array_equal(r0["bmm8_nccl"][0], r0["bmm8_ce"][0])
+    assert np.array_equal(r0["bmm8_ce"][0], r0["bmm8_ce_events"][0])
