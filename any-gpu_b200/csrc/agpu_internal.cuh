@@ -122,12 +122,7 @@ agpu_status launch_gemm(agpu_device* dev, const float* a, const float* b, float*
 struct GemmEpilogue {
   const float* bias = nullptr;   // [n] or null
   const float* resid = nullptr;  // [batch, m, n] or null (may alias nothing but C's shape)
-  int act = 0;                   // 0 none, 1 swish, 2 relu, 3 SwiGLU; 4, 5: row epilogues
-  // acts 4 and 5 (gemm_row_epilogue.cuh; no bias or residual with them)
-  const float* rowvec = nullptr;  // [batch, m]
-  const float* aux = nullptr;     // [batch, m, n]
-  float scale = 1.0f;
-  int causal = 0;
+  int act = 0;                   // 0 none, 1 swish, 2 relu
 };
 agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
                            uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
@@ -164,12 +159,6 @@ agpu_status launch_attention_strided(agpu_device* dev, const float* q, const flo
 agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
                              cudaStream_t st);
-// The tensor-core forward that also writes each query row's base-2
-// log-sum-exp of its scaled scores to lse [bh, s]; AGPU_ERR_UNSUPPORTED (set,
-// nothing launched) when those kernels do not take the call.
-agpu_status launch_attention_lse(agpu_device* dev, const float* q, const float* k,
-                                 const float* v, float* o, float* lse, uint32_t bh, uint32_t s,
-                                 uint32_t d, bool causal, cudaStream_t st);
 // dQ, dK, dV of attention from dO (recomputes P; tensor-core GEMMs + two row
 // kernels; scratch from the device pool).
 agpu_status launch_attention_backward(agpu_device* dev, const float* q, const float* k,

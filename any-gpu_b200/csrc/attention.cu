@@ -55,15 +55,18 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-using ptx::round_tf32;
+// Round a finite non-negative float to tf32, nearest with ties to even (the
+// tensor core would otherwise truncate P).
+__device__ __forceinline__ uint32_t round_tf32(float x) {
+  uint32_t u = __float_as_uint(x);
+  u += 0xFFFu + ((u >> 13) & 1u);
+  return u & 0xFFFFE000u;
+}
 
 // Output strides (elements) and which input maps order heads before sequence.
 struct AttnOut {
   long long s, h, b;
   int hs;  // bit 1: k, bit 2: v
-  // optional: base-2 log-sum-exp of each query row's scaled scores,
-  // [batch, heads, seq] (the attention backward rebuilds P from it)
-  float* lse = nullptr;
 };
 
 // Q is read by the softmax threads themselves (one row each) and parked in
@@ -450,9 +453,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       lsum[h * 128 + row] = l;
       ptx::named_bar_sync(1 + q, 64);
       l += lsum[(h ^ 1) * 128 + row];
-      // P = exp2(x - m_used) / l, so the row's base-2 log-sum-exp is m_used + log2(l)
-      if (ol.lse && h == 0 && qrow < S)
-        ol.lse[((long long)bat * tiles.H + head) * S + qrow] = m_used + log2f(l);
       // One o_full phase per tile, awaited once each, in order (the o_done
       // parity of the last P V could be passed while the one before it is
       // still running).
@@ -892,9 +892,6 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
       lsum[h * 128 + row] = l;
       ptx::named_bar_sync(1 + q, 64);
       l += lsum[(h ^ 1) * 128 + row];
-      // P = exp2(x - m_used) / l, so the row's base-2 log-sum-exp is m_used + log2(l)
-      if (ol.lse && h == 0 && qrow < S)
-        ol.lse[((long long)bat * tiles.H + head) * S + qrow] = m_used + log2f(l);
       if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(o_full, (uint32_t)(tile_i & 1),
                                                           status, 0x22a, abort_flag));
       if (ok) {
@@ -1064,13 +1061,13 @@ agpu_status make_attn_map(CUtensorMap* map, const float* base, int D, int S, int
 template <int D, bool CAUSAL>
 agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, int B, int H, int s, const AttnStrides& sd,
-                             cudaStream_t st, float* lse) {
+                             cudaStream_t st) {
   using C = AttnCfg<D>;
   CUtensorMap tk, tv;
   bool hk, hv;
   AGPU_TRY(make_attn_map(&tk, k, D, s, H, B, sd.k, KT, false, &hk));
   AGPU_TRY(make_attn_map(&tv, v, D, s, H, B, sd.v, KT, true, &hv));
-  AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0), lse};
+  AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0)};
   AttnQ qin{q, sd.q[0], sd.q[1], sd.q[2]};
   auto kern = attention_tf32_kernel<D, CAUSAL>;
   AGPU_CUDA((set_smem_once<attention_tf32_kernel<D, CAUSAL>>(dev, C::SMEM)));
@@ -1089,13 +1086,13 @@ agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, c
 template <int D, bool CAUSAL>
 agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k, const float* v,
                                float* o, int B, int H, int s, const AttnStrides& sd,
-                               cudaStream_t st, float* lse) {
+                               cudaStream_t st) {
   using C = PairAttnCfg<D>;
   CUtensorMap tk, tv;
   bool hk, hv;
   AGPU_TRY(make_attn_map(&tk, k, D, s, H, B, sd.k, KH, false, &hk));
   AGPU_TRY(make_attn_map(&tv, v, D, s, H, B, sd.v, KB, true, &hv));
-  AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0), lse};
+  AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0)};
   AttnQ qin{q, sd.q[0], sd.q[1], sd.q[2]};
   auto kern = attention_pair_kernel<D, CAUSAL>;
   AGPU_CUDA((set_smem_once<attention_pair_kernel<D, CAUSAL>>(dev, C::SMEM)));
@@ -1125,15 +1122,11 @@ agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k,
 
 }  // namespace
 
-// The dispatch of launch_attention_strided; with `lse` non-null only the
-// tensor-core kernels may run (they write the rows' log-sum-exp), and a shape
-// or precision mode they do not take returns AGPU_ERR_UNSUPPORTED.
-static agpu_status attention_dispatch(agpu_device* dev, const float* q, const float* k,
-                                      const float* v, float* o, uint32_t B, uint32_t H,
-                                      uint32_t s, uint32_t d, const long long (&qs)[3],
-                                      const long long (&ks)[3], const long long (&vs)[3],
-                                      const long long (&os)[3], bool causal, cudaStream_t st,
-                                      float* lse) {
+agpu_status launch_attention_strided(agpu_device* dev, const float* q, const float* k,
+                                     const float* v, float* o, uint32_t B, uint32_t H,
+                                     uint32_t s, uint32_t d, const long long (&qs)[3],
+                                     const long long (&ks)[3], const long long (&vs)[3],
+                                     const long long (&os)[3], bool causal, cudaStream_t st) {
   if ((uint64_t)B * H * s * d == 0) return AGPU_OK;
   AttnStrides sd;
   for (int i = 0; i < 3; ++i) {
@@ -1155,19 +1148,18 @@ static agpu_status attention_dispatch(agpu_device* dev, const float* q, const fl
   }();
   if (tc && pair_ok && s >= 2 * QT) {
     if (d == 128)
-      return causal ? run_attention_pair<128, true>(dev, q, k, v, o, B, H, s, sd, st, lse)
-                    : run_attention_pair<128, false>(dev, q, k, v, o, B, H, s, sd, st, lse);
-    return causal ? run_attention_pair<64, true>(dev, q, k, v, o, B, H, s, sd, st, lse)
-                  : run_attention_pair<64, false>(dev, q, k, v, o, B, H, s, sd, st, lse);
+      return causal ? run_attention_pair<128, true>(dev, q, k, v, o, B, H, s, sd, st)
+                    : run_attention_pair<128, false>(dev, q, k, v, o, B, H, s, sd, st);
+    return causal ? run_attention_pair<64, true>(dev, q, k, v, o, B, H, s, sd, st)
+                  : run_attention_pair<64, false>(dev, q, k, v, o, B, H, s, sd, st);
   }
   if (tc) {
     if (d == 128)
-      return causal ? run_attention_tc<128, true>(dev, q, k, v, o, B, H, s, sd, st, lse)
-                    : run_attention_tc<128, false>(dev, q, k, v, o, B, H, s, sd, st, lse);
-    return causal ? run_attention_tc<64, true>(dev, q, k, v, o, B, H, s, sd, st, lse)
-                  : run_attention_tc<64, false>(dev, q, k, v, o, B, H, s, sd, st, lse);
+      return causal ? run_attention_tc<128, true>(dev, q, k, v, o, B, H, s, sd, st)
+                    : run_attention_tc<128, false>(dev, q, k, v, o, B, H, s, sd, st);
+    return causal ? run_attention_tc<64, true>(dev, q, k, v, o, B, H, s, sd, st)
+                  : run_attention_tc<64, false>(dev, q, k, v, o, B, H, s, sd, st);
   }
-  if (lse) return fail(AGPU_ERR_UNSUPPORTED, "sdpa: no tensor-core path for this call");
   if (d > 256) return fail(AGPU_ERR_UNSUPPORTED, "sdpa: head dim %u > 256", d);
   const long long warps = (long long)B * H * s;
   const unsigned blocks = (unsigned)ceil_div((uint64_t)warps * 32, 256);
@@ -1179,27 +1171,12 @@ static agpu_status attention_dispatch(agpu_device* dev, const float* q, const fl
   return after_launch(dev, "attention_simt_kernel");
 }
 
-agpu_status launch_attention_strided(agpu_device* dev, const float* q, const float* k,
-                                     const float* v, float* o, uint32_t B, uint32_t H,
-                                     uint32_t s, uint32_t d, const long long (&qs)[3],
-                                     const long long (&ks)[3], const long long (&vs)[3],
-                                     const long long (&os)[3], bool causal, cudaStream_t st) {
-  return attention_dispatch(dev, q, k, v, o, B, H, s, d, qs, ks, vs, os, causal, st, nullptr);
-}
-
 // Contiguous [bh, s, d] operands: heads = bh, batch = 1.
 agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
                              cudaStream_t st) {
   const long long c[3] = {(long long)d, (long long)s * d, (long long)bh * s * d};
   return launch_attention_strided(dev, q, k, v, o, 1, bh, s, d, c, c, c, c, causal, st);
-}
-
-agpu_status launch_attention_lse(agpu_device* dev, const float* q, const float* k,
-                                 const float* v, float* o, float* lse, uint32_t bh, uint32_t s,
-                                 uint32_t d, bool causal, cudaStream_t st) {
-  const long long c[3] = {(long long)d, (long long)s * d, (long long)bh * s * d};
-  return attention_dispatch(dev, q, k, v, o, 1, bh, s, d, c, c, c, c, causal, st, lse);
 }
 
 }  // namespace agpu

@@ -15,25 +15,15 @@
 // The five products run on the tensor-core GEMMs (launch_gemm: tcgen05 in
 // TF32, 3xTF32 or exact FFMA per the precision mode), with the transposes
 // folded into operand majors -- kind::tf32 reads either major -- so no
-// transpose pass.  P and dS live in two [heads, S, S] scratch buffers from
-// the device pool, processed in head chunks of at most 2^30 elements each.
-//
-// TF32 path (the tensor-core forward takes the shape): the forward runs again
-// and writes each query row's base-2 log-sum-exp L; with D = rowsum(dO o O)
-// (= rowsum(P o dP)) and Q' = tf32(Q * log2(e) / sqrt(d)) -- the forward's own
-// scaled, rounded Q -- the S product's epilogue writes P = exp2(Q'K^T - L)
-// directly and the dO V^T product's epilogue writes dS = P o (dP - D) / sqrt(d)
-// (GEMM acts 4 and 5): no score or dP round trip through HBM and no row
-// kernel.  Other shapes and the fp32-accuracy modes take the general path:
-// S to HBM, P by a row kernel, dP to HBM, dS by a second row kernel (both
-// HBM-bound, one block per row, each row read from HBM and again from cache).
+// transpose pass.  P and dP/dS live in two [heads, S, S] scratch buffers from
+// the device pool, processed in head chunks of at most 2^30 elements each; the
+// two row kernels below (probabilities, softmax backward) are HBM-bound: one
+// block per row (grid-stride), each row read once from HBM and again from
+// cache.
 #include <algorithm>
 #include <cmath>
 
-#include <cstdlib>
-
 #include "agpu_internal.cuh"
-#include "ptx.cuh"
 
 namespace agpu {
 
@@ -101,79 +91,6 @@ __global__ void __launch_bounds__(kRowThreads) attn_softmax_bwd_kernel(
   }
 }
 
-// D[row] = sum_d dO[row, d] * O[row, d] and Qs = tf32(q * scale_log2), a warp
-// per row of d (<= 256) elements.
-__global__ void __launch_bounds__(256) attn_bwd_prep_kernel(
-    const float* __restrict__ q, const float* __restrict__ dout, const float* __restrict__ o,
-    float* __restrict__ qs, float* __restrict__ dvec, long long rows, int d, float scale_log2) {
-  const int lane = threadIdx.x % 32;
-  const long long warps = (long long)gridDim.x * (blockDim.x / 32);
-  for (long long r = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows;
-       r += warps) {
-    const long long base = r * d;
-    float acc = 0.f;
-    for (int j = lane; j < d; j += 32) {
-      acc += dout[base + j] * o[base + j];
-      qs[base + j] = __uint_as_float(ptx::round_tf32(q[base + j] * scale_log2));
-    }
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) dvec[r] = acc;
-  }
-}
-
-// The TF32 path (see the file comment); AGPU_ERR_UNSUPPORTED when the
-// tensor-core forward does not take the shape (nothing left enqueued).
-agpu_status backward_from_lse(agpu_device* dev, const float* q, const float* k, const float* v,
-                              const float* dout, float* dq, float* dk, float* dv, uint32_t bh,
-                              uint32_t s, uint32_t d, bool causal, cudaStream_t st) {
-  const float scale = 1.0f / std::sqrt((float)d);
-  const float scale_log2 = scale * 1.4426950408889634f;
-  const uint64_t ss = (uint64_t)s * s, n = (uint64_t)bh * s * d, rows = (uint64_t)bh * s;
-  const uint64_t chunk = std::max<uint64_t>(1, std::min<uint64_t>(bh, (1ull << 30) / ss));
-  // O, Q', L, D, then P and dS for one head chunk (every piece 16-byte aligned)
-  const uint64_t rows4 = (rows + 3) / 4 * 4;
-  const uint64_t total = 2 * n + 2 * rows4 + 2 * chunk * ss;
-  void* buf = nullptr;
-  AGPU_TRY(pool_alloc(dev, total * sizeof(float), &buf, st));
-  float* O = static_cast<float*>(buf);
-  float* Qs = O + n;
-  float* L = Qs + n;
-  float* Dv = L + rows4;
-  float* P = Dv + rows4;
-  float* G = P + chunk * ss;
-  agpu_status rc = launch_attention_lse(dev, q, k, v, O, L, bh, s, d, causal, st);
-  if (rc == AGPU_OK) {
-    const long long wgrid = std::min<long long>(((long long)rows + 7) / 8, 16LL * dev->sm_count);
-    attn_bwd_prep_kernel<<<(unsigned)wgrid, 256, 0, st>>>(q, dout, O, Qs, Dv, (long long)rows,
-                                                          (int)d, scale_log2);
-    rc = after_launch(dev, "attn_bwd_prep_kernel");
-  }
-  for (uint64_t h0 = 0; h0 < bh && rc == AGPU_OK; h0 += chunk) {
-    const uint32_t nh = (uint32_t)std::min<uint64_t>(chunk, bh - h0);
-    const uint64_t off = h0 * s * d;
-    GemmEpilogue probs;  // P = exp2(Q'K^T - L), 0 above the diagonal when causal
-    probs.act = 4;
-    probs.rowvec = L + h0 * s;
-    probs.scale = 1.0f;
-    probs.causal = causal ? 1 : 0;
-    rc = launch_gemm_ex(dev, Qs + off, k + off, P, nh, s, s, d, false, true, probs, st);
-    // dV = P^T dO
-    if (rc == AGPU_OK) rc = launch_gemm(dev, P, dout + off, dv + off, nh, s, d, s, true, false, st);
-    GemmEpilogue dsm;  // dS = P o (dO V^T - D) / sqrt(d)
-    dsm.act = 5;
-    dsm.rowvec = Dv + h0 * s;
-    dsm.aux = P;
-    dsm.scale = scale;
-    if (rc == AGPU_OK)
-      rc = launch_gemm_ex(dev, dout + off, v + off, G, nh, s, s, d, false, true, dsm, st);
-    // dQ = dS K;  dK = dS^T Q
-    if (rc == AGPU_OK) rc = launch_gemm(dev, G, k + off, dq + off, nh, s, d, s, false, false, st);
-    if (rc == AGPU_OK) rc = launch_gemm(dev, G, q + off, dk + off, nh, s, d, s, true, false, st);
-  }
-  pool_free(dev, buf, st);
-  return rc;
-}
-
 }  // namespace
 
 agpu_status launch_attention_backward(agpu_device* dev, const float* q, const float* k,
@@ -181,14 +98,6 @@ agpu_status launch_attention_backward(agpu_device* dev, const float* q, const fl
                                       float* dv, uint32_t bh, uint32_t s, uint32_t d,
                                       bool causal, cudaStream_t st) {
   if ((uint64_t)bh * s * d == 0) return AGPU_OK;
-  static const bool lse_ok = [] {
-    const char* e = getenv("AGPU_SDPA_BWD_LSE");
-    return !(e && e[0] == '0');
-  }();
-  if (lse_ok && effective_precision(dev) == AGPU_PREC_TF32) {
-    const agpu_status r = backward_from_lse(dev, q, k, v, dout, dq, dk, dv, bh, s, d, causal, st);
-    if (r != AGPU_ERR_UNSUPPORTED) return r;
-  }
   const float scale = 1.0f / std::sqrt((float)d);
   const uint64_t ss = (uint64_t)s * s;
   const uint64_t chunk = std::max<uint64_t>(1, std::min<uint64_t>(bh, (1ull << 30) / ss));

@@ -36,7 +36,6 @@
 #include "umma2_splitk_kernel.cuh"
 #include "umma2_x3_kernel.cuh"
 #include "pair_launch.cuh"
-#include "gemm_row_epilogue.cuh"
 
 namespace agpu {
 
@@ -65,8 +64,7 @@ struct GemmPolicy {
   // fused epilogue (applied once): C = act(A*B + bias[col] + resid[row, col])
   const float* bias;   // [N] or null (Linear bias, the reference's add_per_col)
   const float* resid;  // [batch, M, N] or null (residual add)
-  int act;             // 0 none, 1 swish, 2 relu, 3 SwiGLU (paired), 4 / 5 row epilogues
-  RowEpilogue re;      // acts 4 and 5
+  int act;             // 0 none, 1 swish, 2 relu
   // MN-major operand loaded through the 4-D chunked view, one TMA box per
   // stage (else one box per 32-column chunk)
   bool a_chunked = false, b_chunked = false;
@@ -187,10 +185,7 @@ struct GemmPolicy {
             val.x += rr.x; val.y += rr.y; val.z += rr.z; val.w += rr.w;
           }
         }
-        if (last && act >= 4) {
-          val = row_epilogue(val, act, re, __ldg(re.rowvec + (long long)t.b * M + grow),
-                             re.aux + (long long)t.b * c_batch + off, grow, col);
-        } else if (last && act) {
+        if (last && act) {
           val.x = epi_act(val.x, act); val.y = epi_act(val.y, act);
           val.z = epi_act(val.z, act); val.w = epi_act(val.w, act);
         }
@@ -324,29 +319,12 @@ __global__ void __launch_bounds__(256) gemm_ffma_kernel(const float* __restrict_
       const int gn = n0 + tx * 4 + j;
       if (gn < N) {
         float v = acc[i][j];
-        if (ep.act >= 4) {
-          RowEpilogue re;
-          re.rowvec = ep.rowvec; re.aux = ep.aux; re.scale = ep.scale; re.causal = ep.causal;
-          const long long e = (long long)b * M * N + (long long)gm * N + gn;
-          C[(long long)gm * N + gn] =
-              row_epilogue1(v, ep.act, re, ep.rowvec[(long long)b * M + gm], ep.aux + e, gm, gn);
-          continue;
-        }
         if (ep.bias) v += ep.bias[gn];
         if (ep.resid) v += ep.resid[(long long)b * M * N + (long long)gm * N + gn];
         C[(long long)gm * N + gn] = epi_act(v, ep.act);
       }
     }
   }
-}
-
-RowEpilogue row_epi(const GemmEpilogue& ep) {
-  RowEpilogue re;
-  re.rowvec = ep.rowvec;
-  re.aux = ep.aux;
-  re.scale = ep.scale;
-  re.causal = ep.causal;
-  return re;
 }
 
 // ------------------------------------------------------ tensor-map encode --
@@ -475,7 +453,6 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
-  pol.re = row_epi(ep);
   auto kern = umma::umma_tf32_kernel<P, X3>;
   AGPU_CUDA((set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM)));
   const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
@@ -500,7 +477,6 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
-  pol.re = row_epi(ep);
   return launch_pair(dev, ta, tb, pol, pol.tiles, s,
                      "gemm_tf32 (umma_tf32_pair_kernel)");
 }
@@ -551,7 +527,6 @@ static agpu_status run_tc_pair_x3(agpu_device* dev, const float* a, const float*
     pol.bias = ep.bias;
     pol.resid = ep.resid;
     pol.act = ep.act;
-    pol.re = row_epi(ep);
     pol.seg = x3_seg();
     auto kern = umma::umma_x3_pair_kernel<P>;
     cudaError_t e = set_smem_once<umma::umma_x3_pair_kernel<P>>(dev, Cfg::SMEM);
@@ -599,7 +574,6 @@ static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const fl
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
-  pol.re = row_epi(ep);
   auto kern = umma::umma_tf32_pair_splitk_kernel<P, S>;
   AGPU_CUDA((set_smem_once<umma::umma_tf32_pair_splitk_kernel<P, S>>(dev, Cfg::SMEM)));
   cudaLaunchConfig_t cfg = {};
@@ -821,8 +795,7 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
   }
   const bool tiny = (uint64_t)m * n * k * batch < (1ull << 15);
   const bool vec_ep = (reinterpret_cast<uintptr_t>(ep.bias) |
-                       reinterpret_cast<uintptr_t>(ep.resid) |
-                       reinterpret_cast<uintptr_t>(ep.aux)) % 16 == 0;
+                       reinterpret_cast<uintptr_t>(ep.resid)) % 16 == 0;
   if (p == AGPU_PREC_FFMA || tiny || k == 0 || !vec_ep || !gemm_tc_eligible(a, b, c, m, n, k))
     return run_ffma(dev, a, b, c, batch, m, n, k, a_trans, b_trans, ep, s);
   if (p == AGPU_PREC_TF32X3)

@@ -38,16 +38,6 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
-// Round a finite float to tf32 (the magnitude to nearest, ties to even),
-// as bits: the tensor core would otherwise truncate an fp32 operand.  The
-// attention forward rounds its pre-scaled Q with it and the attention
-// backward rebuilds the same Q, so both see identical operands.
-__device__ __forceinline__ uint32_t round_tf32(float x) {
-  uint32_t u = __float_as_uint(x);
-  u += 0xFFFu + ((u >> 13) & 1u);
-  return u & 0xFFFFE000u;
-}
-
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

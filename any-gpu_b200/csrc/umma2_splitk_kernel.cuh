@@ -22,7 +22,6 @@
 
 #include <cuda.h>
 
-#include "gemm_row_epilogue.cuh"
 #include "ptx.cuh"
 #include "umma_kernel.cuh"
 #include "umma2_kernel.cuh"
@@ -239,11 +238,7 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
                 pol.resid + (long long)tile.b * pol.c_batch + o));
             acc.x += rr.x; acc.y += rr.y; acc.z += rr.z; acc.w += rr.w;
           }
-          if (pol.act >= 4) {
-            acc = row_epilogue(acc, pol.act, pol.re,
-                               __ldg(pol.re.rowvec + (long long)tile.b * pol.M + grow),
-                               pol.re.aux + (long long)tile.b * pol.c_batch + o, grow, col);
-          } else if (pol.act) {
+          if (pol.act) {
             acc.x = splitk_act(acc.x, pol.act); acc.y = splitk_act(acc.y, pol.act);
             acc.z = splitk_act(acc.z, pol.act); acc.w = splitk_act(acc.w, pol.act);
           }

@@ -35,9 +35,6 @@
  *                         batch_matmul + softmax pipeline
  *   AGPU_X3_SEG=N         3xTF32 on CTA pairs: K-blocks (of 32) per accumulator
  *                         segment (default 16; 0 = none: faster, less accurate)
- *   AGPU_SDPA_BWD_LSE=0   attention backward in TF32 through the general path
- *                         (P and dS by row kernels) instead of the forward's
- *                         log-sum-exp and the fused GEMM epilogues
  */
 #ifndef AGPU_H
 #define AGPU_H
