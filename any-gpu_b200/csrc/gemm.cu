@@ -68,6 +68,10 @@ struct GemmPolicy {
   // MN-major operand loaded through the 4-D chunked view, one TMA box per
   // stage (else one box per 32-column chunk)
   bool a_chunked = false, b_chunked = false;
+  // C written by TMA bulk stores (store_tma) through this map {N, M, batch},
+  // box 32 x 32, 128-byte swizzle; else by the transposing store
+  bool c_tma = false;
+  CUtensorMap tmap_c;
 
   struct Tile { int b, m0, n0; };
 
@@ -149,11 +153,78 @@ struct GemmPolicy {
     __syncwarp();
   }
 
+  // TMA store of one 32 x 32 block (c_tma): thread `lane` holds row m0 + row,
+  // columns n0 + col0 .. +31, applies the epilogue in registers and writes
+  // its row into one of the warp's two 4 KB staging buffers in the 128-byte
+  // swizzle the map expects (16-byte chunk j of row r at position j ^ r % 8,
+  // so the warp's writes spread over all banks); one lane then issues the
+  // bulk tensor store and moves on.  A buffer is rewritten two blocks later,
+  // once the store that read it has (cp.async.bulk.wait_group.read 1); the
+  // TMA unit clips rows past M and columns past N.  Blocks alternate buffers
+  // by column-chunk parity; a tile whose last live chunk is even (an edge
+  // tile with an odd chunk count) drains its stores before the next tile
+  // starts again at buffer 0.
+  __device__ void store_tma(const Tile& t, int row, int col0, const uint32_t (&v)[32],
+                            float* stg, int lane) const {
+    float* buf = stg + ((col0 >> 5) & 1) * 1024;
+    if (lane == 0) ptx::bulk_wait_read1();
+    __syncwarp();
+    const int grow = t.m0 + row, col = t.n0 + col0;
+    float4 w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                         __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (col + 4 * j < N) {
+          const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + col + 4 * j));
+          w[j].x += bb.x; w[j].y += bb.y; w[j].z += bb.z; w[j].w += bb.w;
+        }
+    }
+    if (resid && grow < M) {
+      const float* rp = resid + (long long)t.b * c_batch + (long long)grow * N + col;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (col + 4 * j < N) {
+          const float4 rr = __ldg(reinterpret_cast<const float4*>(rp + 4 * j));
+          w[j].x += rr.x; w[j].y += rr.y; w[j].z += rr.z; w[j].w += rr.w;
+        }
+    }
+    if (act) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        w[j].x = epi_act(w[j].x, act); w[j].y = epi_act(w[j].y, act);
+        w[j].z = epi_act(w[j].z, act); w[j].w = epi_act(w[j].w, act);
+      }
+    }
+    uint8_t* rowp = reinterpret_cast<uint8_t*>(buf) + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) = w[j];
+    ptx::fence_proxy_async_smem();  // the async proxy (TMA) sees the staged block
+    __syncwarp();
+    const int row_base = grow - lane;
+    if (lane == 0) {
+      if (row_base < M && col < N) {
+        ptx::tma_store_3d(&tmap_c, buf, col, row_base, t.b);
+        ptx::bulk_commit();
+      }
+      if (((col0 >> 5) & 1) == 0 && (col0 + 32 >= BN || col + 32 >= N)) ptx::bulk_wait_read0();
+    }
+  }
+
   // Thread `lane` holds row (row_base + lane), columns n0+col0 .. +31.  The
   // warp transposes its 32x32 block through shared memory so that each
-  // store instruction writes four full 128-byte row segments.
+  // store instruction writes four full 128-byte row segments.  A tile's only
+  // (last, not accumulating) write goes through store_tma when the map is set.
   __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float* stg,
                         int lane, bool accumulate, bool last) const {
+    if (c_tma && last && !accumulate) {
+      store_tma(t, row, col0, v, stg, lane);
+      return;
+    }
     float4* srow = reinterpret_cast<float4*>(stg + lane * kEpiStride);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -433,6 +504,23 @@ static agpu_status make_gemm_maps(CUtensorMap* ta, CUtensorMap* tb, P* pol, cons
   return AGPU_OK;
 }
 
+// The map of C for the TMA-store epilogue: {N, M, batch}, 32 x 32 boxes,
+// 128-byte swizzle (AGPU_GEMM_TMA_STORE=0: the transposing store instead).
+// SwiGLU writes an N/2-wide C through its own store.
+template <class P>
+static agpu_status make_c_map(P* pol, float* c, uint32_t batch, uint32_t m, uint32_t n, int act) {
+  static const bool enabled = [] {
+    const char* e = getenv("AGPU_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  pol->c_tma = false;
+  if (!enabled || act == 3 || n % 4 != 0 || (reinterpret_cast<uintptr_t>(c) & 15) != 0)
+    return AGPU_OK;
+  AGPU_TRY(make_tmap_f32_3d(&pol->tmap_c, c, n, m, batch, (uint64_t)m * n, 32, 32, false, false));
+  pol->c_tma = true;
+  return AGPU_OK;
+}
+
 template <int BN, bool A_MN, bool B_MN, bool X3>
 static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, float* c,
                           uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
@@ -453,6 +541,7 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
+  AGPU_TRY(make_c_map(&pol, c, batch, m, n, ep.act));
   auto kern = umma::umma_tf32_kernel<P, X3>;
   AGPU_CUDA((set_smem_once<umma::umma_tf32_kernel<P, X3>>(dev, Cfg::SMEM)));
   const long long grid = std::min<long long>(pol.tiles, dev->sm_count);
@@ -477,6 +566,7 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
+  AGPU_TRY(make_c_map(&pol, c, batch, m, n, ep.act));
   return launch_pair(dev, ta, tb, pol, pol.tiles, s,
                      "gemm_tf32 (umma_tf32_pair_kernel)");
 }
@@ -528,6 +618,9 @@ static agpu_status run_tc_pair_x3(agpu_device* dev, const float* a, const float*
     pol.resid = ep.resid;
     pol.act = ep.act;
     pol.seg = x3_seg();
+    st = make_c_map(&pol, c, batch, m, n, ep.act);
+  }
+  if (st == AGPU_OK) {
     auto kern = umma::umma_x3_pair_kernel<P>;
     cudaError_t e = set_smem_once<umma::umma_x3_pair_kernel<P>>(dev, Cfg::SMEM);
     if (e == cudaSuccess) {

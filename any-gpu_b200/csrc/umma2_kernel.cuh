@@ -43,7 +43,7 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 4;            // 128 rows per CTA
   static constexpr int B_BYTES = (BN / 2) * BK * 4;      // BN/2 columns per CTA
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int EPI_BYTES = kEpiWarps * 32 * kEpiStride * 4;
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiWarpFloats * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - EPI_BYTES - BAR_BYTES;
   static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
@@ -62,7 +62,7 @@ struct PairCfg {
 template <class P>
 __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     umma_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                          const __grid_constant__ CUtensorMap tmap_b, const P pol,
+                          const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ P pol,
                           unsigned int* status) {
   using C = PairCfg<P::BN>;
   constexpr int BN = P::BN;
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     }
   } else {
     const int q = warp & 3;
-    float* stg = epi + (warp - 2) * 32 * kEpiStride;
+    float* stg = epi + (warp - 2) * kEpiWarpFloats;
     int local = 0;
     for (long long t = cluster_id; t < num_tiles; t += n_clusters, ++local) {
       const auto tile = pol.rank_tile(pol.tile(t), rank);
@@ -236,6 +236,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     }
   }
 
+  // the epilogue's bulk (TMA) stores of C are complete before the CTA exits
+  if (warp >= 2 && lane == 0) ptx::bulk_wait0();
   __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();

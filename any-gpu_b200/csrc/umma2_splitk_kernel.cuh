@@ -59,7 +59,7 @@ __device__ __forceinline__ float splitk_act(float x, int act) {
 template <class P, int S>
 __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     umma_tf32_pair_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                 const __grid_constant__ CUtensorMap tmap_b, const P pol,
+                                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ P pol,
                                  unsigned int* status) {
   using C = PairCfg<P::BN>;
   constexpr int BN = P::BN;

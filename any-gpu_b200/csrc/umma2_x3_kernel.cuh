@@ -42,7 +42,7 @@ struct PairX3Cfg {
   static constexpr int B_BYTES = (BN / 2) * BK * 4;    // BN/2 columns per CTA
   static constexpr int HI_BYTES = A_BYTES + B_BYTES;   // the operands as stored
   static constexpr int STAGE_BYTES = 2 * HI_BYTES;     // + their lo parts
-  static constexpr int EPI_BYTES = kEpiWarps * 32 * kEpiStride * 4;
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiWarpFloats * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - EPI_BYTES - BAR_BYTES;
   static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(PairX3Cfg<P::BN>::THREADS, 1)
     umma_x3_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_alo,
-                        const __grid_constant__ CUtensorMap tmap_blo, const P pol,
+                        const __grid_constant__ CUtensorMap tmap_blo, const __grid_constant__ P pol,
                         unsigned int* status) {
   using C = PairX3Cfg<P::BN>;
   constexpr int BN = P::BN;
@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(PairX3Cfg<P::BN>::THREADS, 1)
     }
   } else {
     const int q = warp & 3;
-    float* stg = epi + (warp - 2) * 32 * kEpiStride;
+    float* stg = epi + (warp - 2) * kEpiWarpFloats;
     long long unit = 0;
     bool ok = true;
     for (long long t = cluster_id; t < num_tiles && ok; t += n_clusters) {
@@ -291,6 +291,8 @@ __global__ void __launch_bounds__(PairX3Cfg<P::BN>::THREADS, 1)
     }
   }
 
+  // the epilogue's bulk (TMA) stores of C are complete before the CTA exits
+  if (warp >= 2 && lane == 0) ptx::bulk_wait0();
   __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();

@@ -35,6 +35,10 @@ constexpr int BM = 128;
 constexpr int BK = 32;          // fp32 elements per 128-byte swizzle row
 constexpr int kEpiWarps = 4;
 constexpr int kEpiStride = 36;  // floats per epilogue staging row (conflict-free float4)
+// Epilogue staging per warp: two 32 x 32 fp32 buffers (4 KB each, 1024-byte
+// aligned) for the TMA-store epilogue; the transposing store uses the first
+// 32 x kEpiStride floats.
+constexpr int kEpiWarpFloats = 2048;
 constexpr int kSegX3 = 16;      // K-blocks per accumulator segment in 3xTF32 mode
 
 template <int BN_, bool X3>
@@ -43,7 +47,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int EPI_BYTES = kEpiWarps * 32 * kEpiStride * 4;
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiWarpFloats * 4;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - EPI_BYTES - BAR_BYTES;
   static constexpr int STAGES_RAW = BUDGET / (STAGE_BYTES * (X3 ? 2 : 1));
@@ -95,7 +99,7 @@ __device__ __forceinline__ void split_tf32(uint32_t* hi, uint32_t* lo, int words
 template <class P, bool X3>
 __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
     umma_tf32_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                     const __grid_constant__ CUtensorMap tmap_b, const P pol,
+                     const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ P pol,
                      unsigned int* status) {
   using C = Cfg<P::BN, X3>;
   constexpr int BN = P::BN;
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
     }
   } else if (warp < 2 + kEpiWarps) {
     const int q = warp & 3;  // TMEM sub-partition this warp may access
-    float* stg = epi + (warp - 2) * 32 * kEpiStride;
+    float* stg = epi + (warp - 2) * kEpiWarpFloats;
     int local = 0;
     bool ok = true;
     for (long long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -274,6 +278,9 @@ __global__ void __launch_bounds__(Cfg<P::BN, X3>::THREADS, 1)
     }
   }
 
+  // the epilogue's bulk (TMA) stores of C are complete before the CTA exits
+  if (warp >= 2 && lane == 0) ptx::bulk_wait0();
+  __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -35,6 +35,8 @@
  *                         batch_matmul + softmax pipeline
  *   AGPU_X3_SEG=N         3xTF32 on CTA pairs: K-blocks (of 32) per accumulator
  *                         segment (default 16; 0 = none: faster, less accurate)
+ *   AGPU_GEMM_TMA_STORE=0 GEMM outputs by the warp-transposing float4 store
+ *                         instead of TMA bulk tensor stores (bit-identical)
  */
 #ifndef AGPU_H
 #define AGPU_H
