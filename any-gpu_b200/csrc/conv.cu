@@ -34,6 +34,7 @@ namespace agpu {
 agpu_status make_tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
                              uint64_t batch, uint64_t batch_stride_elems, uint32_t box_inner,
                              uint32_t box_outer, bool mn_major, bool round_tf32);
+bool tma_store_enabled();
 
 using umma::BK;
 using umma::BM;
@@ -68,6 +69,11 @@ struct ConvPolicy {
   long long tiles;
   const float* bias;  // may be null
   float* out;
+  // output by TMA bulk stores (store_tma) through the map {Wo, Ho, Cout, N}
+  // with 32 x 1 x 32 boxes; needs BW >= 32, so that a warp's 32 tile rows
+  // are 32 consecutive pixels of one output row
+  bool c_tma = false;
+  CUtensorMap tmap_y;
 
   struct Tile { int n, oh0, ow0, oc0; };
 
@@ -101,8 +107,42 @@ struct ConvPolicy {
   __device__ void store_swiglu(const Tile&, int, int, const uint32_t (&)[32],
                                const uint32_t (&)[32], float*, int) const {}
 
-  __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float*,
-                        int, bool accumulate, bool) const {
+  // Thread `lane` holds pixel (oh, ow0 + lane) of the warp's output row,
+  // channels oc0 + col0 .. +31; it writes column `lane` of a [32 channels]
+  // [32 pixels] block (conflict-free: one bank per lane) into one of the
+  // warp's two 4 KB staging buffers, and one lane issues the bulk tensor
+  // store (clipped at Wo, Ho and Cout by the map).  Buffers alternate by
+  // column-chunk parity as in the GEMM's store_tma.
+  __device__ void store_tma(const Tile& t, int row, int col0, const uint32_t (&v)[32],
+                            float* stg, int lane) const {
+    float* buf = stg + ((col0 >> 5) & 1) * 1024;
+    if (lane == 0) ptx::bulk_wait_read1();
+    __syncwarp();
+    const int oc_lane = t.oc0 + col0 + lane;
+    const float b_lane = (bias && oc_lane < cout) ? __ldg(bias + oc_lane) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      buf[j * 32 + lane] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, b_lane, j);
+    ptx::fence_proxy_async_smem();  // the async proxy (TMA) sees the staged block
+    __syncwarp();
+    if (lane == 0) {
+      const int r0 = row - lane;  // the warp's first tile row
+      const int oh = t.oh0 + r0 / BW, ow = t.ow0 + r0 % BW;
+      if (oh < Ho && ow < Wo) {
+        ptx::tma_store_4d(&tmap_y, buf, ow, oh, t.oc0 + col0, t.n);
+        ptx::bulk_commit();
+      }
+      if (((col0 >> 5) & 1) == 0 && (col0 + 32 >= BN || t.oc0 + col0 + 32 >= cout))
+        ptx::bulk_wait_read0();
+    }
+  }
+
+  __device__ void store(const Tile& t, int row, int col0, const uint32_t (&v)[32], float* stg,
+                        int lane, bool accumulate, bool last) const {
+    if (c_tma && last && !accumulate) {
+      store_tma(t, row, col0, v, stg, lane);
+      return;
+    }
     const int oh = t.oh0 + row / BW, ow = t.ow0 + row % BW;
     if (oh >= Ho || ow >= Wo) return;
     const long long plane = (long long)Ho * Wo;
@@ -496,6 +536,22 @@ agpu_status conv_tc_staged(agpu_device* dev, const ConvParams& p, const float* x
 
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(AGPU_ERR_CUDA, "no cuTensorMapEncodeTiled");
+  pol.c_tma = false;
+  if (tma_store_enabled() && pol.BW >= 32 && p.wo % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    cuuint64_t dims[4] = {(cuuint64_t)p.wo, (cuuint64_t)p.ho, (cuuint64_t)p.cout,
+                          (cuuint64_t)p.n};
+    cuuint64_t strides[3] = {(cuuint64_t)p.wo * 4, (cuuint64_t)p.ho * p.wo * 4,
+                             (cuuint64_t)p.cout * p.ho * p.wo * 4};
+    cuuint32_t box[4] = {32, 1, 32, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(&pol.tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(AGPU_ERR_CUDA, "conv2d: output tensor map encode failed (%d)", (int)r);
+    pol.c_tma = true;
+  }
   CUtensorMap ta, tb;
   {
     cuuint64_t dims[4] = {(cuuint64_t)Cs, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};

@@ -27,7 +27,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <climits>
 #include <cstdlib>
+#include <cstring>
 
 #include "agpu_internal.cuh"
 #include "ptx.cuh"
@@ -507,14 +509,18 @@ static agpu_status make_gemm_maps(CUtensorMap* ta, CUtensorMap* tb, P* pol, cons
 // The map of C for the TMA-store epilogue: {N, M, batch}, 32 x 32 boxes,
 // 128-byte swizzle (AGPU_GEMM_TMA_STORE=0: the transposing store instead).
 // SwiGLU writes an N/2-wide C through its own store.
-template <class P>
-static agpu_status make_c_map(P* pol, float* c, uint32_t batch, uint32_t m, uint32_t n, int act) {
+bool tma_store_enabled() {
   static const bool enabled = [] {
     const char* e = getenv("AGPU_GEMM_TMA_STORE");
     return !(e && e[0] == '0');
   }();
+  return enabled;
+}
+
+template <class P>
+static agpu_status make_c_map(P* pol, float* c, uint32_t batch, uint32_t m, uint32_t n, int act) {
   pol->c_tma = false;
-  if (!enabled || act == 3 || n % 4 != 0 || (reinterpret_cast<uintptr_t>(c) & 15) != 0)
+  if (!tma_store_enabled() || act == 3 || n % 4 != 0 || (reinterpret_cast<uintptr_t>(c) & 15) != 0)
     return AGPU_OK;
   AGPU_TRY(make_tmap_f32_3d(&pol->tmap_c, c, n, m, batch, (uint64_t)m * n, 32, 32, false, false));
   pol->c_tma = true;
@@ -648,19 +654,20 @@ static agpu_status run_tc_pair_x3(agpu_device* dev, const float* a, const float*
   return st;
 }
 
-// Split-K over a cluster of S CTA pairs per 256 x 256 tile (S = 2 or 4).
-template <bool A_MN, bool B_MN, int S>
+// Split-K over a cluster of S CTA pairs per 256 x BN tile (S = 2 or 4,
+// BN = 256 or 128).
+template <int BN, bool A_MN, bool B_MN, int S>
 static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const float* b, float* c,
                                       uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                       const GemmEpilogue& ep, cudaStream_t s) {
-  using P = GemmPairPolicy<256, A_MN, B_MN>;
-  using Cfg = umma::PairCfg<256>;
+  using P = GemmPairPolicy<BN, A_MN, B_MN>;
+  using Cfg = umma::PairCfg<BN>;
   CUtensorMap ta, tb;
   P pol;
   AGPU_TRY(make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, P::HALF, true));
   pol.M = m; pol.N = n; pol.K = k;
   pol.tiles_m = (int)ceil_div(m, P::PM);
-  pol.tiles_n = (int)ceil_div(n, 256);
+  pol.tiles_n = (int)ceil_div(n, BN);
   pol.tiles = (long long)pol.tiles_m * pol.tiles_n * batch;
   pol.C = c;
   pol.c_batch = (long long)m * n;
@@ -689,13 +696,13 @@ static agpu_status run_tc_pair_splitk(agpu_device* dev, const float* a, const fl
 
 // Clusters of 2*S CTAs of the split-K kernel that fit on the device at once
 // (a cluster occupies 2*S SMs of one GPC: 15 of 8 CTAs on a B200).
-template <int S>
+template <int BN, int S>
 static int splitk_max_clusters(agpu_device* dev) {
   static std::atomic<int> cached{-1};
   int v = cached.load(std::memory_order_acquire);
   if (v >= 0) return v;
-  using P = GemmPairPolicy<256, false, true>;
-  using Cfg = umma::PairCfg<256>;
+  using P = GemmPairPolicy<BN, false, true>;
+  using Cfg = umma::PairCfg<BN>;
   int n = 0;
   if (set_smem_once<umma::umma_tf32_pair_splitk_kernel<P, S>>(dev, Cfg::SMEM) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -719,23 +726,57 @@ static int splitk_max_clusters(agpu_device* dev) {
   return n;
 }
 
-// K slices for a pair GEMM whose 256 x 256 tiles leave most SM pairs idle:
-// the largest S in {4, 2} whose clusters (one per tile) all fit at once, with
-// >= 2 K-blocks per slice and fewer tiles than half the SM pairs; else 1
-// (AGPU_GEMM_SPLITK=0 disables).
-static int splitk_slices(agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n, uint32_t k) {
-  static const bool enabled = [] {
+// Split-K plan for a pair GEMM whose 256 x 256 tiles leave most SM pairs
+// idle (fewer tiles than half the pairs): among 256 x 256 and 256 x 128 tiles
+// with S = 4 or 2 K slices -- all S * tiles pairs busy at once, every tile's
+// cluster resident at once, >= 2 K-blocks per slice -- the one with the least
+// MMA work per pair (tile columns x K-blocks per slice), wider tiles first on
+// a tie (fewer operand bytes per FLOP); else s = 1, no split.
+// AGPU_GEMM_SPLITK=0 disables, =256 keeps 256-column tiles.
+struct SplitK {
+  int bn, s;
+};
+
+static SplitK splitk_plan(agpu_device* dev, uint32_t batch, uint32_t m, uint32_t n, uint32_t k) {
+  static const int mode = [] {
     const char* e = getenv("AGPU_GEMM_SPLITK");
-    return !(e && e[0] == '0');
+    if (e && e[0] == '0') return 0;
+    if (e && strcmp(e, "256") == 0) return 2;
+    return 1;
   }();
-  if (!enabled) return 1;
+  SplitK best{256, 1};
+  if (mode == 0) return best;
   const long long pairs = std::max(1, dev->sm_count / 2);
-  const long long tiles = (long long)ceil_div(m, 256) * ceil_div(n, 256) * batch;
   const long long nk = ceil_div(k, BK);
-  if (2 * tiles > pairs) return 1;
-  if (nk >= 8 && tiles <= splitk_max_clusters<4>(dev)) return 4;
-  if (nk >= 4 && tiles <= splitk_max_clusters<2>(dev)) return 2;
-  return 1;
+  if (2 * (long long)ceil_div(m, 256) * ceil_div(n, 256) * batch > pairs) return best;
+  long long best_work = LLONG_MAX;
+  const SplitK cand[4] = {{256, 4}, {256, 2}, {128, 4}, {128, 2}};
+  for (const SplitK& c : cand) {
+    if (c.bn == 128 && mode == 2) continue;
+    const long long tiles = (long long)ceil_div(m, 256) * ceil_div(n, c.bn) * batch;
+    if (tiles * c.s > pairs || nk < 2 * c.s) continue;
+    const int fit = c.bn == 256 ? (c.s == 4 ? splitk_max_clusters<256, 4>(dev)
+                                            : splitk_max_clusters<256, 2>(dev))
+                                : (c.s == 4 ? splitk_max_clusters<128, 4>(dev)
+                                            : splitk_max_clusters<128, 2>(dev));
+    if (tiles > fit) continue;
+    const long long work = (long long)c.bn * ceil_div(nk, c.s);
+    if (work < best_work) {
+      best = c;
+      best_work = work;
+    }
+  }
+  return best;
+}
+
+template <int BN, int S>
+static agpu_status run_splitk_layout(agpu_device* dev, const float* a, const float* b, float* c,
+                                     uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool at,
+                                     bool bt, const GemmEpilogue& ep, cudaStream_t s) {
+  if (!at && !bt) return run_tc_pair_splitk<BN, false, true, S>(dev, a, b, c, batch, m, n, k, ep, s);
+  if (!at && bt) return run_tc_pair_splitk<BN, false, false, S>(dev, a, b, c, batch, m, n, k, ep, s);
+  if (at && !bt) return run_tc_pair_splitk<BN, true, true, S>(dev, a, b, c, batch, m, n, k, ep, s);
+  return run_tc_pair_splitk<BN, true, false, S>(dev, a, b, c, batch, m, n, k, ep, s);
 }
 
 // The CTA-pair kernel serves TF32 GEMMs with at least one full 256 x 256 tile;
@@ -788,19 +829,15 @@ static agpu_status dispatch_tc(agpu_device* dev, const float* a, const float* b,
     return run_tc_pair_x3<true, false>(dev, a, b, c, batch, m, n, k, ep, s);
   }
   if (!X3 && use_pair(m, n)) {
-    const int sl = splitk_slices(dev, batch, m, n, k);
-    if (sl == 4) {
-      if (!at && !bt) return run_tc_pair_splitk<false, true, 4>(dev, a, b, c, batch, m, n, k, ep, s);
-      if (!at && bt) return run_tc_pair_splitk<false, false, 4>(dev, a, b, c, batch, m, n, k, ep, s);
-      if (at && !bt) return run_tc_pair_splitk<true, true, 4>(dev, a, b, c, batch, m, n, k, ep, s);
-      return run_tc_pair_splitk<true, false, 4>(dev, a, b, c, batch, m, n, k, ep, s);
-    }
-    if (sl == 2) {
-      if (!at && !bt) return run_tc_pair_splitk<false, true, 2>(dev, a, b, c, batch, m, n, k, ep, s);
-      if (!at && bt) return run_tc_pair_splitk<false, false, 2>(dev, a, b, c, batch, m, n, k, ep, s);
-      if (at && !bt) return run_tc_pair_splitk<true, true, 2>(dev, a, b, c, batch, m, n, k, ep, s);
-      return run_tc_pair_splitk<true, false, 2>(dev, a, b, c, batch, m, n, k, ep, s);
-    }
+    const SplitK sk = splitk_plan(dev, batch, m, n, k);
+    if (sk.s == 4 && sk.bn == 256)
+      return run_splitk_layout<256, 4>(dev, a, b, c, batch, m, n, k, at, bt, ep, s);
+    if (sk.s == 2 && sk.bn == 256)
+      return run_splitk_layout<256, 2>(dev, a, b, c, batch, m, n, k, at, bt, ep, s);
+    if (sk.s == 4 && sk.bn == 128)
+      return run_splitk_layout<128, 4>(dev, a, b, c, batch, m, n, k, at, bt, ep, s);
+    if (sk.s == 2 && sk.bn == 128)
+      return run_splitk_layout<128, 2>(dev, a, b, c, batch, m, n, k, at, bt, ep, s);
     if (use_wide(dev, batch, m, n, k)) {
       if (!at && !bt) return run_tc_pair<512, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
       if (!at && bt) return run_tc_pair<512, false, false>(dev, a, b, c, batch, m, n, k, ep, s);
@@ -861,7 +898,7 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
     // over the 32-column block pairs (rows of 64: gate 32 | up 32)
     const bool fused = p == AGPU_PREC_TF32 && !ep.bias && !ep.resid && n % 64 == 0 &&
                        use_pair(m, n) && gemm_tc_eligible(a, b, c, m, n, k) &&
-                       splitk_slices(dev, batch, m, n, k) == 1;
+                       splitk_plan(dev, batch, m, n, k).s == 1;
     if (fused) {
       if (use_wide(dev, batch, m, n, k)) {
         if (!a_trans && !b_trans) return run_tc_pair<512, false, true>(dev, a, b, c, batch, m, n, k, ep, s);

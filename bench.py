@@ -495,9 +495,11 @@ class Matmul(Workload):
         super().__init__(args, world, rank, replicas)
         self.dom_kernel = (
             "umma_tf32_kernel<GemmPolicy<128|256, 3xTF32>> (single CTA, K segments)"
-            if precision == "tf32x3" else
+            if self.precision == "tf32x3" and n < 256 else
+            "umma_x3_pair_kernel<GemmPairX3Policy<256>> (CTA pairs, K segments summed in TMEM)"
+            if self.precision == "tf32x3" else
             "umma_tf32_kernel<GemmPolicy<128|256>> (single CTA)" if n < 256 else
-            "umma_tf32_pair_splitk_kernel<GemmPairPolicy<256>, 4|2> (cluster split-K)"
+            "umma_tf32_pair_splitk_kernel<GemmPairPolicy<256|128>, 4|2> (cluster split-K)"
             if n <= 1024 else "umma_tf32_pair_kernel<GemmPairPolicy<256|512>>")
         ws = 3 * n * n * 4
         self.l2 = (f"working set {ws / 2**20:.1f} MiB "

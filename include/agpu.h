@@ -25,6 +25,7 @@
  * on by default; results stay within the documented tolerances either way):
  *   AGPU_GEMM_PAIR=0      TF32 GEMMs on single-CTA 128-row tiles, not CTA pairs
  *   AGPU_GEMM_SPLITK=0    no cluster split-K for GEMMs with few tiles
+ *                         (=256: split-K on 256 x 256 tiles only, not 256 x 128)
  *   AGPU_GEMM_WIDE=0|2    never / always 256 x 512 pair tiles (default: estimate)
  *   AGPU_GEMM_CHUNKED=0   MN-major operands by one TMA box per 32 columns
  *                         (bit-identical output)

@@ -98,14 +98,15 @@ def test_gemm_transposed_operands(dev, orc, ta, tb, batch, m, n, k, prec):
 
 
 @pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("batch,m,n,k", [(1, 256, 256, 256),     # 1 tile, 4 K slices
-                                         (1, 1024, 1024, 1024),  # 16 tiles, 4 slices
-                                         (2, 512, 512, 2048),    # 8 tiles, 4 slices
-                                         (1, 1280, 1536, 512),   # 30 tiles, 2 slices
-                                         (1, 300, 520, 132)])    # ragged M, N and K
+@pytest.mark.parametrize("batch,m,n,k", [(1, 256, 256, 256),     # 2 tiles of 256x128, 4 slices
+                                         (1, 1024, 1024, 1024),  # 32 tiles of 256x128, 2 slices
+                                         (2, 512, 512, 2048),    # 8 tiles of 256x256, 4 slices
+                                         (1, 1280, 1536, 512),   # 30 tiles of 256x256, 2 slices
+                                         (1, 300, 520, 132)])    # 256x128, ragged M, N and K
 def test_gemm_split_k_cluster(dev, orc, ta, tb, batch, m, n, k):
     """GEMMs with too few 256 x 256 tiles for the SM pairs run K-split over a
-    cluster of pairs, the partials summed through distributed shared memory."""
+    cluster of pairs (256 x 256 or 256 x 128 tiles, 4 or 2 slices), the
+    partials summed through distributed shared memory."""
     r = np.random.default_rng(m + n + k)
     a = r.uniform(-1, 1, batch * m * k).astype(np.float32)
     b = r.uniform(-1, 1, batch * k * n).astype(np.float32)
