@@ -195,7 +195,12 @@ class Workload:
         self.total = self.total_items()
         self.sharded = world > 1 and self.shardable and not replicas
         w, r = (world, rank) if self.sharded else (1, 0)
-        rounds = max(1, (self.total // world) // self.round_items) if self.sharded else 1
+        rounds = 1
+        if self.sharded:
+            per_rank = self.total // world
+            rounds = max(1, per_rank // self.round_items)
+            if args.rounds:
+                rounds = max(1, min(args.rounds, per_rank))
         self.plan = ShardPlan(self.total, w, r, rounds)
         self.local = self.plan.my_count
         self.job_items = self.total if (self.sharded or world == 1) else self.total * world
@@ -373,6 +378,9 @@ class BmmSoftmax(Workload):
     l2 = "inputs 2 GiB + output 1 GiB > 126 MB L2 (no flush needed)"
     item = "batch item"
     seed = 1235
+    # 8 items per round: at N = 8 one round, whose 128 MiB copies per peer
+    # reach 712 GB/s received; 4 rounds of 32 MiB copies measured 545 against
+    # 655 TFLOPS (their gathers slower by more than the compute they hide)
     round_items = 8
     M = N = K = 2048
     item_elems = {"a": M * K, "b": K * N}
@@ -1285,6 +1293,8 @@ def main():
                     help="N > 1: every rank runs the whole config, no collective (weak)")
     ap.add_argument("--comm", choices=["ce", "nccl"], default="ce",
                     help="N > 1 output gathers: copy engines over CUDA IPC, or NCCL collectives")
+    ap.add_argument("--rounds", type=int, default=0,
+                    help="N > 1: rounds of the sharded step (0: the workload's default)")
     ap.add_argument("--ce-streams", type=int, default=1,
                     help="copy streams of the copy-engine gathers (peers spread over them)")
     ap.add_argument("--ce-sync", choices=["flags", "events"], default="flags",

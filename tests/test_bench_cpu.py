@@ -40,7 +40,7 @@ def test_bench_workload_plans_cpu():
     import argparse
     import bench
     args = argparse.Namespace(batch=64, size=512, precision="tf32", bh=256, seq=2048, images=16,
-                              llama_batch=32, graph=None)
+                              llama_batch=32, graph=None, rounds=0)
     for cls in (bench.BmmSoftmax, bench.Sdpa, bench.Unet, bench.Llama):
         one = cls(args, 1, 0)
         assert one.scaling() == "strong" and one.local == one.total
@@ -49,6 +49,8 @@ def test_bench_workload_plans_cpu():
             assert all(w.flops == one.flops for w in ranks)
             assert sum(w.local for w in ranks) == one.total
             assert all(w.scaling() == "strong" and w.sharded for w in ranks)
+            if cls is bench.BmmSoftmax:  # 8 items per rank per round
+                assert all(len(w.plan.spans) == max(1, 64 // world // 8) for w in ranks)
             rep = cls(args, world, 0, replicas=True)
             assert rep.scaling() == "weak" and rep.flops == world * one.flops
     mm = bench.Matmul(args, 4, 1)
