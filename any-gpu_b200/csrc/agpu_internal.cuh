@@ -123,7 +123,20 @@ struct GemmEpilogue {
   const float* bias = nullptr;   // [n] or null
   const float* resid = nullptr;  // [batch, m, n] or null (may alias nothing but C's shape)
   int act = 0;                   // 0 none, 1 swish, 2 relu
+  // Row-vector modes for the attention backward (C = A B^T with no bias,
+  // resid or act; only on the TF32 CTA-pair kernel -- launch_gemm_ex returns
+  // AGPU_ERR_UNSUPPORTED, launching nothing, where that kernel does not run
+  // the GEMM whole):
+  //   mode 1: C = 2^(A*B * scale - rowvec[batch, row]), 0 where col > row if causal
+  //   mode 2: C = C o (A*B - rowvec[batch, row]) * scale  (C read, then overwritten)
+  int mode = 0;
+  const float* rowvec = nullptr;  // [batch, m]
+  float scale = 1.0f;
+  bool causal = false;
 };
+// Whether launch_gemm_ex would run a row-vector mode for this shape.
+bool gemm_rowvec_mode_ok(agpu_device* dev, const float* a, const float* b, const float* c,
+                         uint32_t batch, uint32_t m, uint32_t n, uint32_t k);
 agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
                            uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
                            bool b_trans, const GemmEpilogue& ep, cudaStream_t s);
@@ -159,8 +172,14 @@ agpu_status launch_attention_strided(agpu_device* dev, const float* q, const flo
 agpu_status launch_attention(agpu_device* dev, const float* q, const float* k, const float* v,
                              float* o, uint32_t bh, uint32_t s, uint32_t d, bool causal,
                              cudaStream_t st);
-// dQ, dK, dV of attention from dO (recomputes P; tensor-core GEMMs + two row
-// kernels; scratch from the device pool).
+// The forward on CTA pairs writing each row's log-sum-exp of its base-2
+// scores (P = 2^(q.k / sqrt(d) * log2 e - lse)) to lse [bh, s];
+// AGPU_ERR_UNSUPPORTED, launching nothing, where the pair kernel does not run.
+agpu_status launch_attention_lse(agpu_device* dev, const float* q, const float* k,
+                                 const float* v, float* o, float* lse, uint32_t bh, uint32_t s,
+                                 uint32_t d, bool causal, cudaStream_t st);
+// dQ, dK, dV of attention from dO (recomputes P; tensor-core GEMMs; scratch
+// from the device pool).
 agpu_status launch_attention_backward(agpu_device* dev, const float* q, const float* k,
                                       const float* v, const float* dout, float* dq, float* dk,
                                       float* dv, uint32_t bh, uint32_t s, uint32_t d,

@@ -528,12 +528,12 @@ struct PairAttnCfg {
   static_assert(2 * KB + 2 * D <= 512, "tensor memory budget");
 };
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool LSE>
 __global__ void __launch_bounds__(kPairAttnThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, AttnQ qin,
                           float* __restrict__ out, int S, float scale_log2, AttnOut ol,
-                          AttnTiles tiles, unsigned int* status) {
+                          AttnTiles tiles, unsigned int* status, float* __restrict__ lse) {
   using C = PairAttnCfg<D>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -800,6 +800,7 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
       const int nb = blocks(q0);
       const int qrow = q0 + rank * QT + row;
       float m_used = -INFINITY, l = 0.f;
+      [[maybe_unused]] float lx = 0.f;  // LSE: the sum of P before truncation
       for (int j = 0; j < nb; ++j, ++g) {
         const int sb = (int)(g & 1);
         if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(&s_full[sb], (uint32_t)((g >> 1) & 1),
@@ -867,6 +868,7 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
               }
             }
             l *= alpha;
+            if constexpr (LSE) lx *= alpha;
             m_used = m_new;
           }
         }
@@ -874,10 +876,22 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
           // P truncated to tf32 as the tensor core reads it; l sums exactly
           // those values, so P / l sums to one
           float ls[4] = {0.f, 0.f, 0.f, 0.f};
+          if constexpr (LSE) {
+            float lxs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int k = 0; k < 64; ++k) {
-            v[k] = __float_as_uint(ex2(__uint_as_float(v[k]) - m_used)) & 0xFFFFE000u;
-            ls[k & 3] += __uint_as_float(v[k]);
+            for (int k = 0; k < 64; ++k) {
+              const float e = ex2(__uint_as_float(v[k]) - m_used);
+              lxs[k & 3] += e;
+              v[k] = __float_as_uint(e) & 0xFFFFE000u;
+              ls[k & 3] += __uint_as_float(v[k]);
+            }
+            lx += (lxs[0] + lxs[1]) + (lxs[2] + lxs[3]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 64; ++k) {
+              v[k] = __float_as_uint(ex2(__uint_as_float(v[k]) - m_used)) & 0xFFFFE000u;
+              ls[k & 3] += __uint_as_float(v[k]);
+            }
           }
           l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
           ptx::tmem_st32(sbase, v0);
@@ -892,6 +906,15 @@ __global__ void __launch_bounds__(kPairAttnThreads, 1)
       lsum[h * 128 + row] = l;
       ptx::named_bar_sync(1 + q, 64);
       l += lsum[(h ^ 1) * 128 + row];
+      if constexpr (LSE) {
+        // the row's log-sum-exp of its base-2 scores (P = 2^(s - lse)), from
+        // the untruncated sum; lsum is reused once the partner has read l
+        ptx::named_bar_sync(1 + q, 64);
+        lsum[h * 128 + row] = lx;
+        ptx::named_bar_sync(1 + q, 64);
+        lx += lsum[(h ^ 1) * 128 + row];
+        if (h == 0 && qrow < S) lse[((long long)bat * tiles.H + head) * S + qrow] = m_used + log2f(lx);
+      }
       if (ok) ok = __all_sync(0xffffffffu, ptx::mbar_wait(o_full, (uint32_t)(tile_i & 1),
                                                           status, 0x22a, abort_flag));
       if (ok) {
@@ -1086,7 +1109,7 @@ agpu_status run_attention_tc(agpu_device* dev, const float* q, const float* k, c
 template <int D, bool CAUSAL>
 agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k, const float* v,
                                float* o, int B, int H, int s, const AttnStrides& sd,
-                               cudaStream_t st) {
+                               cudaStream_t st, float* lse = nullptr) {
   using C = PairAttnCfg<D>;
   CUtensorMap tk, tv;
   bool hk, hv;
@@ -1094,8 +1117,9 @@ agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k,
   AGPU_TRY(make_attn_map(&tv, v, D, s, H, B, sd.v, KB, true, &hv));
   AttnOut ol{sd.o[0], sd.o[1], sd.o[2], (hk ? 2 : 0) | (hv ? 4 : 0)};
   AttnQ qin{q, sd.q[0], sd.q[1], sd.q[2]};
-  auto kern = attention_pair_kernel<D, CAUSAL>;
-  AGPU_CUDA((set_smem_once<attention_pair_kernel<D, CAUSAL>>(dev, C::SMEM)));
+  auto kern = lse ? attention_pair_kernel<D, CAUSAL, true> : attention_pair_kernel<D, CAUSAL, false>;
+  AGPU_CUDA(lse ? (set_smem_once<attention_pair_kernel<D, CAUSAL, true>>(dev, C::SMEM))
+                : (set_smem_once<attention_pair_kernel<D, CAUSAL, false>>(dev, C::SMEM)));
   AttnTiles tiles;
   tiles.nqt = (int)ceil_div(s, 2 * QT);
   tiles.H = H;
@@ -1116,7 +1140,7 @@ agpu_status run_attention_pair(agpu_device* dev, const float* q, const float* k,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   AGPU_CUDA(cudaLaunchKernelEx(&cfg, kern, tk, tv, qin, o, s, scale_log2, ol, tiles,
-                               dev->d_status));
+                               dev->d_status, lse));
   return after_launch(dev, "attention_pair_kernel");
 }
 
@@ -1169,6 +1193,33 @@ agpu_status launch_attention_strided(agpu_device* dev, const float* q, const flo
   else
     attention_simt_kernel<false><<<blocks, 256, 0, st>>>(q, k, v, o, B, H, s, d, scale, sd);
   return after_launch(dev, "attention_simt_kernel");
+}
+
+// The forward on CTA pairs with each row's log-sum-exp of its base-2 scores
+// (s = q.k / sqrt(d) * log2 e, so P = 2^(s - lse)) into lse [bh, s];
+// AGPU_ERR_UNSUPPORTED (nothing launched, no message) where the pair kernel
+// does not run: another precision, s < 256, d not 64 or 128, pitches TMA
+// cannot address, or AGPU_SDPA_PAIR=0.  Contiguous [bh, s, d] operands.
+agpu_status launch_attention_lse(agpu_device* dev, const float* q, const float* k,
+                                 const float* v, float* o, float* lse, uint32_t bh, uint32_t s,
+                                 uint32_t d, bool causal, cudaStream_t st) {
+  static const bool pair_ok = [] {
+    const char* e = getenv("AGPU_SDPA_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15u) == 0;
+  if (!pair_ok || effective_precision(dev) != AGPU_PREC_TF32 || !aligned ||
+      (d != 64 && d != 128) || s < 2 * QT || bh > 65535 || bh == 0)
+    return AGPU_ERR_UNSUPPORTED;
+  AttnStrides sd;
+  const long long c[3] = {(long long)d, (long long)s * d, (long long)bh * s * d};
+  for (int i = 0; i < 3; ++i) sd.q[i] = sd.k[i] = sd.v[i] = sd.o[i] = c[i];
+  if (d == 128)
+    return causal ? run_attention_pair<128, true>(dev, q, k, v, o, 1, bh, s, sd, st, lse)
+                  : run_attention_pair<128, false>(dev, q, k, v, o, 1, bh, s, sd, st, lse);
+  return causal ? run_attention_pair<64, true>(dev, q, k, v, o, 1, bh, s, sd, st, lse)
+                : run_attention_pair<64, false>(dev, q, k, v, o, 1, bh, s, sd, st, lse);
 }
 
 // Contiguous [bh, s, d] operands: heads = bh, batch = 1.

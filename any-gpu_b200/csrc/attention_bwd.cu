@@ -15,13 +15,23 @@
 // The five products run on the tensor-core GEMMs (launch_gemm: tcgen05 in
 // TF32, 3xTF32 or exact FFMA per the precision mode), with the transposes
 // folded into operand majors -- kind::tf32 reads either major -- so no
-// transpose pass.  P and dP/dS live in two [heads, S, S] scratch buffers from
-// the device pool, processed in head chunks of at most 2^30 elements each; the
-// two row kernels below (probabilities, softmax backward) are HBM-bound: one
-// block per row (grid-stride), each row read once from HBM and again from
-// cache.
+// transpose pass.  Heads are processed in chunks of at most 2^30 score
+// elements.  Two ways, the same math:
+//
+//  * TF32 where the CTA-pair kernels run both the forward and the S-sized
+//    products (S >= 256, d 64 or 128): the forward is rerun to give each
+//    row's log-sum-exp L and O; D = rowsum(dO o O) (= rowsum(P o dP), since
+//    O = P V); then P = 2^(S * scale * log2 e - L) is formed in the S
+//    product's epilogue and dS = P o (dP - D) * scale in the dP product's
+//    epilogue, in place over P -- no row pass over the [heads, S, S]
+//    matrices and one such buffer instead of two;
+//  * otherwise P and dP/dS in two [heads, S, S] pool buffers and the two row
+//    kernels below (probabilities, softmax backward), HBM-bound: one block
+//    per row (grid-stride), each row read once from HBM and again from cache.
+//    AGPU_SDPA_BWD_FUSED=0 in the environment keeps this way for every shape.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "agpu_internal.cuh"
 
@@ -91,6 +101,34 @@ __global__ void __launch_bounds__(kRowThreads) attn_softmax_bwd_kernel(
   }
 }
 
+// D[r] = sum_c dO[r, c] * O[r, c]: one warp per row of d (64 or 128) floats.
+__global__ void __launch_bounds__(256) attn_rowdot_kernel(const float* __restrict__ a,
+                                                          const float* __restrict__ b,
+                                                          float* __restrict__ out, long long rows,
+                                                          int d) {
+  const long long r = (long long)blockIdx.x * 8 + threadIdx.x / 32;
+  if (r >= rows) return;
+  const int lane = threadIdx.x % 32;
+  const float* x = a + r * d;
+  const float* y = b + r * d;
+  float acc = 0.f;
+  for (int c = lane * 2; c < d; c += 64) {
+    const float2 u = *reinterpret_cast<const float2*>(x + c);
+    const float2 w = *reinterpret_cast<const float2*>(y + c);
+    acc += u.x * w.x + u.y * w.y;
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[r] = acc;
+}
+
+bool bwd_fused_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("AGPU_SDPA_BWD_FUSED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace
 
 agpu_status launch_attention_backward(agpu_device* dev, const float* q, const float* k,
@@ -101,6 +139,60 @@ agpu_status launch_attention_backward(agpu_device* dev, const float* q, const fl
   const float scale = 1.0f / std::sqrt((float)d);
   const uint64_t ss = (uint64_t)s * s;
   const uint64_t chunk = std::max<uint64_t>(1, std::min<uint64_t>(bh, (1ull << 30) / ss));
+  // the epilogue way: every chunk's S-sized products on the pair kernel (the
+  // last, smaller chunk included) and the forward on CTA pairs
+  const uint32_t last = (uint32_t)(bh - (bh - 1) / chunk * chunk);
+  const bool fused = bwd_fused_enabled() && effective_precision(dev) == AGPU_PREC_TF32 &&
+                     (d == 64 || d == 128) && s >= 256 && s % 4 == 0 &&
+                     gemm_rowvec_mode_ok(dev, q, k, q, (uint32_t)std::min<uint64_t>(chunk, bh),
+                                         s, s, d) &&
+                     gemm_rowvec_mode_ok(dev, q, k, q, last, s, s, d);
+  if (fused) {
+    const uint64_t od = chunk * s * d, rows_max = chunk * s;
+    void *pbuf = nullptr, *obuf = nullptr;
+    AGPU_TRY(pool_alloc(dev, chunk * ss * sizeof(float), &pbuf, st));
+    agpu_status rc = pool_alloc(dev, (od + 2 * rows_max) * sizeof(float), &obuf, st);
+    if (rc != AGPU_OK) {
+      pool_free(dev, pbuf, st);
+      return rc;
+    }
+    float* P = static_cast<float*>(pbuf);
+    float* O = static_cast<float*>(obuf);
+    float* L = O + od;           // od % 4 == 0: 16-byte aligned
+    float* Dv = L + rows_max;    // rows_max % 4 == 0 (s % 4 == 0)
+    for (uint64_t h0 = 0; h0 < bh && rc == AGPU_OK; h0 += chunk) {
+      const uint32_t n = (uint32_t)std::min<uint64_t>(chunk, bh - h0);
+      const uint64_t off = h0 * s * d;
+      const long long rows = (long long)n * s;
+      // forward rerun: O and each row's log-sum-exp
+      rc = launch_attention_lse(dev, q + off, k + off, v + off, O, L, n, s, d, causal, st);
+      if (rc != AGPU_OK) break;
+      attn_rowdot_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(dout + off, O, Dv, rows,
+                                                                      (int)d);
+      rc = after_launch(dev, "attn_rowdot_kernel");
+      // P = 2^(Q K^T * scale * log2 e - L), masked above the diagonal if causal
+      GemmEpilogue e1;
+      e1.mode = 1;
+      e1.rowvec = L;
+      e1.scale = scale * 1.4426950408889634f;
+      e1.causal = causal;
+      if (rc == AGPU_OK) rc = launch_gemm_ex(dev, q + off, k + off, P, n, s, s, d, false, true, e1, st);
+      // dV = P^T dO
+      if (rc == AGPU_OK) rc = launch_gemm(dev, P, dout + off, dv + off, n, s, d, s, true, false, st);
+      // dS = P o (dO V^T - D) * scale, in place over P
+      GemmEpilogue e2;
+      e2.mode = 2;
+      e2.rowvec = Dv;
+      e2.scale = scale;
+      if (rc == AGPU_OK) rc = launch_gemm_ex(dev, dout + off, v + off, P, n, s, s, d, false, true, e2, st);
+      // dQ = dS K;  dK = dS^T Q
+      if (rc == AGPU_OK) rc = launch_gemm(dev, P, k + off, dq + off, n, s, d, s, false, false, st);
+      if (rc == AGPU_OK) rc = launch_gemm(dev, P, q + off, dk + off, n, s, d, s, true, false, st);
+    }
+    pool_free(dev, obuf, st);
+    pool_free(dev, pbuf, st);
+    return rc;
+  }
   void *pbuf = nullptr, *gbuf = nullptr;
   AGPU_TRY(pool_alloc(dev, chunk * ss * sizeof(float), &pbuf, st));
   agpu_status rc = pool_alloc(dev, chunk * ss * sizeof(float), &gbuf, st);

@@ -104,6 +104,7 @@ struct ConvPolicy {
   __device__ bool col_live(const Tile& t, int col0) const { return t.oc0 + col0 < cout; }
   // no paired (SwiGLU) epilogue for convolutions
   __device__ bool paired() const { return false; }
+  static constexpr bool TILE_EPILOGUE = false;  // per-chunk stores
   __device__ void store_swiglu(const Tile&, int, int, const uint32_t (&)[32],
                                const uint32_t (&)[32], float*, int) const {}
 

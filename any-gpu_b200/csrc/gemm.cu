@@ -55,10 +55,13 @@ __device__ __forceinline__ float epi_act(float x, int act) {
 
 // Row-major (batched) GEMM: tiles 128 x BN walk batch-major with a 16-row-
 // block group swizzle (L2 reuse of the B column block across the group).
-template <int BN_, bool A_MN_, bool B_MN_>
+template <int BN_, bool A_MN_, bool B_MN_, bool ROWVEC_ = false>
 struct GemmPolicy {
   static constexpr int BN = BN_;
   static constexpr bool A_MN = A_MN_, B_MN = B_MN_;
+  // the row-vector modes' whole-tile epilogue (store_tile), compiled into
+  // the pair kernel only for these instantiations
+  static constexpr bool TILE_EPILOGUE = ROWVEC_;
   int M, N, K, tiles_m, tiles_n;
   long long tiles;
   float* C;
@@ -67,6 +70,11 @@ struct GemmPolicy {
   const float* bias;   // [N] or null (Linear bias, the reference's add_per_col)
   const float* resid;  // [batch, M, N] or null (residual add)
   int act;             // 0 none, 1 swish, 2 relu
+  // row-vector modes (GemmEpilogue::mode; TMA-store path only)
+  int mode = 0;
+  const float* rowvec = nullptr;  // [batch, M]
+  float ep_scale = 1.0f;
+  bool causal = false;
   // MN-major operand loaded through the 4-D chunked view, one TMA box per
   // stage (else one box per 32-column chunk)
   bool a_chunked = false, b_chunked = false;
@@ -155,6 +163,98 @@ struct GemmPolicy {
     __syncwarp();
   }
 
+  // Mode 2 runs a whole-tile epilogue (TILE_EPILOGUE instantiations: the
+  // pair kernel calls store_tile instead of store per chunk): the warp walks
+  // the tile's live 32-column chunks itself, so it can overlap across chunks
+  // -- the next chunk's tensor-memory load is issued while this one is staged
+  // and stored, and the blocks of P two chunks ahead are in flight in
+  // registers.  (Mode 1 measured faster per chunk, in store_tma.)
+  __device__ bool whole_tile() const { return mode == 2; }
+
+  // Mode 2: 32 rows x 32 columns of P at (row_base, col) into registers in
+  // the coalesced layout: p[i] = row 4 i + lane / 8, columns 4 (lane % 8) ..
+  // +3 (one warp instruction reads 4 whole 128-byte rows); zeros outside.
+  __device__ void load_p(const Tile& t, int row_base, int col, float4 (&p)[8], int lane) const {
+    const float* src = C + (long long)t.b * c_batch;
+    const int gc = col + 4 * (lane & 7);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int gr = row_base + 4 * i + (lane >> 3);
+      p[i] = (gr < M && gc < N)
+                 ? __ldcg(reinterpret_cast<const float4*>(src + (long long)gr * N + gc))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+
+  // Thread `lane` owns row t.m0 + row; trow addresses the warp's TMEM lanes
+  // at the tile's first accumulator column.  Chunk c's block of P sits in
+  // register set c % 3 (mode 2): while chunk c is combined, chunks c + 1 and
+  // c + 2 are in flight -- the sets rotate by name (the loop is unrolled by
+  // three), so no pending load is ever read early.
+  __device__ void store_tile(const Tile& t, int row, uint32_t trow, float* stg, int lane) const {
+    const int grow = t.m0 + row, row_base = grow - lane;
+    const float rv = grow < M ? __ldg(rowvec + (long long)t.b * M + grow) : 0.f;
+    const int nch = min(BN / 32, (N - t.n0 + 31) / 32);
+    float4 pa[8], pb[8], pc[8];
+    if (mode == 2) {
+      load_p(t, row_base, t.n0, pa, lane);
+      if (nch > 1) load_p(t, row_base, t.n0 + 32, pb, lane);
+    }
+    uint32_t v[32];
+    ptx::tmem_ld32(trow, v);
+    auto step = [&](int c, float4 (&pu)[8], float4 (&pf)[8]) {
+      const int col = t.n0 + 32 * c;
+      float* buf = stg + (c & 1) * 1024;
+      if (mode == 2 && c + 2 < nch) load_p(t, row_base, col + 64, pf, lane);
+      if (lane == 0) ptx::bulk_wait_read1();  // the store two chunks back has read `buf`
+      ptx::tmem_wait_ld();
+      float4 w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                           __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+      if (c + 1 < nch) ptx::tmem_ld32(trow + 32 * (c + 1), v);  // lands while this chunk stores
+      __syncwarp();
+      uint8_t* rowp = reinterpret_cast<uint8_t*>(buf) + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) = w[j];
+      if (mode == 2) {
+        // dS = P o (dP - D[row]) * scale in the coalesced layout: row 4 i +
+        // lane / 8 of the staged dP block times the same row of P
+        __syncwarp();
+        const int jj = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3);
+          const float d = __shfl_sync(0xffffffffu, rv, r);
+          float4* cell = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(buf) + r * 128 +
+                                                   ((jj ^ (r & 7)) << 4));
+          const float4 a = *cell;
+          float4 o;
+          o.x = pu[i].x * (a.x - d) * ep_scale;
+          o.y = pu[i].y * (a.y - d) * ep_scale;
+          o.z = pu[i].z * (a.z - d) * ep_scale;
+          o.w = pu[i].w * (a.w - d) * ep_scale;
+          *cell = o;
+        }
+      }
+      ptx::fence_proxy_async_smem();  // the async proxy (TMA) sees the staged block
+      __syncwarp();
+      if (lane == 0 && row_base < M) {
+        ptx::tma_store_3d(&tmap_c, buf, col, row_base, t.b);
+        ptx::bulk_commit();
+      }
+    };
+#pragma unroll 1
+    for (int c = 0; c < nch; c += 3) {
+      step(c, pa, pc);
+      if (c + 1 < nch) step(c + 1, pb, pa);
+      if (c + 2 < nch) step(c + 2, pc, pb);
+    }
+    if (lane == 0) ptx::bulk_wait_read0();  // the next tile starts again at buffer 0
+  }
+
   // TMA store of one 32 x 32 block (c_tma): thread `lane` holds row m0 + row,
   // columns n0 + col0 .. +31, applies the epilogue in registers and writes
   // its row into one of the warp's two 4 KB staging buffers in the 128-byte
@@ -199,6 +299,17 @@ struct GemmPolicy {
       for (int j = 0; j < 8; ++j) {
         w[j].x = epi_act(w[j].x, act); w[j].y = epi_act(w[j].y, act);
         w[j].z = epi_act(w[j].z, act); w[j].w = epi_act(w[j].w, act);
+      }
+    }
+    if (mode == 1) {  // P = 2^(S * scale - L[row]), 0 above the diagonal if causal
+      const float rv = grow < M ? __ldg(rowvec + (long long)t.b * M + grow) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int cc = col + 4 * j;
+        w[j].x = (causal && cc > grow) ? 0.f : ptx::ex2_approx(fmaf(w[j].x, ep_scale, -rv));
+        w[j].y = (causal && cc + 1 > grow) ? 0.f : ptx::ex2_approx(fmaf(w[j].y, ep_scale, -rv));
+        w[j].z = (causal && cc + 2 > grow) ? 0.f : ptx::ex2_approx(fmaf(w[j].z, ep_scale, -rv));
+        w[j].w = (causal && cc + 3 > grow) ? 0.f : ptx::ex2_approx(fmaf(w[j].w, ep_scale, -rv));
       }
     }
     uint8_t* rowp = reinterpret_cast<uint8_t*>(buf) + lane * 128;
@@ -272,9 +383,9 @@ struct GemmPolicy {
 // CTA-pair GEMM tile: 256 x BN (BN = 256, or 512 as two MMAs of N 256);
 // CTA `rank` of the pair stages rows m0 + 128*rank .. +127 of A and, per
 // MMA sub-block s, columns n0 + s*MMA_N + rank*MMA_N/2 .. of B.
-template <int BN_, bool A_MN_, bool B_MN_>
-struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_> {
-  using Base = GemmPolicy<BN_, A_MN_, B_MN_>;
+template <int BN_, bool A_MN_, bool B_MN_, bool ROWVEC_ = false>
+struct GemmPairPolicy : GemmPolicy<BN_, A_MN_, B_MN_, ROWVEC_> {
+  using Base = GemmPolicy<BN_, A_MN_, B_MN_, ROWVEC_>;
   using Tile = typename Base::Tile;
   using Cfg = umma::PairCfg<BN_>;
   static constexpr int PM = 2 * BM;  // tile rows of the pair
@@ -555,11 +666,11 @@ static agpu_status run_tc(agpu_device* dev, const float* a, const float* b, floa
   return after_launch(dev, "gemm_tf32 (umma_tf32_kernel)");
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool ROWVEC = false>
 static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b, float* c,
                                uint32_t batch, uint32_t m, uint32_t n, uint32_t k,
                                const GemmEpilogue& ep, cudaStream_t s) {
-  using P = GemmPairPolicy<BN, A_MN, B_MN>;
+  using P = GemmPairPolicy<BN, A_MN, B_MN, ROWVEC>;
   CUtensorMap ta, tb;
   P pol;
   AGPU_TRY(make_gemm_maps(&ta, &tb, &pol, a, b, batch, m, n, k, P::HALF, true));
@@ -572,7 +683,12 @@ static agpu_status run_tc_pair(agpu_device* dev, const float* a, const float* b,
   pol.bias = ep.bias;
   pol.resid = ep.resid;
   pol.act = ep.act;
+  pol.mode = ep.mode;
+  pol.rowvec = ep.rowvec;
+  pol.ep_scale = ep.scale;
+  pol.causal = ep.causal;
   AGPU_TRY(make_c_map(&pol, c, batch, m, n, ep.act));
+  if (ep.mode != 0 && !pol.c_tma) return fail(AGPU_ERR_CUDA, "gemm: row-vector mode without a C map");
   return launch_pair(dev, ta, tb, pol, pol.tiles, s,
                      "gemm_tf32 (umma_tf32_pair_kernel)");
 }
@@ -882,6 +998,13 @@ bool gemm_tc_eligible(const float* a, const float* b, const float* c, uint32_t m
   return mis == 0 && (k % 4 == 0) && (n % 4 == 0) && (m % 4 == 0) && k >= 8;
 }
 
+bool gemm_rowvec_mode_ok(agpu_device* dev, const float* a, const float* b, const float* c,
+                         uint32_t batch, uint32_t m, uint32_t n, uint32_t k) {
+  return batch > 0 && effective_precision(dev) == AGPU_PREC_TF32 && use_pair(m, n) &&
+         gemm_tc_eligible(a, b, c, m, n, k) && tma_store_enabled() &&
+         splitk_plan(dev, batch, m, n, k).s == 1;
+}
+
 agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, float* c,
                            uint32_t batch, uint32_t m, uint32_t n, uint32_t k, bool a_trans,
                            bool b_trans, const GemmEpilogue& ep, cudaStream_t s) {
@@ -892,6 +1015,15 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
     return AGPU_OK;
   }
   const agpu_precision p = effective_precision(dev);
+  if (ep.mode != 0) {
+    // C = A B^T only (the attention backward's S and dP products)
+    if (ep.bias || ep.resid || ep.act || !ep.rowvec || k == 0 || a_trans || !b_trans ||
+        !gemm_rowvec_mode_ok(dev, a, b, c, batch, m, n, k))
+      return AGPU_ERR_UNSUPPORTED;
+    return use_wide(dev, batch, m, n, k)
+               ? run_tc_pair<512, false, false, true>(dev, a, b, c, batch, m, n, k, ep, s)
+               : run_tc_pair<256, false, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+  }
   if (ep.act == 3) {
     // SwiGLU: fused into the CTA-pair kernel's epilogue when that kernel runs
     // the GEMM whole; otherwise the plain GEMM into scratch, then swish * up

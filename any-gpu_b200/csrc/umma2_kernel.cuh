@@ -58,7 +58,16 @@ struct PairCfg {
 //   void load(ta, tb, sa, sb, uint32_t leader_bar, const Tile&, int kb, int rank) const;
 //       issues this CTA's STAGE_BYTES with tma_load_*_pair(..., leader_bar, ...)
 //   Tile rank_tile(const Tile&, int rank) const;   // the CTA's 128-row half
+//   static constexpr bool TILE_EPILOGUE;  // true: where whole_tile(),
+//       store_tile(tile, row, tmem_row_addr, staging, lane) drains the tile
 // and, for BN > 256, the B sub-block layout described at PairCfg.
+// whether a TILE_EPILOGUE policy drains this launch's tiles with store_tile
+template <class P>
+__device__ __forceinline__ bool tile_epi(const P& pol) {
+  if constexpr (P::TILE_EPILOGUE) return pol.whole_tile();
+  else return false;
+}
+
 template <class P>
 __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     umma_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -215,6 +224,8 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
           ptx::tmem_wait_ld();
           pol.store_swiglu(tile, q * 32 + lane, c * 32, g, u, stg, lane);
         }
+      } else if (tile_epi(pol)) {  // the policy walks the tile's chunks itself
+        if constexpr (P::TILE_EPILOGUE) pol.store_tile(tile, q * 32 + lane, trow, stg, lane);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {

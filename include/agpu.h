@@ -36,6 +36,9 @@
  *                         batch_matmul + softmax pipeline
  *   AGPU_X3_SEG=N         3xTF32 on CTA pairs: K-blocks (of 32) per accumulator
  *                         segment (default 16; 0 = none: faster, less accurate)
+ *   AGPU_SDPA_BWD_FUSED=0 attention backward with the two row passes over the
+ *                         [heads, S, S] matrices instead of the forward rerun
+ *                         and the GEMM epilogues that form P and dS
  *   AGPU_GEMM_TMA_STORE=0 GEMM outputs by the warp-transposing float4 store
  *                         instead of TMA bulk tensor stores (bit-identical)
  */
@@ -294,8 +297,11 @@ AGPU_API agpu_status agpu_sdpa_causal(agpu_device* dev, const agpu_buffer* q,
  * scale rule and the softmax Jacobian: P = softmax(Q K^T / sqrt(d_k)) is
  * recomputed, dV = P^T dO, dS = P o (dO V^T - rowsum(P o dO V^T)) / sqrt(d_k),
  * dQ = dS K, dK = dS^T Q.  The products run on the tensor-core GEMMs in the
- * current precision mode; P and dS use 2 x min(batch_heads, 2^30 / seq_len^2)
- * x seq_len^2 floats of pool scratch.  Shape checks as the forward. */
+ * current precision mode.  In TF32 with seq_len >= 256 and d_k 64 or 128 the
+ * forward is rerun for each row's log-sum-exp and O, P is formed in the
+ * S product's epilogue and dS in the dP product's, in place: pool scratch of
+ * min(batch_heads, 2^30 / seq_len^2) x seq_len^2 floats plus O; otherwise P
+ * and dS take twice that.  Shape checks as the forward. */
 AGPU_API agpu_status agpu_sdpa_backward(agpu_device* dev, const agpu_buffer* q,
                                         const agpu_buffer* k, const agpu_buffer* v,
                                         const agpu_buffer* grad_out, uint32_t batch_heads,

@@ -65,9 +65,57 @@ def test_sdpa_backward_fp32_modes_vs_float64(dev, orc, prec):
             assert _rel(a[sl], w) <= 1e-5, (prec, h, name, _rel(a[sl], w))
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("bh,s,d", [(16, 1024, 128), (24, 768, 64), (6, 1000, 64), (5, 2048, 128)])
+def test_sdpa_backward_epilogue_way_vs_float64(dev, bh, s, d, causal):
+    """Shapes whose S-sized products run on the CTA-pair GEMM: P formed in the
+    S product's epilogue from the forward's row log-sum-exp, dS in the dP
+    product's epilogue in place over P (D = rowsum(dO o O)).  Sampled heads
+    against float64 within the TF32 tolerance."""
+    q, k, v, do = _inputs(bh, s, d, bh + s + d + causal)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d, causal=causal)]
+    hs = s * d
+    for h in sorted({0, bh // 2, bh - 1}):
+        sl = slice(h * hs, (h + 1) * hs)
+        want = _f64_backward(q[sl], k[sl], v[sl], do[sl], s, d, causal)
+        for name, a, w in zip(("dq", "dk", "dv"), got, want):
+            assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
+
+
+def test_sdpa_backward_both_ways_agree(dev, tmp_path):
+    """The row-kernel way (AGPU_SDPA_BWD_FUSED=0, in a child process) and the
+    epilogue way give the same gradients within the TF32 tolerance."""
+    import os
+    import subprocess
+    import sys
+    bh, s, d = 8, 1024, 128
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{os.path.join(root, 'any-gpu_b200')!r}, {root!r}]\n"
+        "from tests.test_attention_bwd_gpu import _inputs\n"
+        "from any_gpu import GpuDevice\n"
+        "d = GpuDevice.gpu(0)\n"
+        f"q, k, v, do = _inputs({bh}, {s}, {d}, 41)\n"
+        "g = [d.upload(x) for x in (q, k, v, do)]\n"
+        f"out = [d.read(x) for x in d.sdpa_backward(*g, {bh}, {s}, {d}, causal=True)]\n"
+        f"np.save({str(tmp_path)!r} + '/g.npy', np.stack(out))\n"
+        "d.close()\n")
+    r = subprocess.run([sys.executable, "-c", script], capture_output=True, text=True,
+                       timeout=300, env=dict(os.environ, AGPU_SDPA_BWD_FUSED="0"))
+    assert r.returncode == 0, r.stderr[-2000:]
+    rows = np.load(tmp_path / "g.npy")
+    q, k, v, do = _inputs(bh, s, d, 41)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d, causal=True)]
+    for name, a, b in zip(("dq", "dk", "dv"), got, rows):
+        assert _rel(a, b) <= 1e-3, (name, _rel(a, b))
+
+
 def test_sdpa_backward_benchmark_size_sampled(dev):
-    """B8 H32 S2048 D128 (the SDPA benchmark config): three heads against
-    float64 (P and dS scratch: 2 x 4 GiB in head chunks)."""
+    """B8 H32 S2048 D128 (the SDPA benchmark config, the epilogue way): three
+    heads against float64."""
     bh, s, d = 256, 2048, 128
     q, k, v, do = _inputs(bh, s, d, 77)
     g = [dev.upload(x) for x in (q, k, v, do)]
