@@ -105,6 +105,7 @@ struct ConvPolicy {
   // no paired (SwiGLU) epilogue for convolutions
   __device__ bool paired() const { return false; }
   static constexpr bool TILE_EPILOGUE = false;  // per-chunk stores
+  static constexpr int EPI_EXTRA = 0;
   __device__ void store_swiglu(const Tile&, int, int, const uint32_t (&)[32],
                                const uint32_t (&)[32], float*, int) const {}
 

@@ -60,8 +60,12 @@ struct GemmPolicy {
   static constexpr int BN = BN_;
   static constexpr bool A_MN = A_MN_, B_MN = B_MN_;
   // the row-vector modes' whole-tile epilogue (store_tile), compiled into
-  // the pair kernel only for these instantiations
+  // the pair kernel only for these instantiations, with a 13 KB slice of
+  // extra epilogue memory per warp: three 4 KB blocks of P in flight (TMA
+  // loads through C's map) and their mbarriers
   static constexpr bool TILE_EPILOGUE = ROWVEC_;
+  static constexpr int kPBufs = 3;
+  static constexpr int EPI_EXTRA = ROWVEC_ ? umma::kEpiWarps * 13 * 1024 : 0;
   int M, N, K, tiles_m, tiles_n;
   long long tiles;
   float* C;
@@ -167,92 +171,114 @@ struct GemmPolicy {
   // pair kernel calls store_tile instead of store per chunk): the warp walks
   // the tile's live 32-column chunks itself, so it can overlap across chunks
   // -- the next chunk's tensor-memory load is issued while this one is staged
-  // and stored, and the blocks of P two chunks ahead are in flight in
-  // registers.  (Mode 1 measured faster per chunk, in store_tma.)
+  // and stored, and the blocks of P up to kPBufs chunks ahead are in flight.
+  // (Mode 1 measured faster per chunk, in store_tma.)
   __device__ bool whole_tile() const { return mode == 2; }
 
-  // Mode 2: 32 rows x 32 columns of P at (row_base, col) into registers in
-  // the coalesced layout: p[i] = row 4 i + lane / 8, columns 4 (lane % 8) ..
-  // +3 (one warp instruction reads 4 whole 128-byte rows); zeros outside.
-  __device__ void load_p(const Tile& t, int row_base, int col, float4 (&p)[8], int lane) const {
-    const float* src = C + (long long)t.b * c_batch;
-    const int gc = col + 4 * (lane & 7);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int gr = row_base + 4 * i + (lane >> 3);
-      p[i] = (gr < M && gc < N)
-                 ? __ldcg(reinterpret_cast<const float4*>(src + (long long)gr * N + gc))
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+  // Warp slice of the extra epilogue memory: kPBufs blocks of P (4 KB
+  // each, 1024-aligned, the 128-byte swizzle of C's map), then kPBufs
+  // mbarriers, then the count of blocks this warp has loaded so far (which
+  // fixes each buffer's phase across tiles).
+  __device__ static uint64_t* pbar(float* xtra) {
+    return reinterpret_cast<uint64_t*>(xtra + kPBufs * 1024);
+  }
+  __device__ static unsigned int* pcount(float* xtra) {
+    return reinterpret_cast<unsigned int*>(pbar(xtra) + kPBufs);
+  }
+  __device__ void init_extra(float* xtra) const {
+    for (int k = 0; k < kPBufs; ++k) ptx::mbar_init(pbar(xtra) + k, 1);
+    *pcount(xtra) = 0u;
   }
 
   // Thread `lane` owns row t.m0 + row; trow addresses the warp's TMEM lanes
-  // at the tile's first accumulator column.  Chunk c's block of P sits in
-  // register set c % 3 (mode 2): while chunk c is combined, chunks c + 1 and
-  // c + 2 are in flight -- the sets rotate by name (the loop is unrolled by
-  // three), so no pending load is ever read early.
-  __device__ void store_tile(const Tile& t, int row, uint32_t trow, float* stg, int lane) const {
+  // at the tile's first accumulator column.  Block c of P (the warp's 32
+  // rows, the tile's columns 32 c ..) is the warp's load number g + c, into
+  // buffer (g + c) % kPBufs; lane 0 keeps kPBufs loads in flight, issuing
+  // block c + kPBufs as soon as block c has been read.  Every wait is
+  // bounded; after an expired one the warp waits (bounded) for its loads
+  // still in flight and returns false.
+  __device__ bool store_tile(const Tile& t, int row, uint32_t trow, float* stg, float* xtra,
+                             int lane, unsigned int* status, volatile int* abort_flag) const {
     const int grow = t.m0 + row, row_base = grow - lane;
     const float rv = grow < M ? __ldg(rowvec + (long long)t.b * M + grow) : 0.f;
     const int nch = min(BN / 32, (N - t.n0 + 31) / 32);
-    float4 pa[8], pb[8], pc[8];
-    if (mode == 2) {
-      load_p(t, row_base, t.n0, pa, lane);
-      if (nch > 1) load_p(t, row_base, t.n0 + 32, pb, lane);
-    }
+    uint64_t* bars = pbar(xtra);
+    const unsigned int g = *reinterpret_cast<volatile unsigned int*>(pcount(xtra));
+    auto issue = [&](int c) {  // lane 0
+      const int k = (int)((g + c) % kPBufs);
+      ptx::mbar_arrive_expect_tx(bars + k, 4096);
+      ptx::tma_load_3d(xtra + k * 1024, &tmap_c, bars + k, t.n0 + 32 * c, row_base, t.b);
+    };
+    if (lane == 0)
+      for (int c = 0; c < min(kPBufs, nch); ++c) issue(c);
+    bool ok = true;
+    int c = 0;
     uint32_t v[32];
     ptx::tmem_ld32(trow, v);
-    auto step = [&](int c, float4 (&pu)[8], float4 (&pf)[8]) {
+#pragma unroll 1
+    for (; c < nch; ++c) {
       const int col = t.n0 + 32 * c;
       float* buf = stg + (c & 1) * 1024;
-      if (mode == 2 && c + 2 < nch) load_p(t, row_base, col + 64, pf, lane);
+      const unsigned int gc = g + c;
+      float* pb = xtra + (gc % kPBufs) * 1024;
       if (lane == 0) ptx::bulk_wait_read1();  // the store two chunks back has read `buf`
       ptx::tmem_wait_ld();
-      float4 w[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                           __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
-      if (c + 1 < nch) ptx::tmem_ld32(trow + 32 * (c + 1), v);  // lands while this chunk stores
       __syncwarp();
       uint8_t* rowp = reinterpret_cast<uint8_t*>(buf) + lane * 128;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) = w[j];
-      if (mode == 2) {
-        // dS = P o (dP - D[row]) * scale in the coalesced layout: row 4 i +
-        // lane / 8 of the staged dP block times the same row of P
-        __syncwarp();
-        const int jj = lane & 7;
+        *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+            make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                        __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+      if (c + 1 < nch) ptx::tmem_ld32(trow + 32 * (c + 1), v);  // lands while this chunk stores
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(bars + gc % kPBufs, (gc / kPBufs) & 1,
+                                                  status, 0x309, abort_flag));
+      if (!ok) break;
+      __syncwarp();
+      // dS = P o (dP - D[row]) * scale, row 4 i + lane / 8 of both blocks
+      // (the same swizzled positions)
+      const int jj = lane & 7;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = 4 * i + (lane >> 3);
-          const float d = __shfl_sync(0xffffffffu, rv, r);
-          float4* cell = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(buf) + r * 128 +
-                                                   ((jj ^ (r & 7)) << 4));
-          const float4 a = *cell;
-          float4 o;
-          o.x = pu[i].x * (a.x - d) * ep_scale;
-          o.y = pu[i].y * (a.y - d) * ep_scale;
-          o.z = pu[i].z * (a.z - d) * ep_scale;
-          o.w = pu[i].w * (a.w - d) * ep_scale;
-          *cell = o;
+      for (int i = 0; i < 8; ++i) {
+        const int r = 4 * i + (lane >> 3);
+        const float d = __shfl_sync(0xffffffffu, rv, r);
+        const int off = r * 128 + ((jj ^ (r & 7)) << 4);
+        float4* cell = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(buf) + off);
+        const float4 pv = *reinterpret_cast<const float4*>(reinterpret_cast<uint8_t*>(pb) + off);
+        const float4 a = *cell;
+        float4 o;
+        o.x = pv.x * (a.x - d) * ep_scale;
+        o.y = pv.y * (a.y - d) * ep_scale;
+        o.z = pv.z * (a.z - d) * ep_scale;
+        o.w = pv.w * (a.w - d) * ep_scale;
+        *cell = o;
+      }
+      // the async proxy sees the staged block; and pb's generic reads come
+      // before the TMA load that refills it
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (c + kPBufs < nch) issue(c + kPBufs);
+        if (row_base < M) {
+          ptx::tma_store_3d(&tmap_c, buf, col, row_base, t.b);
+          ptx::bulk_commit();
         }
       }
-      ptx::fence_proxy_async_smem();  // the async proxy (TMA) sees the staged block
-      __syncwarp();
-      if (lane == 0 && row_base < M) {
-        ptx::tma_store_3d(&tmap_c, buf, col, row_base, t.b);
-        ptx::bulk_commit();
-      }
-    };
-#pragma unroll 1
-    for (int c = 0; c < nch; c += 3) {
-      step(c, pa, pc);
-      if (c + 1 < nch) step(c + 1, pb, pa);
-      if (c + 2 < nch) step(c + 2, pc, pb);
     }
-    if (lane == 0) ptx::bulk_wait_read0();  // the next tile starts again at buffer 0
+    if (!ok) {
+      // loads c .. min(c + kPBufs, nch) - 1 may still be in flight
+      if (c + 1 < nch) ptx::tmem_wait_ld();
+      for (int e = c; e < min(c + kPBufs, nch); ++e)
+        ptx::mbar_wait_for(bars + (g + e) % kPBufs, ((g + e) / kPBufs) & 1, nullptr, 0, nullptr,
+                           ptx::kWaitLimitNs);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      *pcount(xtra) = g + (unsigned int)nch;
+      ptx::bulk_wait_read0();  // the next tile starts again at buffer 0
+    }
+    __syncwarp();
+    return ok;
   }
 
   // TMA store of one 32 x 32 block (c_tma): thread `lane` holds row m0 + row,
@@ -1020,9 +1046,7 @@ agpu_status launch_gemm_ex(agpu_device* dev, const float* a, const float* b, flo
     if (ep.bias || ep.resid || ep.act || !ep.rowvec || k == 0 || a_trans || !b_trans ||
         !gemm_rowvec_mode_ok(dev, a, b, c, batch, m, n, k))
       return AGPU_ERR_UNSUPPORTED;
-    return use_wide(dev, batch, m, n, k)
-               ? run_tc_pair<512, false, false, true>(dev, a, b, c, batch, m, n, k, ep, s)
-               : run_tc_pair<256, false, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
+    return run_tc_pair<256, false, false, true>(dev, a, b, c, batch, m, n, k, ep, s);
   }
   if (ep.act == 3) {
     // SwiGLU: fused into the CTA-pair kernel's epilogue when that kernel runs

@@ -13,7 +13,7 @@ namespace agpu {
 template <class P>
 agpu_status launch_pair(agpu_device* dev, const CUtensorMap& ta, const CUtensorMap& tb,
                         const P& pol, long long tiles, cudaStream_t s, const char* what) {
-  using Cfg = umma::PairCfg<P::BN>;
+  using Cfg = umma::PairCfg<P::BN, P::EPI_EXTRA>;
   auto kern = umma::umma_tf32_pair_kernel<P>;
   AGPU_CUDA(set_smem_once<umma::umma_tf32_pair_kernel<P>>(dev, Cfg::SMEM));
   const long long clusters = std::min<long long>(tiles, std::max(1, dev->sm_count / 2));

@@ -33,7 +33,9 @@ namespace umma {
 // s*MMA_N + r*MMA_N/2 ..).  An accumulator of 2*BN > 512 columns cannot be
 // double-buffered: the MMA then waits for the epilogue between tiles, which
 // the wider tile amortises (and it halves the TMA bytes per FLOP of B).
-template <int BN_>
+// EXTRA_: further epilogue shared memory a policy asks for (P::EPI_EXTRA,
+// split evenly over the epilogue warps, 1024-byte aligned per warp).
+template <int BN_, int EXTRA_ = 0>
 struct PairCfg {
   static constexpr int BN = BN_;             // tile columns (both CTAs)
   static constexpr int NMMA = BN > 256 ? 2 : 1;
@@ -43,11 +45,13 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 4;            // 128 rows per CTA
   static constexpr int B_BYTES = (BN / 2) * BK * 4;      // BN/2 columns per CTA
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int EPI_BYTES = kEpiWarps * kEpiWarpFloats * 4;
+  static_assert(EXTRA_ % (kEpiWarps * 1024) == 0, "per-warp extra epilogue memory alignment");
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiWarpFloats * 4 + EXTRA_;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - EPI_BYTES - BAR_BYTES;
   static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static_assert(STAGES >= 2, "tile too large for the shared-memory ring");
   static constexpr int RING_BYTES = STAGE_BYTES * STAGES;
   static constexpr int SMEM = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr int TMEM_COLS = ACC * BN <= 256 ? 256 : 512;
@@ -59,7 +63,10 @@ struct PairCfg {
 //       issues this CTA's STAGE_BYTES with tma_load_*_pair(..., leader_bar, ...)
 //   Tile rank_tile(const Tile&, int rank) const;   // the CTA's 128-row half
 //   static constexpr bool TILE_EPILOGUE;  // true: where whole_tile(),
-//       store_tile(tile, row, tmem_row_addr, staging, lane) drains the tile
+//       bool store_tile(tile, row, tmem_row_addr, staging, extra, lane,
+//                       status, abort_flag) drains the tile (false: a wait expired)
+//   static constexpr int EPI_EXTRA;   // bytes of extra epilogue memory (0, or
+//       with void init_extra(float* slice) run once per warp slice at start)
 // and, for BN > 256, the B sub-block layout described at PairCfg.
 // whether a TILE_EPILOGUE policy drains this launch's tiles with store_tile
 template <class P>
@@ -73,7 +80,7 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     umma_tf32_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                           const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ P pol,
                           unsigned int* status) {
-  using C = PairCfg<P::BN>;
+  using C = PairCfg<P::BN, P::EPI_EXTRA>;
   constexpr int BN = P::BN;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -81,6 +88,9 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
   float* epi = reinterpret_cast<float*>(smem + C::RING_BYTES);
+  // the policy's extra epilogue memory: one slice per epilogue warp
+  [[maybe_unused]] float* xtra_base = epi + kEpiWarps * kEpiWarpFloats;
+  constexpr int kXtraWarpFloats = P::EPI_EXTRA / 4 / kEpiWarps;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES + C::EPI_BYTES);
   uint64_t* full = bars;                // [STAGES] leader's is the one used
   uint64_t* empty = bars + STAGES;      // [STAGES] both CTAs
@@ -108,6 +118,9 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
+    if constexpr (P::EPI_EXTRA > 0) {
+      for (int w = 0; w < kEpiWarps; ++w) pol.init_extra(xtra_base + w * kXtraWarpFloats);
+    }
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
@@ -225,7 +238,12 @@ __global__ void __launch_bounds__(PairCfg<P::BN>::THREADS, 1)
           pol.store_swiglu(tile, q * 32 + lane, c * 32, g, u, stg, lane);
         }
       } else if (tile_epi(pol)) {  // the policy walks the tile's chunks itself
-        if constexpr (P::TILE_EPILOGUE) pol.store_tile(tile, q * 32 + lane, trow, stg, lane);
+        if constexpr (P::TILE_EPILOGUE) {
+          if (!pol.store_tile(tile, q * 32 + lane, trow, stg,
+                              xtra_base + (warp - 2) * kXtraWarpFloats, lane, status,
+                              abort_flag))
+            break;  // an expired wait (status recorded); its copies have landed
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
