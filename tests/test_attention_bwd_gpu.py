@@ -83,6 +83,22 @@ def test_sdpa_backward_epilogue_way_vs_float64(dev, bh, s, d, causal):
             assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
 
 
+def test_sdpa_backward_head_chunks(dev):
+    """S 4096: at most 2^30 score elements per chunk, so 70 heads run as 64 +
+    6 (the epilogue way's last, smaller chunk included).  Heads on both sides
+    of the chunk boundary against float64."""
+    bh, s, d = 70, 4096, 64
+    q, k, v, do = _inputs(bh, s, d, 70)
+    g = [dev.upload(x) for x in (q, k, v, do)]
+    got = [dev.read(x) for x in dev.sdpa_backward(*g, bh, s, d)]
+    hs = s * d
+    for h in (0, 63, 64, 69):
+        sl = slice(h * hs, (h + 1) * hs)
+        want = _f64_backward(q[sl], k[sl], v[sl], do[sl], s, d, False)
+        for name, a, w in zip(("dq", "dk", "dv"), got, want):
+            assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
+
+
 def test_sdpa_backward_both_ways_agree(dev, tmp_path):
     """The row-kernel way (AGPU_SDPA_BWD_FUSED=0, in a child process) and the
     epilogue way give the same gradients within the TF32 tolerance."""
