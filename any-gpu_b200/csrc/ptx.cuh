@@ -193,17 +193,8 @@ __device__ __forceinline__ void bulk_wait_read1() {
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
-// 16-byte asynchronous global -> shared copy (L2 only); `bytes` 16 or 0 (then
-// the destination is zero-filled and nothing is read).  Completion:
-// cp_async_wait_all in the issuing thread.
-__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
+// ex2.approx.ftz: 2^x on the hardware unit (the GEMM epilogue that forms
+// attention probabilities).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
