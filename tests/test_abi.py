@@ -122,3 +122,15 @@ def test_product_does_not_reference_oracle():
             (ROOT / "any-gpu_b200" / "csrc").glob("*.cu*")):
         text = p.read_text()
         assert "oracle" not in text.lower().replace("oracle-free", ""), p
+
+
+def test_every_environment_switch_is_documented():
+    # the kernel-choice switches the library reads are listed in the header
+    read = set()
+    for p in (ROOT / "any-gpu_b200" / "csrc").glob("*.cu*"):
+        read |= set(re.findall(r'getenv\("(AGPU_[A-Z0-9_]+)"\)', p.read_text()))
+    documented = set()
+    for h in HEADERS:
+        documented |= set(re.findall(r"\b(AGPU_[A-Z0-9_]+)=", h.read_text()))
+    assert read, "no switches found"
+    assert read <= documented, sorted(read - documented)
