@@ -142,8 +142,13 @@ agpu_status launch_attention_backward(agpu_device* dev, const float* q, const fl
   // the epilogue way: every chunk's S-sized products on the pair kernel (the
   // last, smaller chunk included) and the forward on CTA pairs
   const uint32_t last = (uint32_t)(bh - (bh - 1) / chunk * chunk);
+  // decided before anything launches: every operand 16-byte aligned (each
+  // head's [s, d] block then is too), so no product of a later chunk refuses
+  const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(dout)) &
+                        15u) == 0;
   const bool fused = bwd_fused_enabled() && effective_precision(dev) == AGPU_PREC_TF32 &&
-                     (d == 64 || d == 128) && s >= 256 && s % 4 == 0 &&
+                     aligned && (d == 64 || d == 128) && s >= 256 && s % 4 == 0 &&
                      gemm_rowvec_mode_ok(dev, q, k, q, (uint32_t)std::min<uint64_t>(chunk, bh),
                                          s, s, d) &&
                      gemm_rowvec_mode_ok(dev, q, k, q, last, s, s, d);

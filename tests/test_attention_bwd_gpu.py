@@ -99,6 +99,33 @@ def test_sdpa_backward_head_chunks(dev):
             assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
 
 
+def test_sdpa_backward_launch_layer_unaligned_grad(dev):
+    """Launch layer with dO 4 bytes off a 16-byte boundary at a shape that
+    otherwise takes the epilogue way: the call checks every operand before
+    launching and runs the row-kernel way (its dO products on the exact
+    SIMT GEMM), still correct."""
+    import torch
+    bh, s, d = 16, 1024, 64
+    q, k, v, do = _inputs(bh, s, d, 16)
+    Q, K, V = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    DO = torch.zeros(bh * s * d + 1, device="cuda")
+    DO[1:] = torch.from_numpy(do).cuda()
+    dq, dk, dv = (torch.empty(bh * s * d, device="cuda") for _ in range(3))
+    st = torch.cuda.Stream()
+    dev.launch_sdpa_backward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), DO.data_ptr() + 4,
+                             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), bh, s, d, False,
+                             st.cuda_stream)
+    st.synchronize()
+    dev.synchronize()
+    got = [x.cpu().numpy() for x in (dq, dk, dv)]
+    hs = s * d
+    for h in (0, bh - 1):
+        sl = slice(h * hs, (h + 1) * hs)
+        want = _f64_backward(q[sl], k[sl], v[sl], do[sl], s, d, False)
+        for name, a, w in zip(("dq", "dk", "dv"), got, want):
+            assert _rel(a[sl], w) <= 1e-3, (h, name, _rel(a[sl], w))
+
+
 def test_sdpa_backward_both_ways_agree(dev, tmp_path):
     """The row-kernel way (AGPU_SDPA_BWD_FUSED=0, in a child process) and the
     epilogue way give the same gradients within the TF32 tolerance."""
