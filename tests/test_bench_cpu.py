@@ -55,3 +55,20 @@ def test_bench_workload_plans_cpu():
             assert rep.scaling() == "weak" and rep.flops == world * one.flops
     mm = bench.Matmul(args, 4, 1)
     assert not mm.sharded and mm.scaling() == "weak" and mm.flops == 4 * 2.0 * 512 ** 3
+
+
+def test_bench_rounds_override_cpu():
+    """`--rounds R` splits each rank's items into R rounds (at most one item
+    each), and the job is the same whatever the split."""
+    sys.path.insert(0, str(ROOT))
+    import argparse
+    import bench
+    base = dict(batch=64, size=512, precision="tf32", bh=256, seq=2048, images=16,
+                llama_batch=32, graph=None)
+    one = bench.BmmSoftmax(argparse.Namespace(**base, rounds=0), 1, 0)
+    for rounds, world, want in ((4, 8, 4), (1, 2, 1), (100, 8, 8)):
+        ranks = [bench.BmmSoftmax(argparse.Namespace(**base, rounds=rounds), world, r)
+                 for r in range(world)]
+        assert all(len(w.plan.spans) == want for w in ranks)
+        assert sum(w.local for w in ranks) == one.total
+        assert all(w.flops == one.flops for w in ranks)
