@@ -11,7 +11,9 @@
 //   * warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
 //     warp 1 owns tensor memory and issues tcgen05.mma from one thread,
 //     warps 2-5 drain the double-buffered TMEM accumulator (tcgen05.ld),
-//     transpose 32x32 blocks through shared memory and write coalesced rows;
+//     apply the epilogue in registers and write each 32x32 block through a
+//     swizzled staging buffer with a TMA bulk tensor store (read-modify-write
+//     segments transpose through shared memory and store coalesced rows);
 //   * A may be K-major (stored [M,K]) or MN-major (stored [K,M]), B may be
 //     MN-major (stored [K,N], the reference layout) or K-major (stored [N,K]);
 //     kind::tf32 accepts both majors, so no transpose pre-pass is needed for
